@@ -1,0 +1,348 @@
+"""Benchmark of the B200 attention hot path (one JSON line on rank 0).
+
+Default workload = BASELINE config 2: batched paged decode, TinyLlama heads
+(32 q / 4 kv / 64), 22 layers back-to-back, 32 sequences at context 4096, fp32
+KV in 16-token pages with a seeded shuffled page table over a pool of
+32*256*22 pages (5.9 GB: larger than L2, so no flush between steps).
+One step = the 22 per-layer decode calls; each layer has its own Q and page
+table.  The metric is decode-attention KV GB/s: algorithmic bytes (KV read
+once per (sequence, KV head) + Q + O + page table) over device time.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+Multi-GPU (torchrun, one rank per GPU): every rank runs its own config-2
+replica (weak scaling, no collective on the data path) and `value` is the sum
+of bytes over ranks divided by the max over ranks of the timed region.
+
+The CPU baseline and the --impl reference arm time the oracle (oracle/, the
+CPU restatement of the reference's AVX-512 attention; the reference's Rust
+cannot be built here) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+METRIC = "decode attn KV GB/s (frac of 8 TB/s HBM) and µs/layer-step at 1/2/4/8 B200"
+H, N_KV, D, PT = 32, 4, 64, 16
+LAYERS, BATCH, CTX = 22, 32, 4096
+
+
+def load_pkg():
+    if "nyion_rs_b200" in sys.modules:
+        return sys.modules["nyion_rs_b200"]
+    pkg_dir = os.path.join(ROOT, "nyion.rs_b200")
+    spec = importlib.util.spec_from_file_location(
+        "nyion_rs_b200", os.path.join(pkg_dir, "__init__.py"), submodule_search_locations=[pkg_dir])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["nyion_rs_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def layer_step_bytes(batch=BATCH, ctx=CTX) -> int:
+    kv = batch * 2 * N_KV * ctx * D * 4
+    qo = 2 * batch * H * D * 4
+    table = batch * (ctx // PT) * 4
+    return kv + qo + table
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[4:]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = sorted(r[0] for r in rows)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3][1:5]) if v.lower() == "active"})
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(r[2] for r in rows)}
+
+
+# --------------------------------------------------------------------- CPU legs
+def cpu_sample_inputs(seed=1234, n_seq=8):
+    """A bounded sample of config 2 for the CPU oracle: n_seq sequences of one
+    layer (same shapes, same N(0,1) distribution)."""
+    rng = np.random.default_rng(seed)
+    pages = n_seq * (CTX // PT)
+    pool = rng.standard_normal((pages, N_KV, 2, PT, D), dtype=np.float32)
+    table = rng.permutation(pages).astype(np.int32).reshape(n_seq, CTX // PT)
+    q = rng.standard_normal((n_seq, H, D), dtype=np.float32)
+    lens = np.full(n_seq, CTX, np.int32)
+    return q, pool, table, lens
+
+
+def time_cpu_oracle(budget_s: float = 4.0, n_seq=8):
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    threads = os.cpu_count() or 1
+    q, pool, table, lens = cpu_sample_inputs(n_seq=n_seq)
+    O.decode_paged_f32(q[:1], pool, table[:1], lens[:1], N_KV, D, PT, threads=threads)  # warm
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        O.decode_paged_f32(q, pool, table, lens, N_KV, D, PT, threads=threads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    per_layer_step_s = el / reps * (BATCH / n_seq)
+    gbs = layer_step_bytes() / per_layer_step_s / 1e9
+    return {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{reps} x ({n_seq} sequences x 1 layer, ctx {CTX}, fp32 16-token pages) "
+                      f"in {el:.1f} s, scaled to a 32-sequence layer-step",
+            "us_per_layer_step": per_layer_step_s * 1e6,
+            "isa": "avx512" if O.lib().or_avx512_available() else "avx2/scalar"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    steps = []
+    for _ in range(args.warmup):
+        time_cpu_oracle(budget_s=0.5)
+    for _ in range(args.steps):
+        steps.append(time_cpu_oracle(budget_s=max(1.0, 10.0 / max(args.steps, 1))))
+    vals = [s["value"] for s in steps]
+    v = float(np.median(vals))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": layer_step_bytes() * LAYERS / (v * 1e9) * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic N(0,1)",
+        "config": {"workload": "config2: paged decode, 22 layers, B=32, ctx 4096, fp32 KV, 16-token pages",
+                   "l2": "inputs > L2"},
+        "cpu_baseline": {k: steps[-1][k] for k in ("cores", "kind", "sample")} | {"value": v, "unit": "GB/s"},
+        "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference = oracle/ C restatement of ops::attention (AVX-512 dot/AXPY order), "
+                "all host threads; the reference's Rust cannot be built in this environment",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------- GPU leg
+def run_gpu(args, rank, world):
+    import torch
+    import torch.distributed as dist
+    pkg = load_pkg()
+    A = pkg.attn
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    A.lib()
+
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    n_pages = BATCH * (CTX // PT) * LAYERS
+    pool = torch.randn(n_pages, N_KV, 2, PT, D, device=dev, generator=g)
+    perm = torch.randperm(n_pages, device=dev, generator=g).to(torch.int32)
+    tables = perm.reshape(LAYERS, BATCH, CTX // PT).contiguous()
+    q = torch.randn(LAYERS, BATCH, H, D, device=dev, generator=g)
+    out = torch.empty_like(q)
+    lens = torch.full((BATCH,), CTX, dtype=torch.int32, device=dev)
+    ws = A.Workspace(BATCH, N_KV, H, D, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def step(s):
+        for l in range(LAYERS):
+            A.decode_paged_f32(q[l], pool, tables[l], lens, out=out[l], workspace=ws, stream=s)
+
+    with torch.cuda.stream(stream):
+        step(stream)
+    stream.synchronize()
+    if A.device_error(stream) != 0:
+        raise RuntimeError("device error word set after warm-up call")
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step(stream)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    barrier()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        barrier()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    # ---- end to end through the public API: pinned host Q in, host O out ----
+    qh = q.cpu().pin_memory()
+    oh = torch.empty_like(qh).pin_memory()
+    qd = torch.empty_like(q)
+
+    def e2e_step(s):
+        for l in range(LAYERS):
+            qd[l].copy_(qh[l], non_blocking=True)
+            A.decode_paged_f32(qd[l], pool, tables[l], lens, out=out[l], workspace=ws, stream=s)
+            oh[l].copy_(out[l], non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            e2e_step(stream)
+        torch.cuda.synchronize()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step(stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    err = A.device_error(stream)
+    del graph
+
+    step_bytes = layer_step_bytes() * LAYERS
+    value = step_bytes * world / (ms * 1e-3) / 1e9
+    per_launch_us = ms * 1e3 / LAYERS
+    achieved = layer_step_bytes() / (per_launch_us * 1e-6) / 1e9
+    peak, peak_kind = peaks()
+    traffic = None
+    tfile = os.path.join(ROOT, "profiles", "decode_f32_config2_traffic.json")
+    if os.path.exists(tfile):
+        try:
+            traffic = json.load(open(tfile)).get("traffic_bytes_per_launch")
+        except Exception:
+            traffic = None
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        c = time_cpu_oracle(budget_s=args.cpu_seconds)
+        cpu = {"value": c["value"], "unit": "GB/s", "cores": c["cores"], "kind": c["kind"],
+               "sample": c["sample"] + f"; {c['isa']}"}
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1), seeded",
+            "config": {"workload": "config2: paged decode, 22 layers x B=32 x ctx 4096, fp32 KV, "
+                                   "16-token pages, shuffled page table",
+                       "layers": LAYERS, "batch": BATCH, "ctx": CTX, "heads": "32q/4kv/64",
+                       "l2": "inputs 5.9 GB > L2 (no flush needed)", "graph": "CUDA graph of 22 launches",
+                       "parallelism": f"replicas x{world}"},
+            "us_per_layer_step": per_launch_us,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
+                         "bytes_per_launch": layer_step_bytes()},
+            "cpu_baseline": cpu,
+            "e2e": {"value": step_bytes * world / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
+                    "h2d_bytes_per_step": int(qh.numel() * 4), "d2h_bytes_per_step": int(oh.numel() * 4),
+                    "ms_per_step": e2e_ms},
+            "gpu_launches": LAYERS * args.steps,
+            "clocks": clocks.summary(),
+            "device_error": err,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=6.0)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    try:
+        run_gpu(args, rank, world)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

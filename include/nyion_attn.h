@@ -1,0 +1,138 @@
+/*
+ * nyion_attn.h — C ABI of libnyion_attn.so, the B200 (sm_100a) attention hot
+ * path of bmcc-DEV/Nyion.rs.
+ *
+ * Plain pointers and sizes only.  Device pointers are caller-owned unless a
+ * comment says otherwise; `stream` is a cudaStream_t passed as void* (NULL =
+ * the legacy default stream).  Every nyion_attn_* function returns an
+ * int32_t status: 0 = NYION_OK, negative = error, with a readable message from
+ * nyion_attn_last_error() (per calling thread).  There is no CPU fallback
+ * behind any entry point: a missing device or an unsupported shape is an
+ * error.
+ *
+ * Each entry point names the reference interface it replaces (paths are
+ * relative to the reference repository root).
+ */
+#ifndef NYION_ATTN_H
+#define NYION_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NYION_ATTN_VERSION 100
+
+enum {
+  NYION_OK = 0,
+  NYION_ERR_INVALID = -1,      /* bad argument (null pointer, size, alignment) */
+  NYION_ERR_CUDA = -2,         /* CUDA runtime error; message has the CUDA text */
+  NYION_ERR_UNSUPPORTED = -3,  /* shape this build has no kernel for (e.g. head_dim != 64) */
+  NYION_ERR_DEVICE = -4,       /* device error word set: page id out of range, wait timeout */
+  NYION_ERR_WORKSPACE = -5     /* workspace missing or too small */
+};
+
+/* Device error word bits (nyion_attn_device_error). */
+#define NYION_DEVERR_PAGE_RANGE 1
+#define NYION_DEVERR_WAIT_TIMEOUT 2
+#define NYION_DEVERR_SHAPE 4
+
+/* ------------------------------------------------------------------ status */
+int32_t nyion_attn_version(void);
+const char* nyion_attn_last_error(void);
+/* Synchronises `stream`, returns the current device's error word in *bits and
+ * clears it.  Returns NYION_ERR_DEVICE when any bit was set.  Replaces the
+ * reference's per-call stderr + `return -1` (fused_attention.cu:218-240),
+ * which cannot see asynchronous device faults. */
+int32_t nyion_attn_device_error(void* stream, int32_t* bits);
+
+/* --------------------------------------------------------------- workspace */
+/* Bytes of device workspace the decode entry points need for `batch`
+ * sequences of `n_kv_heads` KV heads (split-KV partials + per-(seq, kv head)
+ * counters).  The counters must start at zero: allocate, then call
+ * nyion_attn_workspace_reset once; the kernels leave them at zero again.
+ * Calls that share one workspace must not overlap on the GPU. */
+size_t nyion_attn_decode_workspace_size(int32_t batch, int32_t n_kv_heads, int32_t n_heads,
+                                        int32_t head_dim);
+int32_t nyion_attn_workspace_reset(void* workspace, size_t bytes, void* stream);
+
+/* ---------------------------------------------------- paged fp32 decode ----
+ * GQA decode attention with online softmax over an fp32 paged KV pool, one
+ * query token per sequence.  Replaces the per-head score/softmax/AXPY loops
+ * of ops::attention (swamp-engine/src/ops.rs:170-278) for a batch of
+ * sequences, and the Attention node of the ComputeGraph
+ * (swamp-gpu/src/compute_graph.rs:14-25, swamp-engine/src/scheduler.rs:120-171).
+ *
+ *   q          [batch][n_heads][head_dim] f32
+ *   kv_pool    [n_pool_pages][n_kv_heads][2 (K,V)][page_tokens][head_dim] f32
+ *   page_table [batch][max_pages] int32 page ids into kv_pool
+ *   seq_lens   [batch] int32: sequence b attends tokens [0, seq_lens[b]) (device)
+ *   out        [batch][n_heads][head_dim] f32 (zeros where seq_lens[b] == 0)
+ * Query head h reads KV head h / (n_heads / n_kv_heads) (ops.rs:191).
+ * scale <= 0 selects 1/sqrt(head_dim) (ops.rs:181).
+ * This build: head_dim 64, n_heads / n_kv_heads == 8, page_tokens 16,
+ * batch <= 512 per call (larger batches are split into several launches).
+ * workspace: nyion_attn_decode_workspace_size(batch, ...) bytes, reset once;
+ * NULL selects a library-owned workspace (first use allocates: not under
+ * stream capture). */
+int32_t nyion_attn_decode_paged_f32(const float* q, const float* kv_pool, int64_t n_pool_pages,
+                                    const int32_t* page_table, int32_t max_pages,
+                                    const int32_t* seq_lens, float* out, int32_t batch,
+                                    int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                                    int32_t page_tokens, float scale, void* workspace,
+                                    size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------- reference-layout fp32 decode ----
+ * ops::attention (swamp-engine/src/ops.rs:170-278) with the same argument
+ * meaning: one sequence, query head h reads KV head h / (n_heads/n_kv_heads),
+ * tokens [0, min(q_pos, seq_len - 1)] attended, scale 1/sqrt(head_dim).
+ * The KV cache is the reference's PagedKVCache f32 page geometry
+ * (swamp-engine/src/cache.rs:17-21, 185-237, 681-747) placed in two HBM
+ * arenas (K and V): flat pages 0..127 of 32 slots, 128..1119 of 128 slots,
+ * then 1024-slot pages, consecutive, each [n_layers][n_kv_heads][slots][head_dim]
+ * f32.  n_arena_pages = pages present in each arena.  Uses the
+ * library-owned workspace (first use allocates: not under stream capture). */
+int32_t nyion_attn_decode_zoned_f32(float* out, const float* q, const float* k_arena,
+                                    const float* v_arena, int64_t n_arena_pages, int32_t n_layers,
+                                    int32_t layer_idx, int64_t seq_len, int64_t q_pos,
+                                    int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                                    void* stream);
+
+/* ---------------------------------------------- reference CUDA C ABI -------
+ * Same names, arguments and 0 / -1 results as swamp-gpu/kernels/fused_attention.cu,
+ * so the reference's Rust declarations (swamp-gpu/src/lib.rs:586-677) link
+ * against this library unchanged.  K/V are contiguous
+ * [n_kv_heads][kv_stride][head_dim]; the decode attends tokens [0, seq_len).
+ * On failure the message is in nyion_attn_last_error() (the reference prints
+ * to stderr). */
+
+/* fused_attention.cu:194-243 (device pointers, default stream) */
+int gpu_attention_device(const float* d_q, const float* d_k_cache, const float* d_v_cache,
+                         float* d_output, int n_heads, int n_kv_heads, int seq_len, int head_dim,
+                         int kv_stride);
+/* fused_attention.cu:483-531 */
+int gpu_attention_streamed(const float* d_q, const float* d_k_cache, const float* d_v_cache,
+                           float* d_output, int n_heads, int n_kv_heads, int seq_len,
+                           int head_dim, int kv_stride, void* stream);
+/* fused_attention.cu:335-405 (host pointers; copies in and out, synchronous) */
+int gpu_attention_forward(const float* q, const float* k_cache, const float* v_cache,
+                          float* output, int n_heads, int n_kv_heads, int seq_len, int head_dim);
+/* fused_attention.cu:597-664: a replayable CUDA graph of one decode at fixed
+ * shapes.  d_scores is accepted for ABI compatibility and not used (scores
+ * never leave on-chip memory).  Returns NULL on failure. */
+void* gpu_graph_create_attention(const float* d_q, const float* d_k_cache,
+                                 const float* d_v_cache, float* d_scores, float* d_output,
+                                 int n_heads, int n_kv_heads, int seq_len, int head_dim,
+                                 int kv_stride);
+/* fused_attention.cu:669-679 */
+int gpu_graph_replay_attention(void* graph_handle, void* stream);
+/* fused_attention.cu:682-686 */
+void gpu_graph_destroy(void* graph_handle);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NYION_ATTN_H */

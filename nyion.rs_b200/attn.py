@@ -1,0 +1,179 @@
+"""Host-side binding of libnyion_attn.so (ctypes) with torch tensors as buffers.
+
+This is the Python caller of the C ABI declared in include/nyion_attn.h.  It
+owns no maths: every function checks shapes, passes raw device pointers and
+the current torch stream to the library, and raises NyionError on a non-zero
+status.  There is no CPU fallback: without the library or a CUDA device the
+calls raise.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(PKG_DIR)
+LIB_PATH = os.path.join(PKG_DIR, "libnyion_attn.so")
+HEADER_DIR = os.path.join(ROOT, "include")
+
+NYION_OK = 0
+_lib = None
+
+
+class NyionError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"nyion status {status}: {msg}")
+        self.status = status
+
+
+def lib() -> C.CDLL:
+    """Loads the library; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: run `python nyion.rs_b200/build.py` "
+                               "(there is no CPU fallback)")
+        L = C.CDLL(LIB_PATH)
+        vp, i32, i64, f32, sz = C.c_void_p, C.c_int32, C.c_int64, C.c_float, C.c_size_t
+        sig = {
+            "nyion_attn_version": (i32, []),
+            "nyion_attn_last_error": (C.c_char_p, []),
+            "nyion_attn_device_error": (i32, [vp, C.POINTER(i32)]),
+            "nyion_attn_decode_workspace_size": (sz, [i32, i32, i32, i32]),
+            "nyion_attn_workspace_reset": (i32, [vp, sz, vp]),
+            "nyion_attn_decode_paged_f32": (i32, [vp, vp, i64, vp, i32, vp, vp, i32, i32, i32, i32,
+                                                  i32, f32, vp, sz, vp]),
+            "nyion_attn_decode_zoned_f32": (i32, [vp, vp, vp, vp, i64, i32, i32, i64, i64, i32, i32,
+                                                  i32, vp]),
+            "gpu_attention_device": (C.c_int, [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int,
+                                               C.c_int]),
+            "gpu_attention_streamed": (C.c_int, [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int,
+                                                 C.c_int, C.c_int, vp]),
+            "gpu_attention_forward": (C.c_int, [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int]),
+            "gpu_graph_create_attention": (vp, [vp, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int,
+                                                C.c_int, C.c_int]),
+            "gpu_graph_replay_attention": (C.c_int, [vp, vp]),
+            "gpu_graph_destroy": (None, [vp]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    m = lib().nyion_attn_last_error()
+    return m.decode() if m else ""
+
+
+def check(status: int) -> None:
+    if status != NYION_OK:
+        raise NyionError(status, last_error())
+
+
+def declared_symbols() -> list[str]:
+    """Function names declared in include/*.h (the exported ABI)."""
+    names = []
+    for fn in sorted(os.listdir(HEADER_DIR)):
+        if not fn.endswith(".h"):
+            continue
+        text = open(os.path.join(HEADER_DIR, fn)).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        text = re.sub(r"//[^\n]*", "", text)
+        for m in re.finditer(r"\b([A-Za-z_][A-Za-z0-9_]*)\s*\(", text):
+            name = m.group(1)
+            pre = text[max(0, m.start() - 40):m.start()]
+            if name in ("if", "sizeof", "defined") or "#define" in pre.split("\n")[-1]:
+                continue
+            if re.search(r"(int32_t|int|void|size_t|char)\s*\**\s*$", pre):
+                names.append(name)
+    return sorted(set(names))
+
+
+# ---------------------------------------------------------------------- torch glue
+def _torch():
+    import torch
+    return torch
+
+
+def _ptr(t) -> int:
+    return 0 if t is None else int(t.data_ptr())
+
+
+def _stream_ptr(stream=None) -> int:
+    torch = _torch()
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return int(s.cuda_stream)
+
+
+class Workspace:
+    """Device workspace for the decode entry points (zeroed once)."""
+
+    def __init__(self, batch: int, n_kv_heads: int, n_heads: int, head_dim: int, device=None):
+        torch = _torch()
+        self.nbytes = int(lib().nyion_attn_decode_workspace_size(batch, n_kv_heads, n_heads, head_dim))
+        self.buf = torch.zeros(self.nbytes, dtype=torch.uint8, device=device or "cuda")
+
+    def ptr(self) -> int:
+        return int(self.buf.data_ptr())
+
+
+def decode_paged_f32(q, kv_pool, page_table, seq_lens, out=None, scale: float = 0.0,
+                     workspace: Workspace | None = None, stream=None):
+    """fp32 paged GQA decode (nyion_attn_decode_paged_f32).
+
+    q [B, H, D] f32; kv_pool [P, n_kv, 2, 16, D] f32; page_table [B, max_pages]
+    int32; seq_lens [B] int32 (device); returns out [B, H, D] f32.
+    """
+    torch = _torch()
+    B, H, D = q.shape
+    n_kv = kv_pool.shape[1]
+    assert kv_pool.dtype == torch.float32 and q.dtype == torch.float32
+    assert page_table.dtype == torch.int32 and seq_lens.dtype == torch.int32
+    for t in (q, kv_pool, page_table, seq_lens):
+        assert t.is_cuda and t.is_contiguous()
+    if out is None:
+        out = torch.empty_like(q)
+    ws_ptr, ws_bytes = (0, 0) if workspace is None else (workspace.ptr(), workspace.nbytes)
+    check(lib().nyion_attn_decode_paged_f32(
+        _ptr(q), _ptr(kv_pool), kv_pool.shape[0], _ptr(page_table), page_table.shape[1],
+        _ptr(seq_lens), _ptr(out), B, H, n_kv, D, kv_pool.shape[3], float(scale), ws_ptr, ws_bytes,
+        _stream_ptr(stream)))
+    return out
+
+
+def decode_zoned_f32(q, k_arena, v_arena, n_layers: int, layer: int, seq_len: int, q_pos: int,
+                     out=None, stream=None):
+    """ops::attention over reference-layout zone pages (nyion_attn_decode_zoned_f32).
+
+    q [H, D] f32; k_arena / v_arena: flat f32 arenas holding consecutive zone
+    pages [n_layers][n_kv][slots][D]; returns out [H, D].
+    """
+    torch = _torch()
+    H, D = q.shape
+    n_kv = H // 8
+    per_slot = n_layers * n_kv * D
+    n = k_arena.numel()
+    z0 = min(n // (per_slot * 32), 128)
+    rest = n - z0 * per_slot * 32
+    z1 = min(rest // (per_slot * 128), 992) if z0 == 128 else 0
+    rest -= z1 * per_slot * 128
+    z2 = rest // (per_slot * 1024) if z1 == 992 else 0
+    n_pages = z0 + z1 + z2
+    if out is None:
+        out = torch.empty_like(q)
+    check(lib().nyion_attn_decode_zoned_f32(_ptr(out), _ptr(q), _ptr(k_arena), _ptr(v_arena),
+                                            n_pages, n_layers, layer, seq_len, q_pos, H, n_kv, D,
+                                            _stream_ptr(stream)))
+    return out
+
+
+def device_error(stream=None) -> int:
+    bits = C.c_int32(0)
+    st = lib().nyion_attn_device_error(_stream_ptr(stream), C.byref(bits))
+    if st not in (NYION_OK, -4):
+        check(st)
+    return int(bits.value)

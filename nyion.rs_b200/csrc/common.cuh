@@ -1,0 +1,113 @@
+// common.cuh — shared device helpers for the sm_100a attention kernels.
+//
+// mbarrier + TMA (cp.async.bulk.tensor) wrappers written as inline PTX, the
+// 128-byte swizzle address map the tensor copies write, warp reductions, and
+// the device error word that replaces the reference's stderr + return -1
+// (swamp-gpu/kernels/fused_attention.cu:218-240).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace nyion {
+
+// ---- device error word bits (read back by nyion_attn_device_error) --------
+enum : int32_t {
+  kErrPageRange = 1,     // a page-table entry outside [0, n_pool_pages)
+  kErrWaitTimeout = 2,   // a bounded mbarrier / flag wait ran out
+  kErrShape = 4,         // a launch saw a shape its host check should have caught
+};
+
+// Iteration bound for every spin on an mbarrier: with the nanosleep back-off
+// below this is several seconds, far above any legal TMA latency.
+constexpr uint32_t kSpinLimit = 1u << 22;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: returns false (and leaves the barrier untouched) when the
+// bound runs out; the caller records kErrWaitTimeout and stops.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (i > 64) __nanosleep(64);
+  }
+  return false;
+}
+
+// 2-D tiled TMA load: box at (x = inner element index, y = row) into smem,
+// completion counted in bytes on `bar`.  x * sizeof(elem) is always a
+// multiple of 16 bytes at the call sites (x in {0, 32} for f32 rows of 64).
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x,
+                                            int32_t y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// Byte offset of logical 16-byte chunk `c` (0..7) of row `r` inside a
+// 1024-byte-aligned tile of 128-byte rows written by a SWIZZLE_128B copy.
+__device__ __forceinline__ uint32_t swz128(uint32_t r, uint32_t c) {
+  return (r << 7) | (((c ^ r) & 7u) << 4);
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ void record_error(int32_t* err, int32_t bits) {
+  if (err) atomicOr(err, bits);
+}
+
+// L2-only loads for data another CTA of the same launch wrote.
+__device__ __forceinline__ float4 ld_cg4(const float* p) {
+  return __ldcg(reinterpret_cast<const float4*>(p));
+}
+
+}  // namespace nyion

@@ -1,0 +1,37 @@
+// host.h — internal host-side helpers shared by the entry points.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "nyion_attn.h"
+
+namespace nyion {
+
+// Records a message for nyion_attn_last_error() and returns `status`.
+int32_t fail(int32_t status, const char* fmt, ...);
+// Maps a CUDA runtime error to NYION_ERR_CUDA with its text; 0 on success.
+int32_t check_cuda(cudaError_t e, const char* what);
+
+struct DeviceInfo {
+  int device;
+  int num_sms;
+  int32_t* err_word;  // device error word (lazily allocated, zeroed)
+};
+// Info for the current device; allocates the error word on first use.
+int32_t device_info(DeviceInfo** out);
+
+// 2-D row-major tensor map over `rows` rows of `row_elems` elements of
+// `dtype`, box = (box_x elements, box_y rows), 128-byte swizzle.
+int32_t encode_rows_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes,
+                         const void* base, uint64_t row_elems, uint64_t rows, uint32_t box_x,
+                         uint32_t box_y, CUtensorMapSwizzle swizzle);
+
+// Internal workspace for entry points whose reference signature carries none
+// (gpu_attention_device and friends).  Grown with cudaMalloc and zeroed with
+// cudaMemset, so the first call at a given size must not be under capture.
+int32_t internal_workspace(size_t bytes, void** ptr);
+
+}  // namespace nyion
