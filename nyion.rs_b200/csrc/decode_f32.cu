@@ -1,4 +1,4 @@
-// decode_f32.cu — fp32 GQA decode attention over paged or contiguous KV.
+// decode_f32.cu — fp32 GQA decode attention over paged, contiguous or zoned KV.
 //
 // Restates the maths of ops::attention (swamp-engine/src/ops.rs:170-278):
 // s_t = scale * <q_h, K_t>, p = softmax(s), o_h = sum_t p_t V_t, query head h
@@ -7,16 +7,31 @@
 //
 //   * work = (sequence, KV head, 32-token chunk) triples, flattened and cut
 //     into equal contiguous ranges, one per persistent CTA (stream-K style),
-//     so every SM gets the same number of KV bytes whatever the batch and
+//     so every SM streams the same number of KV bytes whatever the batch and
 //     context mix;
-//   * each chunk (2 pages of 16 tokens; K and V, 16 KB) arrives by four
-//     128B-swizzled TMA tensor copies per page into a 4-stage mbarrier ring;
-//   * the 8 query heads of a GQA group share every K/V byte read: warp w
-//     scores heads 2w, 2w+1 for the chunk's 32 tokens (one token per lane, q
-//     in registers), the PV product splits heads x dims x token-quarters;
-//   * a (sequence, KV head) pair split across CTAs leaves log-sum-exp
-//     partials (m, l, o) in the workspace; the last CTA to finish the pair
-//     (per-pair counter) merges them and resets the counter to zero.
+//   * a producer warp brings each chunk (two 16-token pages of K and V,
+//     16 KB) into a 12-stage ring (full/empty mbarrier pair per stage).  In
+//     the paged pool one 5-D TMA tensor copy moves a whole (page, KV head)
+//     block — K and V, both 128-byte halves of every row, 8 KB — so a chunk
+//     is two copies; page-table reads for the next 32 chunks are issued 16
+//     chunks before they are needed, off the copy-issue critical path;
+//   * six consumer warps take the chunks round-robin.  One warp computes a
+//     whole chunk for all 8 query heads of the GQA group on the tensor cores
+//     (mma.sync m16n8k16 bf16, fp32 accumulate), so every K/V byte is read
+//     from shared memory once.  fp32 accuracy comes from splitting every
+//     operand into bf16 hi + lo: the A operand stacks the hi rows (0..7) over
+//     the lo rows (8..15) and the B operand is issued once with hi and once
+//     with lo, so all four cross products accumulate and the residual is
+//     ~2^-17 relative per operand.  K fragments come from ldmatrix on the
+//     fp32 tile (dims permuted identically in q), P is reused from the score
+//     accumulators as the A operand of P.V (no shared-memory round trip);
+//   * every consumer warp keeps its own log-sum-exp partial (m, l, o) per
+//     (sequence, KV head) segment and publishes it to the workspace when it
+//     leaves the segment; a per-segment counter tells the last contributor
+//     (whichever CTA and warp) to merge them and reset the counter to zero.
+//     No barrier spans the consumer warps, so a slow warp never stalls the
+//     others.  A segment served by one warp alone is written out directly.
+#include <cuda_bf16.h>
 #include <math.h>
 
 #include "common.cuh"
@@ -26,16 +41,18 @@ namespace nyion {
 namespace f32dec {
 
 constexpr int HD = 64;
-constexpr int GROUP = 8;      // query heads per KV head
-constexpr int CHUNK = 32;     // tokens per pipeline stage
-constexpr int PAGE = 16;      // tokens per page (TMA box height)
-constexpr int STAGES = 4;
-constexpr int THREADS = 128;
-constexpr int SUB = CHUNK * 128;     // one 32-row x 128-byte swizzled subtile
-constexpr int STAGE_BYTES = 4 * SUB; // K dims 0-31, K dims 32-63, V 0-31, V 32-63
-constexpr int MAX_SEQS = 512;        // sequences per launch
+constexpr int GROUP = 8;              // query heads per KV head
+constexpr int CHUNK = 32;             // tokens per pipeline stage
+constexpr int PAGE = 16;              // tokens per page (TMA box height)
+constexpr int NC = 6;                 // consumer warps
+constexpr int STAGES = 12;            // two per consumer warp
+constexpr int THREADS = (NC + 1) * 32;
+constexpr int SUB = CHUNK * 128;      // 4096 B; a page block is 2*SUB: four 16-row x 128 B subtiles
+constexpr int PAGE_BYTES = 8192;      // one (page, KV head) block in shared memory
+constexpr int STAGE_BYTES = 4 * SUB;  // per page (8 KB): K dims 0-31 | K 32-63 | V 0-31 | V 32-63
+constexpr int MAX_SEQS = 512;         // sequences per launch
 constexpr int MAX_GRID = 1024;
-constexpr int RING = 32;             // chunks per page-row prefetch batch
+constexpr int RING = 32;              // chunks per page-row prefetch batch
 
 enum Mode { kPool = 0, kContig = 1, kZoned = 2 };
 
@@ -51,33 +68,29 @@ struct Params {
   int32_t n_layers, layer;  // zoned: layers per page, layer read
   float qscale;             // scale * log2(e)
   int32_t* cnt;             // [batch*n_kv] merge counters (start at 0, left at 0)
-  float2* ml;               // [MAX_GRID + pairs][GROUP] (m, l) partials
-  float* po;                // [MAX_GRID + pairs][GROUP][HD] unnormalised o partials
+  float2* ml;               // [(MAX_GRID + pairs) * NC][GROUP] (m, l) partials
+  float* po;                // [(MAX_GRID + pairs) * NC][GROUP][HD] o partials (relative to m)
   int32_t* err;
 };
 
 struct Smem {
   uint8_t kv[STAGES][STAGE_BYTES];   // first member: 1024-byte aligned
-  float p[CHUNK][GROUP];
-  float alpha[GROUP];
-  float lsum[GROUP];
-  float mmax[GROUP];
-  float red[2][16][16];
-  uint64_t full[STAGES];
+  uint64_t full[STAGES];             // TMA bytes landed
+  uint64_t empty[STAGES];            // the consuming warp is done with the stage
   int32_t prefix[MAX_SEQS + 1];      // flat chunk index where sequence b starts
   int32_t lens[MAX_SEQS];
   int32_t rows[2][RING][3];          // per chunk: K row of page 0, page 1, page count
-  int32_t flag;
   int32_t warp_tot[THREADS / 32];
+  int32_t abort_;
 };
+
+__device__ __forceinline__ int chunks_of(int len) { return (len + CHUNK - 1) / CHUNK; }
 
 struct Cursor {
   int b, kvh, chunk, nchunks, len;
 };
 
-__device__ __forceinline__ int chunks_of(int len) { return (len + CHUNK - 1) / CHUNK; }
-
-__device__ __forceinline__ void seek(Cursor& c, const Smem& s, int batch, int n_kv, int i) {
+__device__ __forceinline__ void seek(Cursor& c, const Smem& s, int batch, int i) {
   int lo = 0, hi = batch;   // invariant: prefix[lo] <= i < prefix[hi]
   while (hi - lo > 1) {
     int mid = (lo + hi) >> 1;
@@ -89,88 +102,102 @@ __device__ __forceinline__ void seek(Cursor& c, const Smem& s, int batch, int n_
   int off = i - s.prefix[lo];
   c.kvh = off / c.nchunks;
   c.chunk = off - c.kvh * c.nchunks;
-  (void)n_kv;
 }
 
-__device__ __forceinline__ void advance(Cursor& c, const Smem& s, int batch, int n_kv) {
-  if (++c.chunk < c.nchunks) return;
-  c.chunk = 0;
-  if (++c.kvh < n_kv) return;
-  c.kvh = 0;
-  do { ++c.b; } while (c.b < batch && s.lens[c.b] <= 0);
-  if (c.b < batch) {
-    c.len = s.lens[c.b];
-    c.nchunks = chunks_of(c.len);
+// Page rows of one chunk, prepared by a producer lane in two steps so the
+// page-table load overlaps copy issue: rows_start() reads the table into
+// registers, rows_finish() (16 chunks later) checks and stores them.
+struct RowJob {
+  int valid, npg, b, kvh, tok0;
+  int64_t page[2];
+};
+
+template <int MODE>
+__device__ __forceinline__ void rows_start(RowJob& j, const Smem& s, const Params& p, int i, int end) {
+  j.valid = i < end;
+  if (!j.valid) return;
+  Cursor c;
+  seek(c, s, p.batch, i);
+  j.b = c.b;
+  j.kvh = c.kvh;
+  j.tok0 = c.chunk * CHUNK;
+  j.npg = (c.len - j.tok0 > PAGE) ? 2 : 1;
+  j.page[0] = j.page[1] = -1;
+  if (MODE == kPool) {
+#pragma unroll
+    for (int pg = 0; pg < 2; ++pg) {
+      const int pidx = j.tok0 / PAGE + pg;
+      if (pg < j.npg && pidx < p.max_pages) j.page[pg] = p.table[(int64_t)c.b * p.max_pages + pidx];
+    }
   }
 }
 
-// Warp 0 fills ring slot `slot` with the page rows of flat chunks
-// [first, first + RING) ∩ [first, end): one chunk per lane.
+// Stores per chunk: copy coordinate of page 0, page 1, page count.  Pool mode
+// stores the (page * n_kv + kv head) block index of the 5-D map; the other
+// modes store the first row (of 256 B) in the K and V arenas.
 template <int MODE>
-__device__ void fill_rows(Smem& s, const Params& p, int slot, int first, int end, int lane) {
-  int i = first + lane;
-  if (i >= end) return;
-  Cursor c;
-  seek(c, s, p.batch, p.n_kv, i);
-  int tok0 = c.chunk * CHUNK;
-  int npg = (c.len - tok0 > PAGE) ? 2 : 1;
+__device__ __forceinline__ void rows_finish(Smem& s, const Params& p, const RowJob& j, int slot,
+                                            int lane) {
+  if (!j.valid) return;
   int32_t r[2] = {-4 * PAGE, -4 * PAGE};
-  for (int pg = 0; pg < npg; ++pg) {
+#pragma unroll
+  for (int pg = 0; pg < 2; ++pg) {
+    if (pg >= j.npg) continue;
     if (MODE == kPool) {
-      int pidx = tok0 / PAGE + pg;
-      int64_t page = -1;
-      if (pidx < p.max_pages) page = p.table[(int64_t)c.b * p.max_pages + pidx];
+      const int64_t page = j.page[pg];
       if (page < 0 || page >= p.n_pool_pages) {
         record_error(p.err, kErrPageRange);
-        continue;   // row stays negative: the TMA box is zero-filled
+        continue;   // negative coordinate: the TMA box is zero-filled
       }
-      r[pg] = (int32_t)(((page * p.n_kv + c.kvh) * 2) * PAGE);
+      r[pg] = (int32_t)(page * p.n_kv + j.kvh);
     } else if (MODE == kZoned) {
       // cache.rs:185-237, 681-747: zone z holds pages of bs_z slots laid out
       // [layer][kv_head][slot][head_dim]; pages are consecutive in the arena.
-      const int zone = tok0 < 4096 ? 0 : (tok0 < 131072 ? 1 : 2);
+      const int zone = j.tok0 < 4096 ? 0 : (j.tok0 < 131072 ? 1 : 2);
       const int64_t bs = zone == 0 ? 32 : (zone == 1 ? 128 : 1024);
       const int64_t zs = zone == 0 ? 0 : (zone == 1 ? 4096 : 131072);
       const int64_t zpage = zone == 0 ? 0 : (zone == 1 ? 128 : 1120);
-      const int64_t lp = p.n_layers * (int64_t)p.n_kv;       // rows per slot across layers*heads
+      const int64_t lp = p.n_layers * (int64_t)p.n_kv;
       const int64_t zrow = zone == 0 ? 0 : (zone == 1 ? 128 * lp * 32 : 128 * lp * 32 + 992 * lp * 128);
-      const int64_t local = (tok0 - zs) / bs, slot = (tok0 - zs) % bs;
+      const int64_t local = (j.tok0 - zs) / bs, slot = (j.tok0 - zs) % bs;
       if (zpage + local >= p.n_pool_pages) {
         record_error(p.err, kErrPageRange);
         continue;
       }
-      r[pg] = (int32_t)(zrow + local * lp * bs + ((int64_t)p.layer * p.n_kv + c.kvh) * bs + slot +
+      r[pg] = (int32_t)(zrow + local * lp * bs + ((int64_t)p.layer * p.n_kv + j.kvh) * bs + slot +
                         pg * PAGE);
     } else {
-      r[pg] = c.kvh * p.kv_stride + tok0 + pg * PAGE;
+      r[pg] = j.kvh * p.kv_stride + j.tok0 + pg * PAGE;
     }
   }
   s.rows[slot][lane][0] = r[0];
   s.rows[slot][lane][1] = r[1];
-  s.rows[slot][lane][2] = npg;
+  s.rows[slot][lane][2] = j.npg;
 }
 
 template <int MODE>
 __device__ __forceinline__ void issue(Smem& s, int stage, int k, const CUtensorMap* mk,
                                       const CUtensorMap* mv) {
   const int32_t* e = s.rows[(k / RING) & 1][k % RING];
-  int npg = e[2];
+  const int npg = e[2];
   uint8_t* base = s.kv[stage];
   fence_proxy_async_smem();
-  mbar_arrive_expect_tx(&s.full[stage], (uint32_t)(npg * 4 * PAGE * 128));
+  mbar_arrive_expect_tx(&s.full[stage], (uint32_t)(npg * PAGE_BYTES));
   for (int pg = 0; pg < npg; ++pg) {
-    int32_t rk = e[pg];
-    int32_t rv = (MODE == kPool) ? rk + PAGE : rk;
-    uint8_t* d = base + pg * PAGE * 128;
-    tma_load_2d(d + 0 * SUB, mk, 0, rk, &s.full[stage]);
-    tma_load_2d(d + 1 * SUB, mk, 32, rk, &s.full[stage]);
-    tma_load_2d(d + 2 * SUB, mv, 0, rv, &s.full[stage]);
-    tma_load_2d(d + 3 * SUB, mv, 32, rv, &s.full[stage]);
+    uint8_t* d = base + pg * PAGE_BYTES;
+    if (MODE == kPool) {
+      // (x, slot row, 128-B half, K/V, block): K_lo, K_hi, V_lo, V_hi subtiles
+      tma_load_5d(d, mk, 0, 0, 0, 0, e[pg], &s.full[stage]);
+    } else {
+      // (x, row, 128-B half) boxes of 16 rows: K then V
+      tma_load_3d(d, mk, 0, e[pg], 0, &s.full[stage]);
+      tma_load_3d(d + PAGE_BYTES / 2, mv, 0, e[pg], 0, &s.full[stage]);
+    }
   }
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(THREADS, 2)
+__global__ void __launch_bounds__(THREADS, 1)
 decode_f32_kernel(const Params p, const __grid_constant__ CUtensorMap map_k,
                   const __grid_constant__ CUtensorMap map_v) {
   extern __shared__ uint8_t smem_raw[];
@@ -182,7 +209,11 @@ decode_f32_kernel(const Params p, const __grid_constant__ CUtensorMap map_k,
   if (t == 0) {
     prefetch_tensormap(&map_k);
     prefetch_tensormap(&map_v);
-    for (int i = 0; i < STAGES; ++i) mbar_init(&s.full[i], 1);
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    s.abort_ = 0;
     fence_barrier_init();
   }
 
@@ -192,7 +223,7 @@ decode_f32_kernel(const Params p, const __grid_constant__ CUtensorMap map_k,
     s.lens[b] = L > 0 ? L : 0;
   }
   __syncthreads();
-  constexpr int PER = MAX_SEQS / THREADS;
+  constexpr int PER = (MAX_SEQS + THREADS - 1) / THREADS;
   int local[PER];
   int run = 0;
 #pragma unroll
@@ -216,9 +247,8 @@ decode_f32_kernel(const Params p, const __grid_constant__ CUtensorMap map_k,
 #pragma unroll
   for (int j = 0; j < PER; ++j) {
     int b = t * PER + j;
-    if (b <= p.batch && b < MAX_SEQS + 1) s.prefix[b] = excl + local[j];
+    if (b <= p.batch) s.prefix[b] = excl + local[j];
   }
-  if (t == THREADS - 1 && p.batch == MAX_SEQS) s.prefix[MAX_SEQS] = excl + run;
   __syncthreads();
 
   // zero the outputs of empty sequences
@@ -234,213 +264,323 @@ decode_f32_kernel(const Params p, const __grid_constant__ CUtensorMap map_k,
   if (begin >= end) return;
   const int n = end - begin;
 
-  if (warp == 0) {
-    fill_rows<MODE>(s, p, 0, begin, end, lane);
-    fill_rows<MODE>(s, p, 1, begin + RING, end, lane);
-  }
-  __syncthreads();
-  if (t == 0)
-    for (int k = 0; k < STAGES && k < n; ++k) issue<MODE>(s, k, k, &map_k, &map_v);
-
-  Cursor cur;
-  seek(cur, s, p.batch, p.n_kv, begin);
-
-  float q0[HD], q1[HD];
-  float o[4][4];
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-  const int hq = t >> 6, tq = (t >> 4) & 3, c16 = t & 15, half = c16 >> 3, cc = c16 & 7;
-  int aborted_at = -1;
-
-  for (int k = 0; k < n; ++k) {
-    const int stage = k % STAGES;
-    const bool seg_start = (k == 0) || (cur.chunk == 0);
-    const bool seg_end = (k == n - 1) || (cur.chunk == cur.nchunks - 1);
-    if (seg_start) {
-      const float* qp = p.q + ((int64_t)cur.b * H + cur.kvh * GROUP + 2 * warp) * HD;
-#pragma unroll
-      for (int d = 0; d < HD; d += 4) {
-        float4 a = __ldg(reinterpret_cast<const float4*>(qp + d));
-        float4 bq = __ldg(reinterpret_cast<const float4*>(qp + HD + d));
-        q0[d] = a.x * p.qscale; q0[d + 1] = a.y * p.qscale;
-        q0[d + 2] = a.z * p.qscale; q0[d + 3] = a.w * p.qscale;
-        q1[d] = bq.x * p.qscale; q1[d + 1] = bq.y * p.qscale;
-        q1[d + 2] = bq.z * p.qscale; q1[d + 3] = bq.w * p.qscale;
+  if (warp == NC) {
+    // ================= producer warp =================
+    RowJob job;
+    rows_start<MODE>(job, s, p, begin + lane, end);
+    rows_finish<MODE>(s, p, job, 0, lane);
+    rows_start<MODE>(job, s, p, begin + RING + lane, end);
+    __syncwarp();
+    for (int k = 0; k < n; ++k) {
+      const int stage = k % STAGES;
+      if (k % RING == RING / 2) {
+        // rows for chunks [k - RING/2 + RING, ... + RING) into the other slot
+        rows_finish<MODE>(s, p, job, ((k / RING) + 1) & 1, lane);
+        __syncwarp();
+      } else if (k % RING == 0 && k > 0) {
+        rows_start<MODE>(job, s, p, begin + k + RING + lane, end);
       }
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) o[i][j] = 0.f;
-      m0 = m1 = -INFINITY;
-      l0 = l1 = 0.f;
+      bool ok = true;
+      if (k >= STAGES) ok = mbar_wait_bounded(&s.empty[stage], (uint32_t)(((k / STAGES) - 1) & 1));
+      if (!__all_sync(0xffffffffu, ok)) {
+        record_error(p.err, kErrWaitTimeout);
+        if (lane == 0) {
+          atomicExch(&s.abort_, 1);
+          // the last copy issued into each stage must land before the CTA exits
+          for (int c = k - 1; c >= 0 && c >= k - STAGES; --c)
+            mbar_wait_bounded(&s.full[c % STAGES], (uint32_t)((c / STAGES) & 1));
+        }
+        return;
+      }
+      if (lane == 0) issue<MODE>(s, stage, k, &map_k, &map_v);
+      __syncwarp();
     }
-    // page rows for chunks [k + RING, k + 2*RING) into the ring slot just freed
-    if (warp == 0 && k % RING == 0 && k > 0)
-      fill_rows<MODE>(s, p, ((k / RING) + 1) & 1, begin + k + RING, end, lane);
+    return;
+  }
 
-    const int nv = min(CHUNK, cur.len - cur.chunk * CHUNK);
-    bool ok = mbar_wait_bounded(&s.full[stage], (uint32_t)((k / STAGES) & 1));
-    const uint8_t* st = s.kv[stage];
-
-    // ---- scores: warp -> heads (2w, 2w+1), lane -> token ----
-    float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+  // ================= consumer warps =================
+  const int cw = warp;
+  const int g = lane >> 2, tig = lane & 3;
+  // ldmatrix row addresses for K k-step ks: subtile ks>>1 (2 KB each) of the
+  // page, logical chunk 4*(ks&1) + (lane>>3), row lane&7 of the 8-token
+  // n-tile; n-tile nt adds (nt>>1) pages and (nt&1) * 8 rows as immediates
+  uint32_t koff[4];
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      float4 kk = *reinterpret_cast<const float4*>(st + swz128(lane, c));
-      a0 = fmaf(q0[4 * c], kk.x, a0); a0 = fmaf(q0[4 * c + 1], kk.y, a0);
-      a0 = fmaf(q0[4 * c + 2], kk.z, a0); a0 = fmaf(q0[4 * c + 3], kk.w, a0);
-      b0 = fmaf(q1[4 * c], kk.x, b0); b0 = fmaf(q1[4 * c + 1], kk.y, b0);
-      b0 = fmaf(q1[4 * c + 2], kk.z, b0); b0 = fmaf(q1[4 * c + 3], kk.w, b0);
-    }
+  for (int ks = 0; ks < 4; ++ks) {
+    const uint32_t r = lane & 7, chunk = 4 * (ks & 1) + (lane >> 3);
+    koff[ks] = (ks >> 1) * (SUB / 2) + r * 128 + (((chunk ^ r) & 7) << 4);
+  }
+  // V B-fragment words: token 16kt + 2tig + e (e in {0,1,8,9}) = page kt, row
+  // 2tig + e; dim 8nt + g in subtile nt>>2.  voff[nt&3][e&1] is the lane part.
+  uint32_t voff[4][2];
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      float4 kk = *reinterpret_cast<const float4*>(st + SUB + swz128(lane, c));
-      a1 = fmaf(q0[32 + 4 * c], kk.x, a1); a1 = fmaf(q0[33 + 4 * c], kk.y, a1);
-      a1 = fmaf(q0[34 + 4 * c], kk.z, a1); a1 = fmaf(q0[35 + 4 * c], kk.w, a1);
-      b1 = fmaf(q1[32 + 4 * c], kk.x, b1); b1 = fmaf(q1[33 + 4 * c], kk.y, b1);
-      b1 = fmaf(q1[34 + 4 * c], kk.z, b1); b1 = fmaf(q1[35 + 4 * c], kk.w, b1);
+  for (int n4 = 0; n4 < 4; ++n4)
+#pragma unroll
+    for (int e1 = 0; e1 < 2; ++e1) {
+      const uint32_t row = 2 * tig + e1, chunk = 2 * n4 + (g >> 2);
+      voff[n4][e1] = PAGE_BYTES / 2 + row * 128 + (((chunk ^ row) & 7) << 4) + (g & 3) * 4;
     }
-    const bool valid = lane < nv;
-    float s0 = valid ? a0 + a1 : -INFINITY;
-    float s1 = valid ? b0 + b1 : -INFINITY;
 
-    // ---- online softmax (log2 domain: q carries scale*log2 e) ----
-    float mx0 = warp_max(s0), mx1 = warp_max(s1);
-    float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-    float al0 = exp2f(m0 - mn0), al1 = exp2f(m1 - mn1);
-    float p0 = exp2f(s0 - mn0), p1 = exp2f(s1 - mn1);
-    l0 = fmaf(l0, al0, p0);
-    l1 = fmaf(l1, al1, p1);
-    m0 = mn0;
-    m1 = mn1;
-    *reinterpret_cast<float2*>(&s.p[lane][2 * warp]) = make_float2(p0, p1);
+  // q fragments (A operand of S = Q K^T): rows g = hi, g+8 = lo of head g; the
+  // k positions (2tig, 2tig+1, 2tig+8, 2tig+9) of k-step ks hold dims
+  // 16ks + (tig, 4+tig, 8+tig, 12+tig), the order ldmatrix delivers K.
+  auto load_q = [&](const Cursor& c, float (&x)[16]) {
+    const float* qp = p.q + ((int64_t)c.b * H + c.kvh * GROUP + g) * HD;
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) x[4 * ks + e] = __ldg(qp + 16 * ks + 4 * e + tig);
+  };
+  float qn[16];
+  Cursor nxt;
+  seek(nxt, s, p.batch, begin);
+  load_q(nxt, qn);
+
+  int i = begin;
+  while (i < end) {
+    const Cursor sg = nxt;
+    const int pstart = i - sg.chunk;
+    const int pend = pstart + sg.nchunks;
+    const int seg_hi = min(end, pend);
+    uint32_t qa[4][4];
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      split_bf16x2(qn[4 * ks] * p.qscale, qn[4 * ks + 1] * p.qscale, qa[ks][0], qa[ks][1]);
+      split_bf16x2(qn[4 * ks + 2] * p.qscale, qn[4 * ks + 3] * p.qscale, qa[ks][2], qa[ks][3]);
+    }
+    if (seg_hi < end) {   // next segment's q loads fly while this one computes
+      seek(nxt, s, p.batch, seg_hi);
+      load_q(nxt, qn);
+    }
+    float o[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) o[nt][j] = 0.f;
+    float m = -INFINITY, l = 0.f;
+
+    const int k0 = i - begin;
+    const int kfirst = k0 + ((cw - k0 % NC) + NC) % NC;
+    for (int k = kfirst; k < seg_hi - begin; k += NC) {
+      const int stage = k % STAGES;
+      const int nv = min(CHUNK, sg.len - (begin + k - pstart) * CHUNK);
+      if (!s.abort_) {
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&s.full[stage], (uint32_t)((k / STAGES) & 1)))) {
+          record_error(p.err, kErrWaitTimeout);
+          if (lane == 0) atomicExch(&s.abort_, 1);
+        }
+      }
+      const uint32_t sb = smem_u32(s.kv[stage]);
+
+      // ---- pull the whole chunk into registers, then hand the stage back ----
+      uint32_t kf[4][4][4];   // [ks][nt] ldmatrix.x4: K[8nt+g][16ks + {0,4,8,12} + tig]
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt)
+          ldsm_x4(sb + koff[ks] + (nt >> 1) * PAGE_BYTES + (nt & 1) * 1024, kf[ks][nt][0],
+                  kf[ks][nt][1], kf[ks][nt][2], kf[ks][nt][3]);
+      float vf[2][8][4];      // [kt][nt] V[16kt + 2tig + {0,1,8,9}][8nt + g]
+#pragma unroll
+      for (int kt = 0; kt < 2; ++kt)
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+          const uint32_t a0 = sb + voff[nt & 3][0] + (nt >> 2) * (SUB / 2) + kt * PAGE_BYTES;
+          const uint32_t a1 = sb + voff[nt & 3][1] + (nt >> 2) * (SUB / 2) + kt * PAGE_BYTES;
+          vf[kt][nt][0] = lds32(a0);
+          vf[kt][nt][1] = lds32(a1);
+          vf[kt][nt][2] = lds32(a0 + 1024);
+          vf[kt][nt][3] = lds32(a1 + 1024);
+        }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.empty[stage]);
+
+      // ---- S = Q K^T for the chunk's 32 tokens (4 n-tiles of 8) ----
+      float sc[4][4];
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sc[nt][j] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+          uint32_t bh0, bl0, bh1, bl1;
+          split_bf16x2(__uint_as_float(kf[ks][nt][0]), __uint_as_float(kf[ks][nt][1]), bh0, bl0);
+          split_bf16x2(__uint_as_float(kf[ks][nt][2]), __uint_as_float(kf[ks][nt][3]), bh1, bl1);
+          mma_bf16(sc[nt], qa[ks], bh0, bh1);
+          mma_bf16(sc[nt], qa[ks], bl0, bl1);
+        }
+      }
+      // s[nt][j]: head g, token 8nt + 2tig + j
+      float sv[4][2];
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        sv[nt][0] = sc[nt][0] + sc[nt][2];
+        sv[nt][1] = sc[nt][1] + sc[nt][3];
+        if (nv < CHUNK) {
+          if (8 * nt + 2 * tig >= nv) sv[nt][0] = -INFINITY;
+          if (8 * nt + 2 * tig + 1 >= nv) sv[nt][1] = -INFINITY;
+        }
+      }
+      // ---- online softmax (log2 domain: q carries scale * log2 e) ----
+      float mx = sv[0][0];
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) mx = fmaxf(mx, fmaxf(sv[nt][0], sv[nt][1]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float mn = fmaxf(m, mx);
+      const float al = exp2f(m - mn);
+      float ps = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        sv[nt][0] = exp2f(sv[nt][0] - mn);
+        sv[nt][1] = exp2f(sv[nt][1] - mn);
+        ps += sv[nt][0] + sv[nt][1];
+      }
+      l = fmaf(l, al, ps);
+      m = mn;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[nt][j] *= al;
+
+      // ---- O += P V: k = tokens (2 k-steps of 16), n = dims (8 n-tiles) ----
+#pragma unroll
+      for (int kt = 0; kt < 2; ++kt) {
+        if (16 * kt >= nv) break;
+        uint32_t pa[4];
+        split_bf16x2(sv[2 * kt][0], sv[2 * kt][1], pa[0], pa[1]);
+        split_bf16x2(sv[2 * kt + 1][0], sv[2 * kt + 1][1], pa[2], pa[3]);
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+          float v0 = vf[kt][nt][0], v1 = vf[kt][nt][1], v2 = vf[kt][nt][2], v3 = vf[kt][nt][3];
+          if (nv < CHUNK) {
+            // tokens past the sequence end may hold anything: P is 0 there, V must be finite
+            const int r = 16 * kt + 2 * tig;
+            if (r >= nv) v0 = 0.f;
+            if (r + 1 >= nv) v1 = 0.f;
+            if (r + 8 >= nv) v2 = 0.f;
+            if (r + 9 >= nv) v3 = 0.f;
+          }
+          uint32_t bh0, bl0, bh1, bl1;
+          split_bf16x2(v0, v1, bh0, bl0);
+          split_bf16x2(v2, v3, bh1, bl1);
+          mma_bf16(o[nt], pa, bh0, bh1);
+          mma_bf16(o[nt], pa, bl0, bl1);
+        }
+      }
+    }
+
+    i = seg_hi;
+    if (kfirst >= seg_hi - begin) continue;   // this warp had no chunk in the segment
+
+    // ---- publish this warp's partial (plain stores; counted at the end) ----
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    const int pair = sg.b * p.n_kv + sg.kvh;
+    const int cfirst = pstart / W, clast = (pend - 1) / W;
+    int contributors = 0;   // (CTA, warp) pairs that own at least one chunk of the segment
+    for (int c = cfirst; c <= clast; ++c) {
+      const int lo = max(pstart, c * W), hi = min(pend, (c + 1) * W);
+      contributors += min(NC, hi - lo);
+    }
+    float* dst = p.out + ((int64_t)sg.b * H + sg.kvh * GROUP) * HD;
+    if (contributors == 1) {
+      const float inv = 1.0f / l;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt)
+        *reinterpret_cast<float2*>(dst + g * HD + 8 * nt + 2 * tig) =
+            make_float2((o[nt][0] + o[nt][2]) * inv, (o[nt][1] + o[nt][3]) * inv);
+      continue;
+    }
+    const int64_t slot = ((int64_t)blockIdx.x + pair) * NC + cw;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+      __stcg(reinterpret_cast<float2*>(p.po + (slot * GROUP + g) * HD + 8 * nt + 2 * tig),
+             make_float2(o[nt][0] + o[nt][2], o[nt][1] + o[nt][3]));
+    if (tig == 0) __stcg(&p.ml[slot * GROUP + g], make_float2(m, l));
+    // counting and merging wait until this warp has consumed all its chunks
+  }
+
+  // ---- after the last chunk: count in, and merge where this warp is last ----
+  __threadfence();
+  __syncwarp();
+  for (int i2 = begin; i2 < end;) {
+    Cursor sg;
+    seek(sg, s, p.batch, i2);
+    const int pstart = i2 - sg.chunk, pend = pstart + sg.nchunks, seg_hi = min(end, pend);
+    const int k0 = i2 - begin;
+    const int kfirst = k0 + ((cw - k0 % NC) + NC) % NC;
+    i2 = seg_hi;
+    if (kfirst >= seg_hi - begin) continue;
+    const int cfirst = pstart / W, clast = (pend - 1) / W;
+    int contributors = 0;
+    for (int c = cfirst; c <= clast; ++c) {
+      const int lo = max(pstart, c * W), hi = min(pend, (c + 1) * W);
+      contributors += min(NC, hi - lo);
+    }
+    if (contributors == 1) continue;   // written directly
+    const int pair = sg.b * p.n_kv + sg.kvh;
+    int last = 0;
     if (lane == 0) {
-      s.alpha[2 * warp] = al0;
-      s.alpha[2 * warp + 1] = al1;
+      const int old = atomicAdd(&p.cnt[pair], 1);
+      last = (old == contributors - 1);
+      if (last) atomicExch(&p.cnt[pair], 0);
+      __threadfence();
     }
-    if (__syncthreads_or(!ok)) { aborted_at = k; break; }
-
-    // ---- PV: thread -> heads 4hq..4hq+3, dims 4*c16.., tokens tq mod 4 ----
-    {
-      float4 al = *reinterpret_cast<const float4*>(&s.alpha[4 * hq]);
-      const float alv[4] = {al.x, al.y, al.z, al.w};
+    if (!__shfl_sync(0xffffffffu, last, 0)) continue;
+    float* dst = p.out + ((int64_t)sg.b * H + sg.kvh * GROUP) * HD;
+    // lane -> head lane>>2, dims 16*(lane&3) .. +15.  Contributors are the
+    // warps (lo + q) % NC, q < min(NC, hi - lo), of each CTA c in
+    // [cfirst, clast]; they are folded in one online pass with four partial
+    // loads in flight at a time.
+    const int mh = lane >> 2, md = 16 * (lane & 3);
+    float M = -INFINITY, den = 0.f;
+    float4 acc[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+    for (int e = 0; e < 4; ++e) acc[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int c = cfirst; c <= clast; ++c) {
+      const int lo = max(pstart, c * W) - c * W, hi = min(pend, (c + 1) * W) - c * W;
+      const int nw = min(NC, hi - lo);
+      for (int q0 = 0; q0 < nw; q0 += 4) {
+        float2 mlv[4];
+        float4 ov[4][4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) o[i][j] *= alv[i];
-      const uint8_t* vb = st + (2 + half) * SUB;
+        for (int u = 0; u < 4; ++u) {
+          if (q0 + u < nw) {
+            const int64_t sl = ((int64_t)c + pair) * NC + ((lo + q0 + u) % NC);
+            mlv[u] = __ldcg(&p.ml[sl * GROUP + mh]);
 #pragma unroll
-      for (int j = 0; j < CHUNK / 4; ++j) {
-        const int tt = tq + 4 * j;
-        if (tt < nv) {
-          float4 pp = *reinterpret_cast<const float4*>(&s.p[tt][4 * hq]);
-          float4 v = *reinterpret_cast<const float4*>(vb + swz128(tt, cc));
-          const float pv[4] = {pp.x, pp.y, pp.z, pp.w};
+            for (int e = 0; e < 4; ++e) ov[u][e] = ld_cg4(p.po + (sl * GROUP + mh) * HD + md + 4 * e);
+          } else {
+            mlv[u] = make_float2(-INFINITY, 0.f);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            o[i][0] = fmaf(pv[i], v.x, o[i][0]);
-            o[i][1] = fmaf(pv[i], v.y, o[i][1]);
-            o[i][2] = fmaf(pv[i], v.z, o[i][2]);
-            o[i][3] = fmaf(pv[i], v.w, o[i][3]);
+            for (int e = 0; e < 4; ++e) ov[u][e] = make_float4(0.f, 0.f, 0.f, 0.f);
           }
         }
-      }
-    }
-    __syncthreads();
-    if (t == 0 && k + STAGES < n) issue<MODE>(s, stage, k + STAGES, &map_k, &map_v);
-
-    if (seg_end) {
-      // ---- reduce l over lanes, o over token quarters ----
-      float ls0 = warp_sum(l0), ls1 = warp_sum(l1);
-      if (lane == 0) {
-        s.lsum[2 * warp] = ls0;
-        s.lsum[2 * warp + 1] = ls1;
-        s.mmax[2 * warp] = m0;
-        s.mmax[2 * warp + 1] = m1;
-      }
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+        for (int u = 0; u < 4; ++u) {
+          if (q0 + u >= nw) continue;
+          const float Mn = fmaxf(M, mlv[u].x);
+          const float sa = exp2f(M - Mn), sb = exp2f(mlv[u].x - Mn);
+          den = den * sa + mlv[u].y * sb;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) o[i][j] += __shfl_xor_sync(0xffffffffu, o[i][j], 16);
-      if ((warp & 1) && lane < 16) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          *reinterpret_cast<float4*>(&s.red[warp >> 1][lane][4 * i]) =
-              make_float4(o[i][0], o[i][1], o[i][2], o[i][3]);
-      }
-      __syncthreads();
-      const int pair = cur.b * p.n_kv + cur.kvh;
-      const int pstart = s.prefix[cur.b] + cur.kvh * cur.nchunks;
-      const int pend = pstart + cur.nchunks;
-      const int cfirst = pstart / W, clast = (pend - 1) / W;
-      const bool single = (cfirst == clast);
-      const int slot = blockIdx.x + pair;
-      const int h0 = 4 * (warp >> 1);
-      if (!(warp & 1) && lane < 16) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float4 r = *reinterpret_cast<const float4*>(&s.red[warp >> 1][lane][4 * i]);
-          o[i][0] += r.x; o[i][1] += r.y; o[i][2] += r.z; o[i][3] += r.w;
-        }
-        if (single) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            float inv = 1.0f / s.lsum[h0 + i];
-            float* dst = p.out + ((int64_t)cur.b * H + cur.kvh * GROUP + h0 + i) * HD + 4 * lane;
-            *reinterpret_cast<float4*>(dst) =
-                make_float4(o[i][0] * inv, o[i][1] * inv, o[i][2] * inv, o[i][3] * inv);
+          for (int e = 0; e < 4; ++e) {
+            acc[e].x = fmaf(acc[e].x, sa, ov[u][e].x * sb);
+            acc[e].y = fmaf(acc[e].y, sa, ov[u][e].y * sb);
+            acc[e].z = fmaf(acc[e].z, sa, ov[u][e].z * sb);
+            acc[e].w = fmaf(acc[e].w, sa, ov[u][e].w * sb);
           }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            float* dst = p.po + ((int64_t)slot * GROUP + h0 + i) * HD + 4 * lane;
-            __stcg(reinterpret_cast<float4*>(dst), make_float4(o[i][0], o[i][1], o[i][2], o[i][3]));
-          }
-        }
-      }
-      if (!single) {
-        if (t < GROUP) __stcg(&p.ml[(int64_t)slot * GROUP + t], make_float2(s.mmax[t], s.lsum[t]));
-        __threadfence();
-        __syncthreads();
-        if (t == 0) {
-          int old = atomicAdd(&p.cnt[pair], 1);
-          int last = (old == clast - cfirst);
-          if (last) atomicExch(&p.cnt[pair], 0);
-          __threadfence();
-          s.flag = last;
-        }
-        __syncthreads();
-        if (s.flag) {
-          const int h = t >> 4, c4 = (t & 15) * 4;
-          float M = -INFINITY;
-          for (int cb = cfirst; cb <= clast; ++cb) M = fmaxf(M, __ldcg(&p.ml[(int64_t)(cb + pair) * GROUP + h]).x);
-          float den = 0.f;
-          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int cb = cfirst; cb <= clast; ++cb) {
-            float2 mlv = __ldcg(&p.ml[(int64_t)(cb + pair) * GROUP + h]);
-            float w = exp2f(mlv.x - M);
-            den = fmaf(w, mlv.y, den);
-            float4 ov = ld_cg4(p.po + ((int64_t)(cb + pair) * GROUP + h) * HD + c4);
-            acc.x = fmaf(w, ov.x, acc.x); acc.y = fmaf(w, ov.y, acc.y);
-            acc.z = fmaf(w, ov.z, acc.z); acc.w = fmaf(w, ov.w, acc.w);
-          }
-          float inv = 1.0f / den;
-          float* dst = p.out + ((int64_t)cur.b * H + cur.kvh * GROUP + h) * HD + c4;
-          *reinterpret_cast<float4*>(dst) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+          M = Mn;
         }
       }
     }
-    advance(cur, s, p.batch, p.n_kv);
-  }
-
-  if (aborted_at >= 0) {
-    record_error(p.err, kErrWaitTimeout);
-    // drain the copies still in flight (chunks aborted_at .. aborted_at+STAGES-1)
-    // before the CTA's shared memory is released; each wait is bounded too
-    if (t == 0) {
-      for (int c = aborted_at; c < n && c < aborted_at + STAGES; ++c)
-        mbar_wait_bounded(&s.full[c % STAGES], (uint32_t)((c / STAGES) & 1));
-    }
-    __syncthreads();
+    const float inv = 1.0f / den;
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      *reinterpret_cast<float4*>(dst + mh * HD + md + 4 * e) =
+          make_float4(acc[e].x * inv, acc[e].y * inv, acc[e].z * inv, acc[e].w * inv);
   }
 }
 
@@ -453,7 +593,7 @@ struct WsLayout {
 WsLayout ws_layout(int batch, int n_kv) {
   int b = batch < MAX_SEQS ? batch : MAX_SEQS;
   size_t pairs = (size_t)b * n_kv;
-  size_t slots = MAX_GRID + pairs;
+  size_t slots = (MAX_GRID + pairs) * NC;
   auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
   WsLayout w;
   w.cnt = 0;
@@ -508,6 +648,25 @@ int32_t launch(const Params& base, const CUtensorMap& mk, const CUtensorMap& mv,
   return NYION_OK;
 }
 
+// Pool: (x: 32 floats, slot row: 16 x 256 B, half: 2 x 128 B, K/V: 2 x 4096 B,
+// block = page * n_kv + kv head: 8192 B); one box = one whole block.
+int32_t pool_map(CUtensorMap* m, const float* pool, int64_t n_blocks) {
+  const uint64_t dims[5] = {32, (uint64_t)PAGE, 2, 2, (uint64_t)n_blocks};
+  const uint64_t strides[4] = {HD * 4, 128, PAGE * HD * 4, 2 * PAGE * HD * 4};
+  const uint32_t box[5] = {32, (uint32_t)PAGE, 2, 2, 1};
+  return encode_tmap(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, pool, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// Row arena: (x: 32 floats, row: 256 B, half: 128 B); box = 16 rows x both halves.
+int32_t rows_map(CUtensorMap* m, const float* base, uint64_t rows) {
+  const uint64_t dims[3] = {32, rows, 2};
+  const uint64_t strides[2] = {HD * 4, 128};
+  const uint32_t box[3] = {32, (uint32_t)PAGE, 2};
+  return encode_tmap(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 int32_t check_common(int32_t n_heads, int32_t n_kv_heads, int32_t head_dim) {
   if (n_kv_heads <= 0 || n_heads <= 0 || n_heads % n_kv_heads)
     return fail(NYION_ERR_INVALID, "n_heads (%d) must be a positive multiple of n_kv_heads (%d)",
@@ -548,7 +707,7 @@ extern "C" int32_t nyion_attn_decode_paged_f32(const float* q, const float* kv_p
     return fail(NYION_ERR_INVALID, "decode_paged_f32: batch, max_pages and n_pool_pages must be > 0");
   if (page_tokens != PAGE)
     return fail(NYION_ERR_UNSUPPORTED, "decode_paged_f32: page_tokens must be 16 (got %d)", page_tokens);
-  uint64_t rows = (uint64_t)n_pool_pages * n_kv_heads * 2 * PAGE;
+  uint64_t rows = (uint64_t)n_pool_pages * n_kv_heads;   // (page, kv head) blocks
   if (rows > (1ull << 31))
     return fail(NYION_ERR_INVALID, "decode_paged_f32: pool of %lld pages exceeds 2^31 rows",
                 (long long)n_pool_pages);
@@ -560,8 +719,7 @@ extern "C" int32_t nyion_attn_decode_paged_f32(const float* q, const float* kv_p
     return fail(NYION_ERR_WORKSPACE, "decode_paged_f32: workspace %zu < %zu bytes", workspace_bytes, need);
   }
   CUtensorMap map;
-  st = encode_rows_tmap(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, kv_pool, HD, rows, 32, PAGE,
-                        CU_TENSOR_MAP_SWIZZLE_128B);
+  st = pool_map(&map, kv_pool, n_pool_pages * n_kv_heads);
   if (st) return st;
   Params p{};
   p.n_kv = n_kv_heads;
@@ -596,11 +754,9 @@ extern "C" int32_t nyion_attn_decode_zoned_f32(float* out, const float* q, const
   uint64_t rows = (uint64_t)(z0 * 32 + z1 * 128 + z2 * 1024) * lp;
   if (rows > (1ull << 31)) return fail(NYION_ERR_INVALID, "decode_zoned_f32: arena exceeds 2^31 rows");
   CUtensorMap mk, mv;
-  st = encode_rows_tmap(&mk, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, k_arena, HD, rows, 32, PAGE,
-                        CU_TENSOR_MAP_SWIZZLE_128B);
+  st = rows_map(&mk, k_arena, rows);
   if (st) return st;
-  st = encode_rows_tmap(&mv, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, v_arena, HD, rows, 32, PAGE,
-                        CU_TENSOR_MAP_SWIZZLE_128B);
+  st = rows_map(&mv, v_arena, rows);
   if (st) return st;
   void* ws = nullptr;
   st = internal_workspace(ws_layout(1, n_kv_heads).total, &ws);
@@ -627,11 +783,9 @@ static int32_t contig_decode(const float* d_q, const float* d_k, const float* d_
     return fail(NYION_ERR_INVALID, "seq_len %d must be in [1, kv_stride=%d]", seq_len, kv_stride);
   uint64_t rows = (uint64_t)n_kv_heads * kv_stride;
   CUtensorMap mk, mv;
-  st = encode_rows_tmap(&mk, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, d_k, HD, rows, 32, PAGE,
-                        CU_TENSOR_MAP_SWIZZLE_128B);
+  st = rows_map(&mk, d_k, rows);
   if (st) return st;
-  st = encode_rows_tmap(&mv, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, d_v, HD, rows, 32, PAGE,
-                        CU_TENSOR_MAP_SWIZZLE_128B);
+  st = rows_map(&mv, d_v, rows);
   if (st) return st;
   if (!ws) {
     st = internal_workspace(ws_layout(1, n_kv_heads).total, &ws);

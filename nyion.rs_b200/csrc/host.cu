@@ -98,6 +98,31 @@ int32_t encode_rows_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int elem_b
   return NYION_OK;
 }
 
+int32_t encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
+                    const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                    CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(NYION_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  if (reinterpret_cast<uintptr_t>(base) % 16)
+    return fail(NYION_ERR_INVALID, "tensor base %p is not 16-byte aligned", base);
+  cuuint64_t d[5], st[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+    if (i + 1 < rank) st[i] = strides_bytes[i];
+    if (dims[i] == 0 || dims[i] > (1ull << 32))
+      return fail(NYION_ERR_INVALID, "tensor dim %d extent %llu out of range", i,
+                  (unsigned long long)dims[i]);
+  }
+  CUresult r = fn(map, dtype, (cuuint32_t)rank, const_cast<void*>(base), d, st, b, e,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(NYION_ERR_CUDA, "cuTensorMapEncodeTiled(rank %d) failed (%d)", rank, (int)r);
+  return NYION_OK;
+}
+
 struct Workspace {
   int device = -1;
   void* ptr = nullptr;

@@ -29,6 +29,12 @@ int32_t encode_rows_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int elem_b
                          const void* base, uint64_t row_elems, uint64_t rows, uint32_t box_x,
                          uint32_t box_y, CUtensorMapSwizzle swizzle);
 
+// General tiled tensor map: `rank` dims (innermost first), byte strides of
+// dims 1..rank-1, box extents; element strides 1, zero fill out of range.
+int32_t encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
+                    const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                    CUtensorMapSwizzle swizzle);
+
 // Internal workspace for entry points whose reference signature carries none
 // (gpu_attention_device and friends).  Grown with cudaMalloc and zeroed with
 // cudaMemset, so the first call at a given size must not be under capture.

@@ -100,6 +100,7 @@ def test_config2_shape_one_layer(cuda_device):
     assert np.abs(out1 - ref).max() < TOL
     # the merge counters reset themselves: a second call on the same workspace agrees
     assert np.array_equal(out1, out2)
+    # counters (first workspace region, one int32 per (sequence, KV head)) are back at zero
     assert int(ws.buf[:B * N_KV * 4].view(torch.int32).abs().sum().item()) == 0
 
 
