@@ -84,6 +84,28 @@ int32_t nyion_attn_decode_paged_f32(const float* q, const float* kv_pool, int64_
                                     int32_t page_tokens, float scale, void* workspace,
                                     size_t workspace_bytes, void* stream);
 
+/* ------------------------------------- paged fp32 decode, no allocation ----
+ * No counterpart in the reference.  Same arguments and result as
+ * nyion_attn_decode_paged_f32 without the workspace, for callers that must
+ * not allocate device memory while decoding (a thread inside CUDA-graph
+ * capture, a serving loop that cannot afford cudaFree's device-wide
+ * synchronisation, a host whose HBM is fully owned by its own arena).  The
+ * split-KV scratch is a fixed 8 MiB device array inside the library, reserved
+ * on every GPU that loads it; the call allocates nothing.  Limit:
+ * batch <= 512 and (148 + batch * n_kv_heads) * 6 partial slots of 2112 bytes
+ * must fit the 8 MiB (about batch * n_kv_heads <= 500 on B200); larger calls
+ * return NYION_ERR_WORKSPACE.  The first call on a device resolves the
+ * array's address (cudaGetSymbolAddress): make it before any stream capture.
+ * Calls share the array: calls that overlap on the GPU race, so serialise
+ * them.  Page-id range errors of this variant are not reported by
+ * nyion_attn_device_error. */
+int32_t nyion_attn_decode_paged_f32_noalloc(const float* q, const float* kv_pool,
+                                            int64_t n_pool_pages, const int32_t* page_table,
+                                            int32_t max_pages, const int32_t* seq_lens,
+                                            float* out, int32_t batch, int32_t n_heads,
+                                            int32_t n_kv_heads, int32_t head_dim,
+                                            int32_t page_tokens, float scale, void* stream);
+
 /* ------------------------------------------- reference-layout fp32 decode ----
  * ops::attention (swamp-engine/src/ops.rs:170-278) with the same argument
  * meaning: one sequence, query head h reads KV head h / (n_heads/n_kv_heads),

@@ -34,6 +34,8 @@
 #include <cuda_bf16.h>
 #include <math.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "host.h"
 
@@ -909,4 +911,137 @@ extern "C" void gpu_graph_destroy(void* graph_handle) {
   cudaGraphExecDestroy(h->exec);
   cudaFree(h->ws);
   delete h;
+}
+
+// ---- allocation-free variant of the paged fp32 decode -----------------------
+//
+// For callers that cannot allocate device memory at decode time: a thread in
+// the middle of capturing a CUDA graph (cudaMalloc is not allowed while a
+// capture is open), a latency-critical serving loop that must never hit
+// cudaFree's implicit device synchronisation, or a host whose HBM is entirely
+// handed out by its own arena so an extra cudaMalloc would fail or fragment
+// it.  The split-KV scratch (merge counters and log-sum-exp partials) lives
+// in one file-scope device array instead, sized kNoAllocScratchBytes; every
+// GPU that loads this library reserves it until the process exits.
+//
+// The first call on a device looks up the array's device address with
+// cudaGetSymbolAddress (and sets the kernel's shared-memory attribute); make
+// that first call before any stream capture.  All calls on a device share the
+// one array, so calls that overlap on the GPU (different streams, or graphs
+// replayed concurrently) race and corrupt each other's partials: serialise
+// them.  The merge counters are cleared at the start of every call.
+// Device-side page-id range errors of this variant go to a private error
+// word and are not reported by nyion_attn_device_error.
+namespace nyion {
+namespace f32dec {
+
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;   // 8 MiB per device
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+static __device__ int32_t g_noalloc_err;
+
+struct NoAllocDevice {
+  bool ready = false;
+  uint8_t* scratch = nullptr;   // device address of g_noalloc_scratch
+  int32_t* err = nullptr;       // device address of g_noalloc_err
+  int grid = 0;
+};
+static NoAllocDevice g_noalloc_dev[64];
+static std::mutex g_noalloc_mu;
+
+static int32_t noalloc_setup(NoAllocDevice** out) {
+  int dev = -1;
+  int32_t st = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  if (st) return st;
+  if (dev < 0 || dev >= 64) return fail(NYION_ERR_UNSUPPORTED, "device index %d >= 64", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  NoAllocDevice& d = g_noalloc_dev[dev];
+  if (!d.ready) {
+    void* sp = nullptr;
+    void* ep = nullptr;
+    st = check_cuda(cudaGetSymbolAddress(&sp, g_noalloc_scratch), "cudaGetSymbolAddress(scratch)");
+    if (st) return st;
+    st = check_cuda(cudaGetSymbolAddress(&ep, g_noalloc_err), "cudaGetSymbolAddress(error word)");
+    if (st) return st;
+    int sms = 0, major = 0;
+    st = check_cuda(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "SM count");
+    if (st) return st;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (major != 10) return fail(NYION_ERR_UNSUPPORTED, "device %d is not sm_100a", dev);
+    const size_t smem = smem_bytes();
+    st = check_cuda(cudaFuncSetAttribute(decode_f32_kernel<kPool>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                    "cudaFuncSetAttribute(decode_f32)");
+    if (st) return st;
+    int occ = 0;
+    st = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_f32_kernel<kPool>,
+                                                                  THREADS, smem),
+                    "occupancy(decode_f32)");
+    if (st) return st;
+    d.scratch = static_cast<uint8_t*>(sp);
+    d.err = static_cast<int32_t*>(ep);
+    d.grid = sms * (occ > 0 ? occ : 1);
+    if (d.grid > MAX_GRID) d.grid = MAX_GRID;
+    d.ready = true;
+  }
+  *out = &d;
+  return NYION_OK;
+}
+
+}  // namespace f32dec
+}  // namespace nyion
+
+extern "C" int32_t nyion_attn_decode_paged_f32_noalloc(
+    const float* q, const float* kv_pool, int64_t n_pool_pages, const int32_t* page_table,
+    int32_t max_pages, const int32_t* seq_lens, float* out, int32_t batch, int32_t n_heads,
+    int32_t n_kv_heads, int32_t head_dim, int32_t page_tokens, float scale, void* stream) {
+  int32_t st = check_common(n_heads, n_kv_heads, head_dim);
+  if (st) return st;
+  if (!q || !kv_pool || !page_table || !seq_lens || !out)
+    return fail(NYION_ERR_INVALID, "decode_paged_f32_noalloc: null pointer argument");
+  if (batch <= 0 || max_pages <= 0 || n_pool_pages <= 0)
+    return fail(NYION_ERR_INVALID, "decode_paged_f32_noalloc: batch, max_pages and n_pool_pages must be > 0");
+  if (page_tokens != PAGE)
+    return fail(NYION_ERR_UNSUPPORTED, "decode_paged_f32_noalloc: page_tokens must be 16 (got %d)", page_tokens);
+  if (batch > MAX_SEQS)
+    return fail(NYION_ERR_INVALID, "decode_paged_f32_noalloc: batch %d exceeds %d sequences per call",
+                batch, MAX_SEQS);
+  if ((uint64_t)n_pool_pages * n_kv_heads > (1ull << 31))
+    return fail(NYION_ERR_INVALID, "decode_paged_f32_noalloc: pool too large");
+  NoAllocDevice* d = nullptr;
+  st = noalloc_setup(&d);
+  if (st) return st;
+  // scratch layout for this launch: counters | (m, l) partials | o partials
+  const size_t pairs = (size_t)batch * n_kv_heads;
+  const size_t slots = ((size_t)d->grid + pairs) * NC;
+  auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
+  const size_t off_ml = al(pairs * sizeof(int32_t));
+  const size_t off_po = off_ml + al(slots * GROUP * sizeof(float2));
+  const size_t need = off_po + slots * GROUP * HD * sizeof(float);
+  if (need > kNoAllocScratchBytes)
+    return fail(NYION_ERR_WORKSPACE,
+                "decode_paged_f32_noalloc: %d sequences x %d KV heads need %zu bytes of scratch; "
+                "the static scratch holds %zu (use nyion_attn_decode_paged_f32 with a workspace)",
+                batch, n_kv_heads, need, kNoAllocScratchBytes);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = check_cuda(cudaMemsetAsync(d->scratch, 0, pairs * sizeof(int32_t), s), "clear merge counters");
+  if (st) return st;
+  CUtensorMap map;
+  st = pool_map(&map, kv_pool, n_pool_pages * n_kv_heads);
+  if (st) return st;
+  Params p{};
+  p.q = q;
+  p.out = out;
+  p.table = page_table;
+  p.seq_lens = seq_lens;
+  p.batch = batch;
+  p.n_kv = n_kv_heads;
+  p.max_pages = max_pages;
+  p.n_pool_pages = n_pool_pages;
+  p.qscale = (scale > 0.f ? scale : 1.0f / sqrtf((float)head_dim)) * 1.4426950408889634f;
+  p.cnt = reinterpret_cast<int32_t*>(d->scratch);
+  p.ml = reinterpret_cast<float2*>(d->scratch + off_ml);
+  p.po = reinterpret_cast<float*>(d->scratch + off_po);
+  p.err = d->err;
+  decode_f32_kernel<kPool><<<d->grid, THREADS, smem_bytes(), s>>>(p, map, map);
+  return check_cuda(cudaGetLastError(), "decode_f32_noalloc launch");
 }
