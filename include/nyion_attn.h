@@ -106,6 +106,64 @@ int32_t nyion_attn_decode_paged_f32_noalloc(const float* q, const float* kv_pool
                                             int32_t n_kv_heads, int32_t head_dim,
                                             int32_t page_tokens, float scale, void* stream);
 
+/* ------------------------------------------------------------ 4-bit KV -----
+ * Block format of swamp-engine/src/cache.rs:637-663: 32 values -> 20 bytes
+ * [f16 d][f16 dmin][16 bytes nibbles], element i in byte i/2, low nibble for
+ * even i.  Rows are head_dim values: ceil(head_dim/32) blocks per row. */
+
+/* Quantizer of PagedKVCache::save / save_at (cache.rs:637-663, 768-807), one
+ * fresh row at a time (nibbles written into zeroed bytes): bit-exact.
+ * src [n_rows][head_dim] f32 -> dst [n_rows][ceil(head_dim/32)][20] bytes. */
+int32_t nyion_attn_quantize_q4(const float* src, uint8_t* dst, int64_t n_rows, int32_t head_dim,
+                               void* stream);
+/* Dequant of ensure_f32_page_in_zone (cache.rs:375-394), bit-exact:
+ * f32(d) * q + f32(dmin) with separate multiply and add. */
+int32_t nyion_attn_dequant_q4(const uint8_t* src, float* dst, int64_t n_rows, int32_t head_dim,
+                              void* stream);
+
+/* Q4 paged decode over a token range per sequence, producing log-sum-exp
+ * partials: the per-GPU step of the split-KV path and the 4-bit part of
+ * attention_sparse_q4's window (swamp-engine/src/ops.rs:597-723, with the
+ * writer-consistent nibble order of cache.rs).
+ *   kv_pool    [n_pool_pages][4 KV heads][K|V][16 slots][2 blocks x 20 B]
+ *   page_table [batch][max_pages] (16-token pages, absolute positions)
+ *   sequence b attends tokens [tok_begin[b], tok_end[b]) (device arrays), or
+ *   [u_begin, u_end) for every sequence when the arrays are NULL
+ *   part       [batch][n_heads][head_dim + 2]: o normalised by l, then m (max
+ *              scaled score, natural log units), l = sum exp(s - m); an empty
+ *              range gives (0, -inf, 0).
+ * This build: 32 query heads, 4 KV heads, head_dim 64, page_tokens 16.
+ * workspace: nyion_attn_q4_workspace_size(batch) bytes, reset once, or NULL
+ * for the library-owned one. */
+size_t nyion_attn_q4_workspace_size(int32_t batch);
+int32_t nyion_attn_decode_q4_partial(const float* q, const uint8_t* kv_pool, int64_t n_pool_pages,
+                                     const int32_t* page_table, int32_t max_pages,
+                                     const int32_t* tok_begin, const int32_t* tok_end,
+                                     int32_t u_begin, int32_t u_end, float* part, int32_t batch,
+                                     int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                                     int32_t page_tokens, float scale, void* workspace,
+                                     size_t workspace_bytes, void* stream);
+/* Merges n_parts partial arrays [n_parts][rows][head_dim + 2] (the format
+ * above) into out [rows][head_dim]: m = max m_g, w_g = l_g exp(m_g - m),
+ * out = sum w_g o_g / sum w_g.  Rows whose partials are all empty give 0. */
+int32_t nyion_attn_lse_combine(const float* parts, int32_t n_parts, int64_t rows, int32_t head_dim,
+                               float* out, void* stream);
+/* 4-bit windowed decode with an fp32 ring: sequence b of
+ * length L = seq_lens[b] attends [max(0, L - window), L); the newest
+ * min(ring_tokens, window) tokens come from the fp32 ring
+ * ring [batch][4][K|V][ring_tokens][head_dim] at slot pos % ring_tokens, the
+ * older ones from the Q4 pages.  out [batch][n_heads][head_dim].
+ * workspace: nyion_attn_q4_workspace_size(batch) + 2 * batch * n_heads *
+ * (head_dim + 2) * 4 + 8 * batch bytes, or NULL. */
+int32_t nyion_attn_decode_q4_window_ring(const float* q, const uint8_t* kv_pool,
+                                         int64_t n_pool_pages, const int32_t* page_table,
+                                         int32_t max_pages, const int32_t* seq_lens,
+                                         const float* ring, int32_t ring_tokens, int32_t window,
+                                         float* out, int32_t batch, int32_t n_heads,
+                                         int32_t n_kv_heads, int32_t head_dim, int32_t page_tokens,
+                                         float scale, void* workspace, size_t workspace_bytes,
+                                         void* stream);
+
 /* ------------------------------------------- reference-layout fp32 decode ----
  * ops::attention (swamp-engine/src/ops.rs:170-278) with the same argument
  * meaning: one sequence, query head h reads KV head h / (n_heads/n_kv_heads),

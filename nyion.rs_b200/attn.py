@@ -46,6 +46,14 @@ def lib() -> C.CDLL:
                                                   i32, f32, vp, sz, vp]),
             "nyion_attn_decode_zoned_f32": (i32, [vp, vp, vp, vp, i64, i32, i32, i64, i64, i32, i32,
                                                   i32, vp]),
+            "nyion_attn_quantize_q4": (i32, [vp, vp, i64, i32, vp]),
+            "nyion_attn_dequant_q4": (i32, [vp, vp, i64, i32, vp]),
+            "nyion_attn_q4_workspace_size": (sz, [i32]),
+            "nyion_attn_decode_q4_partial": (i32, [vp, vp, i64, vp, i32, vp, vp, i32, i32, vp, i32, i32,
+                                                   i32, i32, i32, f32, vp, sz, vp]),
+            "nyion_attn_lse_combine": (i32, [vp, i32, i64, i32, vp, vp]),
+            "nyion_attn_decode_q4_window_ring": (i32, [vp, vp, i64, vp, i32, vp, vp, i32, i32, vp, i32,
+                                                       i32, i32, i32, i32, f32, vp, sz, vp]),
             "gpu_attention_device": (C.c_int, [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int,
                                                C.c_int]),
             "gpu_attention_streamed": (C.c_int, [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int,
@@ -169,6 +177,80 @@ def decode_zoned_f32(q, k_arena, v_arena, n_layers: int, layer: int, seq_len: in
                                             n_pages, n_layers, layer, seq_len, q_pos, H, n_kv, D,
                                             _stream_ptr(stream)))
     return out
+
+
+def quantize_q4(src, stream=None):
+    """Reference 4-bit quantizer (bit-exact): src [..., D] f32 -> [..., ceil(D/32)*20] uint8."""
+    torch = _torch()
+    D = src.shape[-1]
+    nblk = (D + 31) // 32
+    rows = src.numel() // D
+    dst = torch.empty(src.shape[:-1] + (nblk * 20,), dtype=torch.uint8, device=src.device)
+    check(lib().nyion_attn_quantize_q4(_ptr(src.contiguous()), _ptr(dst), rows, D, _stream_ptr(stream)))
+    return dst
+
+
+def dequant_q4(src, head_dim: int, stream=None):
+    torch = _torch()
+    rows = src.numel() // (((head_dim + 31) // 32) * 20)
+    dst = torch.empty(src.shape[:-1] + (head_dim,), dtype=torch.float32, device=src.device)
+    check(lib().nyion_attn_dequant_q4(_ptr(src.contiguous()), _ptr(dst), rows, head_dim, _stream_ptr(stream)))
+    return dst
+
+
+class Q4Workspace:
+    def __init__(self, batch: int, extra: int = 0, device=None):
+        torch = _torch()
+        self.nbytes = int(lib().nyion_attn_q4_workspace_size(batch)) + extra
+        self.buf = torch.zeros(self.nbytes, dtype=torch.uint8, device=device or "cuda")
+
+    def ptr(self) -> int:
+        return int(self.buf.data_ptr())
+
+
+def decode_q4_partial(q, kv_pool, page_table, tok_begin=None, tok_end=None, u_begin=0, u_end=0,
+                      part=None, scale: float = 0.0, workspace=None, stream=None):
+    """Q4 paged decode partials [B, H, D+2] over per-sequence token ranges."""
+    torch = _torch()
+    B, H, D = q.shape
+    if part is None:
+        part = torch.empty(B, H, D + 2, dtype=torch.float32, device=q.device)
+    ws_ptr, ws_bytes = (0, 0) if workspace is None else (workspace.ptr(), workspace.nbytes)
+    check(lib().nyion_attn_decode_q4_partial(
+        _ptr(q), _ptr(kv_pool), kv_pool.shape[0], _ptr(page_table), page_table.shape[1],
+        _ptr(tok_begin), _ptr(tok_end), u_begin, u_end, _ptr(part), B, H, kv_pool.shape[1], D,
+        kv_pool.shape[3], float(scale), ws_ptr, ws_bytes, _stream_ptr(stream)))
+    return part
+
+
+def lse_combine(parts, out=None, stream=None):
+    torch = _torch()
+    G = parts.shape[0]
+    D = parts.shape[-1] - 2
+    rows = parts[0].numel() // (D + 2)
+    if out is None:
+        out = torch.empty(parts.shape[1:-1] + (D,), dtype=torch.float32, device=parts.device)
+    check(lib().nyion_attn_lse_combine(_ptr(parts.contiguous()), G, rows, D, _ptr(out), _stream_ptr(stream)))
+    return out
+
+
+def decode_q4_window_ring(q, kv_pool, page_table, seq_lens, ring, window: int, out=None,
+                          scale: float = 0.0, workspace=None, stream=None):
+    """Config-3 decode: Q4 window + fp32 ring of the newest tokens."""
+    torch = _torch()
+    B, H, D = q.shape
+    if out is None:
+        out = torch.empty_like(q)
+    ws_ptr, ws_bytes = (0, 0) if workspace is None else (workspace.ptr(), workspace.nbytes)
+    check(lib().nyion_attn_decode_q4_window_ring(
+        _ptr(q), _ptr(kv_pool), kv_pool.shape[0], _ptr(page_table), page_table.shape[1],
+        _ptr(seq_lens), _ptr(ring), ring.shape[3], window, _ptr(out), B, H, kv_pool.shape[1], D,
+        kv_pool.shape[3], float(scale), ws_ptr, ws_bytes, _stream_ptr(stream)))
+    return out
+
+
+def window_ring_workspace(batch: int, n_heads: int = 32, head_dim: int = 64, device=None):
+    return Q4Workspace(batch, extra=2 * batch * n_heads * (head_dim + 2) * 4 + 8 * batch + 256, device=device)
 
 
 def device_error(stream=None) -> int:

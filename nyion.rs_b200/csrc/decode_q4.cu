@@ -1,0 +1,938 @@
+// decode_q4.cu — the 4-bit KV path: block quantizer / dequantizer, Q4 paged
+// decode producing log-sum-exp partials, the fp32 ring partial, and the
+// partial combine.
+//
+// Block format (swamp-engine/src/cache.rs:637-663, 375-394): 32 values ->
+// 20 bytes [f16 d][f16 dmin][16 bytes of nibbles], element i in byte i/2,
+// low nibble for even i; d = absmax / 7, q = clamp(round((x - dmin) / d), 0, 15),
+// dequant x' = f32(d) * q + f32(dmin).
+//
+// Q4 decode on B200.  A nibble n becomes the fp16 value 1 + n/16 with one
+// shift and one LOP3 per pair of values ((w << s) & 0x03C003C0 | 0x3C003C00),
+// so the block's dot product  sum q_i (d n_i + dmin)  becomes
+//   d * 16 * (sum q_i (1 + n_i/16) - sum q_i) + dmin * sum q_i,
+// with sum q_i (1 + n_i/16) on the tensor cores (mma.sync m16n8k16 f16, fp32
+// accumulate; q split into fp16 hi + lo rows) and the rest a per-score fix-up.
+// P.V uses the same identity: v = 16 d (1 + n/16) + (dmin - 16 d), so
+// o = sum_t (16 p_t d_t) v'_t  +  sum_t p_t (dmin_t - 16 d_t) per block.
+// Only the nibbles of V are staged again in shared memory, as a swizzled fp16
+// tile for ldmatrix.trans; K nibbles go straight from a 4-byte load into the
+// B fragments.  The dims inside a 32-value block are visited in a fixed
+// permutation (pairs (0,4), (1,5), (2,6), (3,7) of each 8-value group) that q
+// and the output share.
+#include <cuda_fp16.h>
+#include <math.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "host.h"
+
+namespace nyion {
+namespace q4 {
+
+constexpr int HD = 64;
+constexpr int GROUP = 8;
+constexpr int BLK = 20;                 // bytes per 32-value block
+constexpr int ROWB = 2 * BLK;           // bytes per token row (head_dim 64)
+constexpr int PAGE = 16;                // tokens per page
+constexpr int NKV = 4;                  // KV heads per page in this build
+constexpr int PAGE_KV = 2 * PAGE * ROWB;      // 1280 B: K rows then V rows of one KV head
+constexpr int PAGE_BYTES = NKV * PAGE_KV;     // 5120 B: one whole page
+constexpr int CHUNK = 64;               // tokens per stage (4 pages)
+constexpr int STAGE_BYTES = 4 * PAGE_BYTES;   // 20 KB
+constexpr int STAGES = 8;
+constexpr int NC = 8;                   // consumer warps: 4 KV heads x 2 token halves
+constexpr int THREADS = (NC + 1) * 32;
+constexpr int MAX_SEQS = 512;
+constexpr int MAX_GRID = 1024;
+constexpr int RING = 32;
+
+// ============================================================================
+// quantizer / dequantizer (bit-exact with cache.rs)
+// ============================================================================
+
+// One thread per (row, block): src [n_rows][head_dim] f32 -> dst [n_rows][nblk][20].
+__global__ void quantize_kernel(const float* __restrict__ src, uint8_t* __restrict__ dst,
+                                int64_t n_rows, int head_dim) {
+  const int nblk = (head_dim + 31) / 32;
+  const int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (id >= n_rows * nblk) return;
+  const int64_t row = id / nblk;
+  const int blk = (int)(id % nblk);
+  const int start = blk * 32;
+  const int len = min(32, head_dim - start);
+  const float* x = src + row * head_dim + start;
+  float v[32];
+  float mx = 0.0f, mn = 3.40282347e+38f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    v[i] = (i < len) ? x[i] : 0.0f;
+    if (i < len) {
+      mx = fmaxf(mx, fabsf(v[i]));
+      mn = fminf(mn, v[i]);
+    }
+  }
+  const float d = mx > 1e-10f ? __fdiv_rn(mx, 7.0f) : 0.0f;
+  const float dmin = mn;
+  const unsigned short hd = __half_as_ushort(__float2half_rn(d));
+  const unsigned short hm = __half_as_ushort(__float2half_rn(dmin));
+  uint32_t w[5];
+  w[0] = (uint32_t)hd | ((uint32_t)hm << 16);
+  w[1] = w[2] = w[3] = w[4] = 0u;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    uint32_t q = 0;
+    if (i < len && d > 1e-10f) {
+      float r = roundf(__fdiv_rn(__fsub_rn(v[i], dmin), d));
+      r = fminf(fmaxf(r, 0.0f), 15.0f);
+      q = (uint32_t)r;
+    }
+    // nibble i lives in byte 4 + i/2: word 1 + i/8, bit (i % 8) * 4
+    w[1 + i / 8] |= q << ((i % 8) * 4);
+  }
+  uint32_t* out = reinterpret_cast<uint32_t*>(dst + id * BLK);
+#pragma unroll
+  for (int j = 0; j < 5; ++j) out[j] = w[j];
+}
+
+__global__ void dequant_kernel(const uint8_t* __restrict__ src, float* __restrict__ dst,
+                               int64_t n_rows, int head_dim) {
+  const int nblk = (head_dim + 31) / 32;
+  const int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (id >= n_rows * nblk) return;
+  const int64_t row = id / nblk;
+  const int blk = (int)(id % nblk);
+  const int start = blk * 32;
+  const int len = min(32, head_dim - start);
+  const uint32_t* in = reinterpret_cast<const uint32_t*>(src + id * BLK);
+  const float d = __half2float(__ushort_as_half((unsigned short)(in[0] & 0xffffu)));
+  const float dmin = __half2float(__ushort_as_half((unsigned short)(in[0] >> 16)));
+  float* y = dst + row * head_dim + start;
+  for (int i = 0; i < len; ++i) {
+    const uint32_t q = (in[1 + i / 8] >> ((i % 8) * 4)) & 0xfu;
+    y[i] = __fadd_rn(__fmul_rn(d, (float)q), dmin);   // separate mul and add
+  }
+}
+
+// ============================================================================
+// Q4 paged decode -> log-sum-exp partials
+// ============================================================================
+
+struct Params {
+  const float* q;              // [batch][H][HD]
+  const uint8_t* pool;         // [n_pool_pages][NKV][K|V][PAGE][40]
+  const int32_t* table;        // [batch][max_pages]
+  const int32_t* tok_begin;    // [batch] or null -> u_begin
+  const int32_t* tok_end;      // [batch] or null -> u_end
+  int32_t u_begin, u_end;
+  int32_t batch, max_pages;
+  int64_t n_pool_pages;
+  float qscale;                // scale * log2(e)
+  float* part;                 // [batch][H][HD + 2]: o / l, m (natural log), l
+  int32_t* cnt;                // [batch * NKV]
+  float2* ml;                  // [(MAX_GRID + batch) * 2][NKV][GROUP]
+  float* po;                   // [(MAX_GRID + batch) * 2][NKV][GROUP][HD]
+  int32_t* err;
+};
+
+struct Smem {
+  uint8_t kv[STAGES][STAGE_BYTES];
+  uint8_t vt[NC][32 * 128];          // per warp: V chunk as fp16 [32 tokens][64], swizzled
+  uint64_t full[STAGES], empty[STAGES];
+  int32_t prefix[MAX_SEQS + 1];      // flat chunk index where sequence b starts
+  int32_t c0[MAX_SEQS];              // first chunk (absolute, in 64-token units) of sequence b
+  int32_t beg[MAX_SEQS], end[MAX_SEQS];
+  int32_t rows[2][RING][5];          // per chunk: 4 page ids (or -1) and the sequence index
+  int32_t warp_tot[THREADS / 32];
+  int32_t abort_;
+};
+
+__device__ __forceinline__ int seek_seq(const Smem& s, int batch, int i) {
+  int lo = 0, hi = batch;
+  while (hi - lo > 1) {
+    int mid = (lo + hi) >> 1;
+    if (s.prefix[mid] <= i) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
+struct RowJob {
+  int valid, b;
+  int32_t page[4];
+};
+
+__device__ __forceinline__ void rows_start(RowJob& j, const Smem& s, const Params& p, int i,
+                                           int end) {
+  j.valid = i < end;
+  if (!j.valid) return;
+  j.b = seek_seq(s, p.batch, i);
+  const int chunk = s.c0[j.b] + (i - s.prefix[j.b]);
+#pragma unroll
+  for (int pg = 0; pg < 4; ++pg) {
+    const int tok0 = chunk * CHUNK + pg * PAGE;
+    const int pidx = chunk * 4 + pg;
+    j.page[pg] = -2;   // not needed
+    if (tok0 < s.end[j.b] && tok0 + PAGE > s.beg[j.b])
+      j.page[pg] = (pidx < p.max_pages) ? p.table[(int64_t)j.b * p.max_pages + pidx] : -1;
+  }
+}
+
+__device__ __forceinline__ void rows_finish(Smem& s, const Params& p, const RowJob& j, int slot,
+                                            int lane) {
+  if (!j.valid) return;
+#pragma unroll
+  for (int pg = 0; pg < 4; ++pg) {
+    int32_t v = j.page[pg];
+    if (v == -1 || (v >= 0 && v >= p.n_pool_pages)) {
+      record_error(p.err, kErrPageRange);
+      v = -2;    // skipped: the stage slot keeps stale bytes, all its tokens are masked out
+    } else if (v < -2) {
+      record_error(p.err, kErrPageRange);
+      v = -2;
+    }
+    s.rows[slot][lane][pg] = v;
+  }
+  s.rows[slot][lane][4] = j.b;
+}
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// fp16x2 {1 + n_a/16, 1 + n_b/16} from the nibbles at bits [s+0..3] and [s+16..19] of w
+template <int SHIFT>
+__device__ __forceinline__ uint32_t nib2h(uint32_t w) {
+  const uint32_t x = SHIFT >= 0 ? (w << SHIFT) : (w >> (-SHIFT));
+  return (x & 0x03C003C0u) | 0x3C003C00u;
+}
+
+__device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, "
+      "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void split_f16x2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __floats2half2_rn(x0, x1);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  const float2 hf = __half22float2(h);
+  const __half2 r = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
+  lo = *reinterpret_cast<const uint32_t*>(&r);
+}
+
+__device__ __forceinline__ float2 hdr2f(uint32_t w) {   // (d, dmin) of a block header word
+  return make_float2(__half2float(__ushort_as_half((unsigned short)(w & 0xffffu))),
+                     __half2float(__ushort_as_half((unsigned short)(w >> 16))));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                          uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ void sts_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
+// dim visited at position c (0..63) of a row: pairs (0,4),(1,5),(2,6),(3,7) per 8-group
+__device__ __forceinline__ int perm_dim(int c) {
+  const int base = c & ~7, e = c & 7;
+  return base + ((e & 1) ? 4 : 0) + (e >> 1);
+}
+
+__global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                     ~uintptr_t(1023));
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int H = NKV * GROUP;
+
+  if (t == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], NC);
+    }
+    s.abort_ = 0;
+    fence_barrier_init();
+  }
+  for (int b = t; b < p.batch; b += THREADS) {
+    int lo = p.tok_begin ? p.tok_begin[b] : p.u_begin;
+    int hi = p.tok_end ? p.tok_end[b] : p.u_end;
+    lo = max(lo, 0);
+    if (hi < lo) hi = lo;
+    s.beg[b] = lo;
+    s.end[b] = hi;
+    s.c0[b] = lo / CHUNK;
+  }
+  __syncthreads();
+  constexpr int PER = (MAX_SEQS + THREADS - 1) / THREADS;
+  int local[PER];
+  int run = 0;
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int b = t * PER + j;
+    int c = 0;
+    if (b < p.batch && s.end[b] > s.beg[b]) c = (s.end[b] + CHUNK - 1) / CHUNK - s.c0[b];
+    local[j] = run;
+    run += c;
+  }
+  int incl = run;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) s.warp_tot[warp] = incl;
+  __syncthreads();
+  int woff = 0;
+  for (int w = 0; w < warp; ++w) woff += s.warp_tot[w];
+  const int excl = woff + incl - run;
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int b = t * PER + j;
+    if (b <= p.batch) s.prefix[b] = excl + local[j];
+  }
+  __syncthreads();
+
+  // empty ranges: partial = (0, -inf, 0)
+  for (int b = blockIdx.x; b < p.batch; b += gridDim.x) {
+    if (s.end[b] <= s.beg[b]) {
+      for (int e = t; e < H * (HD + 2); e += THREADS) {
+        const int c = e % (HD + 2);
+        p.part[(int64_t)b * H * (HD + 2) + e] = (c == HD) ? -INFINITY : 0.0f;
+      }
+    }
+  }
+
+  const int total = s.prefix[p.batch];
+  const int W = (total + gridDim.x - 1) / gridDim.x;
+  const int begin = blockIdx.x * W;
+  const int end = min(total, begin + W);
+  if (begin >= end) return;
+  const int n = end - begin;
+
+  if (warp == NC) {
+    // ================= producer warp: whole pages by bulk copy =================
+    RowJob job;
+    rows_start(job, s, p, begin + lane, end);
+    rows_finish(s, p, job, 0, lane);
+    rows_start(job, s, p, begin + RING + lane, end);
+    __syncwarp();
+    for (int k = 0; k < n; ++k) {
+      const int stage = k % STAGES;
+      if (k % RING == RING / 2) {
+        rows_finish(s, p, job, ((k / RING) + 1) & 1, lane);
+        __syncwarp();
+      } else if (k % RING == 0 && k > 0) {
+        rows_start(job, s, p, begin + k + RING + lane, end);
+      }
+      bool ok = true;
+      if (k >= STAGES) ok = mbar_wait_bounded(&s.empty[stage], (uint32_t)(((k / STAGES) - 1) & 1));
+      if (!__all_sync(0xffffffffu, ok)) {
+        record_error(p.err, kErrWaitTimeout);
+        if (lane == 0) {
+          atomicExch(&s.abort_, 1);
+          for (int c = k - 1; c >= 0 && c >= k - STAGES; --c)
+            mbar_wait_bounded(&s.full[c % STAGES], (uint32_t)((c / STAGES) & 1));
+        }
+        return;
+      }
+      if (lane == 0) {
+        const int32_t* e = s.rows[(k / RING) & 1][k % RING];
+        uint32_t bytes = 0;
+#pragma unroll
+        for (int pg = 0; pg < 4; ++pg) bytes += (e[pg] >= 0) ? PAGE_BYTES : 0;
+        // an all-skipped chunk still completes the phase through the arrive itself
+        mbar_arrive_expect_tx(&s.full[stage], bytes);
+#pragma unroll
+        for (int pg = 0; pg < 4; ++pg)
+          if (e[pg] >= 0)
+            bulk_load(s.kv[stage] + pg * PAGE_BYTES, p.pool + (int64_t)e[pg] * PAGE_BYTES,
+                      PAGE_BYTES, &s.full[stage]);
+      }
+      __syncwarp();
+    }
+    return;
+  }
+
+  // ================= consumer warps =================
+  const int kvh = warp & 3, th = warp >> 2;
+  const int g = lane >> 2, tig = lane & 3;
+  const uint32_t vt = smem_u32(s.vt[warp]);
+  // ldmatrix.trans row addresses of the V tile for k-step kt, n-tile pair np:
+  // matrix m = lane>>3: tokens 16kt + 8(m&1) + (lane&7), 16-B chunk 2np + (m>>1)
+  uint32_t voff[2][4];
+#pragma unroll
+  for (int kt = 0; kt < 2; ++kt)
+#pragma unroll
+    for (int np = 0; np < 4; ++np) {
+      const uint32_t tok = 16 * kt + 8 * ((lane >> 3) & 1) + (lane & 7);
+      const uint32_t ch = 2 * np + (lane >> 4);
+      voff[kt][np] = tok * 128 + (((ch ^ tok) & 7) << 4);
+    }
+
+  int i = begin;
+  while (i < end) {
+    const int b = seek_seq(s, p.batch, i);
+    const int seg_hi = min(end, s.prefix[b + 1]);
+    const int sb = s.beg[b], se = s.end[b];
+    // q fragments, dims permuted: k-step (blk, ks) pairs dims 32blk + 8tig + {ks*2 + (0,4)} in
+    // a0/a1 and {ks*2 + (1,5)} in a2/a3, hi rows 0-7 and lo rows 8-15
+    uint32_t qa[2][2][4];
+    float qs[2];      // sum of the (hi + lo) q values of head g over each block
+    {
+      const float* qp = p.q + ((int64_t)b * H + kvh * GROUP + g) * HD;
+#pragma unroll
+      for (int blk = 0; blk < 2; ++blk) {
+        float x[8];
+        const float4 a = __ldg(reinterpret_cast<const float4*>(qp + 32 * blk + 8 * tig));
+        const float4 c = __ldg(reinterpret_cast<const float4*>(qp + 32 * blk + 8 * tig + 4));
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = c.x; x[5] = c.y; x[6] = c.z; x[7] = c.w;
+        float sum = 0.f;
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks) {
+          uint32_t h0, l0, h1, l1;
+          split_f16x2(x[2 * ks] * p.qscale, x[2 * ks + 4] * p.qscale, h0, l0);
+          split_f16x2(x[2 * ks + 1] * p.qscale, x[2 * ks + 5] * p.qscale, h1, l1);
+          qa[blk][ks][0] = h0; qa[blk][ks][1] = l0; qa[blk][ks][2] = h1; qa[blk][ks][3] = l1;
+          const float2 fh0 = __half22float2(*reinterpret_cast<const __half2*>(&h0));
+          const float2 fl0 = __half22float2(*reinterpret_cast<const __half2*>(&l0));
+          const float2 fh1 = __half22float2(*reinterpret_cast<const __half2*>(&h1));
+          const float2 fl1 = __half22float2(*reinterpret_cast<const __half2*>(&l1));
+          sum += (fh0.x + fl0.x) + (fh0.y + fl0.y) + (fh1.x + fl1.x) + (fh1.y + fl1.y);
+        }
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        qs[blk] = sum;
+      }
+    }
+    float o[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) o[nt][j] = 0.f;
+    float cb[2] = {0.f, 0.f};   // sum_t p_t (dmin - 16 d) per V block (this thread's tokens)
+    float m = -INFINITY, l = 0.f;
+
+    for (int k = i - begin; k < seg_hi - begin; ++k) {
+      const int stage = k % STAGES;
+      const int chunk = s.c0[b] + (begin + k - s.prefix[b]);
+      const int pos0 = chunk * CHUNK + 32 * th;       // absolute position of this warp's token 0
+      if (!s.abort_) {
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&s.full[stage], (uint32_t)((k / STAGES) & 1)))) {
+          record_error(p.err, kErrWaitTimeout);
+          if (lane == 0) atomicExch(&s.abort_, 1);
+        }
+      }
+      const bool any = (pos0 < se) && (pos0 + 32 > sb);
+      if (any) {
+        const uint32_t kb = smem_u32(s.kv[stage]) + 2 * th * PAGE_BYTES + kvh * PAGE_KV;
+        // token t of this warp: page 2th + t/16 (offset (t/16)*PAGE_BYTES), row t%16
+        // ---- V nibbles of token `lane` -> fp16 tile row `lane` ----
+        {
+          const uint32_t vr = kb + (lane >> 4) * PAGE_BYTES + PAGE * ROWB + (lane & 15) * ROWB;
+#pragma unroll
+          for (int blk = 0; blk < 2; ++blk)
+#pragma unroll
+            for (int wq = 0; wq < 4; ++wq) {
+              const uint32_t w = lds_u32(vr + blk * BLK + 4 + 4 * wq);
+              const uint32_t ch = 4 * blk + wq;
+              sts_v4(vt + lane * 128 + (((ch ^ lane) & 7) << 4), nib2h<6>(w), nib2h<2>(w),
+                     nib2h<-2>(w), nib2h<-6>(w));
+            }
+        }
+        // ---- S = Q K^T: 4 n-tiles of 8 tokens, 2 blocks x 2 k-steps ----
+        float sc[4][2][4];
+        float kd[4][2][2], km[4][2][2];   // K (d, dmin) for tokens 8nt + 2tig + {0,1}
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+          const int tk = 8 * nt + g;
+          const uint32_t kr = kb + (tk >> 4) * PAGE_BYTES + (tk & 15) * ROWB;
+#pragma unroll
+          for (int blk = 0; blk < 2; ++blk) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) sc[nt][blk][j] = 0.f;
+            const uint32_t w = lds_u32(kr + blk * BLK + 4 + 4 * tig);
+            mma_f16(sc[nt][blk], qa[blk][0], nib2h<6>(w), nib2h<2>(w));
+            mma_f16(sc[nt][blk], qa[blk][1], nib2h<-2>(w), nib2h<-6>(w));
+          }
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int tt = 8 * nt + 2 * tig + e;
+            const uint32_t hr = kb + (tt >> 4) * PAGE_BYTES + (tt & 15) * ROWB;
+#pragma unroll
+            for (int blk = 0; blk < 2; ++blk) {
+              const float2 h = hdr2f(lds_u32(hr + blk * BLK));
+              kd[nt][blk][e] = h.x;
+              km[nt][blk][e] = h.y;
+            }
+          }
+        }
+        float sv[4][2];
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            float acc = 0.f;
+#pragma unroll
+            for (int blk = 0; blk < 2; ++blk) {
+              const float dot = sc[nt][blk][e] + sc[nt][blk][2 + e];      // sum q (1 + n/16)
+              acc = fmaf(kd[nt][blk][e] * 16.0f, dot - qs[blk], acc);
+              acc = fmaf(km[nt][blk][e], qs[blk], acc);
+            }
+            const int pos = pos0 + 8 * nt + 2 * tig + e;
+            sv[nt][e] = (pos >= sb && pos < se) ? acc : -INFINITY;
+          }
+        // ---- online softmax ----
+        float mx = sv[0][0];
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) mx = fmaxf(mx, fmaxf(sv[nt][0], sv[nt][1]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float mn = fmaxf(m, mx);
+        const float al = exp2f(m - mn);
+        float ps = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+          sv[nt][0] = exp2f(sv[nt][0] - mn);
+          sv[nt][1] = exp2f(sv[nt][1] - mn);
+          ps += sv[nt][0] + sv[nt][1];
+        }
+        l = fmaf(l, al, ps);
+        m = mn;
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) o[nt][j] *= al;
+        cb[0] *= al;
+        cb[1] *= al;
+        // ---- P'_blk = 16 p d_V (A operand), correction terms ----
+        uint32_t pa[2][2][4];   // [blk][kt]
+#pragma unroll
+        for (int kt = 0; kt < 2; ++kt) {
+          float pv[2][4];       // [blk][token e: 16kt + 2tig + {0,1,8,9}]
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int nt = 2 * kt + (e >> 1);
+            const int tt = 8 * nt + 2 * tig + (e & 1);
+            const float pe = sv[nt][e & 1];
+            const uint32_t hr = kb + (tt >> 4) * PAGE_BYTES + PAGE * ROWB + (tt & 15) * ROWB;
+#pragma unroll
+            for (int blk = 0; blk < 2; ++blk) {
+              const float2 h = hdr2f(lds_u32(hr + blk * BLK));
+              // masked tokens (p = 0) may sit on stale bytes: keep their headers out
+              pv[blk][e] = pe > 0.f ? pe * h.x * 16.0f : 0.f;
+              if (pe > 0.f) cb[blk] = fmaf(pe, h.y - 16.0f * h.x, cb[blk]);
+            }
+          }
+#pragma unroll
+          for (int blk = 0; blk < 2; ++blk) {
+            split_f16x2(pv[blk][0], pv[blk][1], pa[blk][kt][0], pa[blk][kt][1]);
+            split_f16x2(pv[blk][2], pv[blk][3], pa[blk][kt][2], pa[blk][kt][3]);
+          }
+        }
+        __syncwarp();   // V tile rows written by all lanes
+        // ---- O += P' V': k = 16 tokens, n-tiles of 8 (permuted) dims ----
+#pragma unroll
+        for (int kt = 0; kt < 2; ++kt)
+#pragma unroll
+          for (int np = 0; np < 4; ++np) {
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4_t(vt + voff[kt][np], b0, b1, b2, b3);
+            const int blk = np >> 1;
+            mma_f16(o[2 * np], pa[blk][kt], b0, b1);
+            mma_f16(o[2 * np + 1], pa[blk][kt], b2, b3);
+          }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.empty[stage]);
+    }
+
+    // ---- segment end: publish (m, l, o) of (b, kvh) for this warp ----
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+#pragma unroll
+    for (int blk = 0; blk < 2; ++blk) {
+      cb[blk] += __shfl_xor_sync(0xffffffffu, cb[blk], 1);
+      cb[blk] += __shfl_xor_sync(0xffffffffu, cb[blk], 2);
+    }
+    const int pair = b * NKV + kvh;
+    const int pstart = s.prefix[b], pend = s.prefix[b + 1];
+    const int cfirst = pstart / W, clast = (pend - 1) / W;
+    const int contributors = 2 * (clast - cfirst + 1);
+    const int64_t slot = (((int64_t)blockIdx.x + b) * 2 + th) * NKV + kvh;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int c = 8 * nt + 2 * tig + e;
+        const float val = o[nt][e] + o[nt][2 + e] + cb[nt >> 2];
+        __stcg(p.po + (slot * GROUP + g) * HD + perm_dim(c), val);
+      }
+    if (tig == 0) __stcg(&p.ml[slot * GROUP + g], make_float2(m, l));
+    __threadfence();
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) {
+      const int old = atomicAdd(&p.cnt[pair], 1);
+      last = (old == contributors - 1);
+      if (last) atomicExch(&p.cnt[pair], 0);
+      __threadfence();
+    }
+    if (__shfl_sync(0xffffffffu, last, 0)) {
+      // merge every (CTA, half) partial of (b, kvh): lane -> head lane>>2, dims 16*(lane&3)..
+      const int mh = lane >> 2, md = 16 * (lane & 3);
+      float M = -INFINITY, den = 0.f;
+      float4 acc[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int c = cfirst; c <= clast; ++c)
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int64_t sl = (((int64_t)c + b) * 2 + h2) * NKV + kvh;
+          const float2 mlv = __ldcg(&p.ml[sl * GROUP + mh]);
+          if (!(mlv.y > 0.f)) continue;
+          const float Mn = fmaxf(M, mlv.x);
+          const float sa = exp2f(M - Mn), sbw = exp2f(mlv.x - Mn);
+          den = den * sa + mlv.y * sbw;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float4 ov = ld_cg4(p.po + (sl * GROUP + mh) * HD + md + 4 * e);
+            acc[e].x = fmaf(acc[e].x, sa, ov.x * sbw);
+            acc[e].y = fmaf(acc[e].y, sa, ov.y * sbw);
+            acc[e].z = fmaf(acc[e].z, sa, ov.z * sbw);
+            acc[e].w = fmaf(acc[e].w, sa, ov.w * sbw);
+          }
+          M = Mn;
+        }
+      float* dst = p.part + ((int64_t)b * H + kvh * GROUP + mh) * (HD + 2);
+      const float inv = den > 0.f ? 1.0f / den : 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        dst[md + 4 * e + 0] = acc[e].x * inv;
+        dst[md + 4 * e + 1] = acc[e].y * inv;
+        dst[md + 4 * e + 2] = acc[e].z * inv;
+        dst[md + 4 * e + 3] = acc[e].w * inv;
+      }
+      if ((lane & 3) == 0) {
+        dst[HD] = den > 0.f ? M * 0.6931471805599453f : -INFINITY;   // log2 -> natural units
+        dst[HD + 1] = den;
+      }
+    }
+    i = seg_hi;
+  }
+}
+
+// ============================================================================
+// fp32 ring partial: tokens [max(beg, L - R), L) from ring [batch][NKV][2][R][HD]
+// ============================================================================
+// One CTA per (sequence, KV head): 8 warps = 8 query heads, lane = token
+// stride 32.  The ring is small (R <= 1024): plain coalesced loads.
+__global__ void __launch_bounds__(256) ring_partial_kernel(const float* __restrict__ q,
+                                                          const float* __restrict__ ring,
+                                                          const int32_t* __restrict__ seq_lens,
+                                                          int32_t u_len, int32_t ring_tokens,
+                                                          int32_t window, float qscale,
+                                                          float* __restrict__ part) {
+  const int b = blockIdx.x / NKV, kvh = blockIdx.x % NKV;
+  const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int H = NKV * GROUP;
+  const int L = seq_lens ? seq_lens[b] : u_len;
+  const int lo = max(max(0, L - window), L - ring_tokens), hi = L;
+  float* dst = part + ((int64_t)b * H + kvh * GROUP + h) * (HD + 2);
+  const float* qp = q + ((int64_t)b * H + kvh * GROUP + h) * HD;
+  float qv[HD];
+#pragma unroll
+  for (int d = 0; d < HD; ++d) qv[d] = __ldg(qp + d) * qscale;
+  const float* kb = ring + ((int64_t)(b * NKV + kvh) * 2 + 0) * ring_tokens * HD;
+  const float* vb = ring + ((int64_t)(b * NKV + kvh) * 2 + 1) * ring_tokens * HD;
+  float m = -INFINITY, l = 0.f;
+  float o0 = 0.f, o1 = 0.f;   // dims 2*lane, 2*lane+1
+  for (int t0 = lo; t0 < hi; t0 += 32) {
+    const int tt = t0 + lane;
+    float sc = -INFINITY;
+    if (tt < hi) {
+      const float* kr = kb + (int64_t)(tt % ring_tokens) * HD;
+      float a = 0.f;
+#pragma unroll
+      for (int d = 0; d < HD; d += 4) {
+        const float4 kk = __ldg(reinterpret_cast<const float4*>(kr + d));
+        a = fmaf(qv[d], kk.x, a); a = fmaf(qv[d + 1], kk.y, a);
+        a = fmaf(qv[d + 2], kk.z, a); a = fmaf(qv[d + 3], kk.w, a);
+      }
+      sc = a;
+    }
+    const float mx = warp_max(sc);
+    const float mn = fmaxf(m, mx);
+    const float al = exp2f(m - mn);
+    const float pe = exp2f(sc - mn);
+    l = l * al + warp_sum(pe);
+    o0 *= al;
+    o1 *= al;
+    for (int j = 0; j < 32 && t0 + j < hi; ++j) {
+      const float pj = __shfl_sync(0xffffffffu, pe, j);
+      const float2 vv = __ldg(reinterpret_cast<const float2*>(vb + (int64_t)((t0 + j) % ring_tokens) * HD) + lane);
+      o0 = fmaf(pj, vv.x, o0);
+      o1 = fmaf(pj, vv.y, o1);
+    }
+    m = mn;
+  }
+  const float inv = l > 0.f ? 1.0f / l : 0.f;
+  dst[2 * lane] = o0 * inv;
+  dst[2 * lane + 1] = o1 * inv;
+  if (lane == 0) {
+    dst[HD] = l > 0.f ? m * 0.6931471805599453f : -INFINITY;
+    dst[HD + 1] = l;
+  }
+}
+
+// ============================================================================
+// log-sum-exp combine: parts [G][rows][HD+2] -> out [rows][HD]
+// ============================================================================
+__global__ void lse_combine_kernel(const float* __restrict__ parts, int G, int64_t rows,
+                                   float* __restrict__ out) {
+  const int64_t r = (int64_t)blockIdx.x * (blockDim.x / 16) + (threadIdx.x >> 4);
+  const int d4 = (threadIdx.x & 15) * 4;
+  if (r >= rows) return;
+  float M = -INFINITY;
+  for (int gi = 0; gi < G; ++gi) {
+    const float* pp = parts + ((int64_t)gi * rows + r) * (HD + 2);
+    if (pp[HD + 1] > 0.f) M = fmaxf(M, pp[HD]);
+  }
+  float den = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (M != -INFINITY) {
+    for (int gi = 0; gi < G; ++gi) {
+      const float* pp = parts + ((int64_t)gi * rows + r) * (HD + 2);
+      const float lg = pp[HD + 1];
+      if (!(lg > 0.f)) continue;
+      const float w = lg * expf(pp[HD] - M);
+      den += w;
+      acc.x = fmaf(w, pp[d4], acc.x);
+      acc.y = fmaf(w, pp[d4 + 1], acc.y);
+      acc.z = fmaf(w, pp[d4 + 2], acc.z);
+      acc.w = fmaf(w, pp[d4 + 3], acc.w);
+    }
+  }
+  const float inv = den > 0.f ? 1.0f / den : 0.f;
+  *reinterpret_cast<float4*>(out + r * HD + d4) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+}
+
+// Window split of config 3: Q4 tokens [max(0, L - window), max(that, L - ring)),
+// the fp32 ring covers the rest of the window up to L.
+__global__ void q4_window_ranges(const int32_t* __restrict__ seq_lens, int batch, int window,
+                                 int ring, int32_t* __restrict__ beg, int32_t* __restrict__ end) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= batch) return;
+  const int L = seq_lens[b];
+  const int w0 = max(0, L - window);
+  beg[b] = w0;
+  end[b] = max(w0, L - ring);
+}
+
+size_t smem_bytes() { return sizeof(Smem) + 1024; }
+
+struct WsLayout {
+  size_t cnt, ml, po, total;
+};
+
+WsLayout ws_layout(int batch) {
+  const int b = batch < MAX_SEQS ? batch : MAX_SEQS;
+  const size_t slots = (size_t)(MAX_GRID + b) * 2 * NKV;
+  auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
+  WsLayout w;
+  w.cnt = 0;
+  w.ml = al((size_t)b * NKV * sizeof(int32_t));
+  w.po = w.ml + al(slots * GROUP * sizeof(float2));
+  w.total = w.po + al(slots * GROUP * HD * sizeof(float));
+  return w;
+}
+
+int32_t check_shape(int32_t n_heads, int32_t n_kv_heads, int32_t head_dim) {
+  if (n_kv_heads != NKV || n_heads != NKV * GROUP || head_dim != HD)
+    return fail(NYION_ERR_UNSUPPORTED,
+                "the 4-bit kernels of this build take 32 query heads, 4 KV heads, head_dim 64 "
+                "(got %d/%d/%d)", n_heads, n_kv_heads, head_dim);
+  return NYION_OK;
+}
+
+int32_t launch_partial(Params base, int batch, const int32_t* tok_begin, const int32_t* tok_end,
+                       const float* q, float* part, const int32_t* table, void* ws,
+                       cudaStream_t stream) {
+  DeviceInfo* dev = nullptr;
+  int32_t st = device_info(&dev);
+  if (st) return st;
+  static int grid_cache[64] = {0};
+  const int di = dev->device < 64 ? dev->device : 0;
+  const size_t smem = smem_bytes();
+  if (!grid_cache[di]) {
+    st = check_cuda(cudaFuncSetAttribute(decode_q4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem),
+                    "cudaFuncSetAttribute(decode_q4)");
+    if (st) return st;
+    int occ = 0;
+    st = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_q4_kernel, THREADS, smem),
+                    "occupancy(decode_q4)");
+    if (st) return st;
+    grid_cache[di] = dev->num_sms * (occ > 0 ? occ : 1);
+    if (grid_cache[di] > MAX_GRID) grid_cache[di] = MAX_GRID;
+  }
+  const WsLayout w = ws_layout(batch);
+  for (int b0 = 0; b0 < batch; b0 += MAX_SEQS) {
+    Params p = base;
+    const int nb = batch - b0 < MAX_SEQS ? batch - b0 : MAX_SEQS;
+    p.batch = nb;
+    p.tok_begin = tok_begin ? tok_begin + b0 : nullptr;
+    p.tok_end = tok_end ? tok_end + b0 : nullptr;
+    p.q = q + (int64_t)b0 * NKV * GROUP * HD;
+    p.part = part + (int64_t)b0 * NKV * GROUP * (HD + 2);
+    p.table = table + (int64_t)b0 * base.max_pages;
+    p.cnt = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws) + w.cnt);
+    p.ml = reinterpret_cast<float2*>(static_cast<uint8_t*>(ws) + w.ml);
+    p.po = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + w.po);
+    p.err = dev->err_word;
+    decode_q4_kernel<<<grid_cache[di], THREADS, smem, stream>>>(p);
+    st = check_cuda(cudaGetLastError(), "decode_q4 launch");
+    if (st) return st;
+  }
+  return NYION_OK;
+}
+
+}  // namespace q4
+}  // namespace nyion
+
+using namespace nyion;
+using namespace nyion::q4;
+
+extern "C" int32_t nyion_attn_quantize_q4(const float* src, uint8_t* dst, int64_t n_rows,
+                                          int32_t head_dim, void* stream) {
+  if (!src || !dst || n_rows < 0 || head_dim <= 0)
+    return fail(NYION_ERR_INVALID, "quantize_q4: bad arguments");
+  if (n_rows == 0) return NYION_OK;
+  const int64_t n = n_rows * ((head_dim + 31) / 32);
+  quantize_kernel<<<(unsigned)((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(src, dst, n_rows,
+                                                                                          head_dim);
+  return check_cuda(cudaGetLastError(), "quantize_q4 launch");
+}
+
+extern "C" int32_t nyion_attn_dequant_q4(const uint8_t* src, float* dst, int64_t n_rows,
+                                         int32_t head_dim, void* stream) {
+  if (!src || !dst || n_rows < 0 || head_dim <= 0)
+    return fail(NYION_ERR_INVALID, "dequant_q4: bad arguments");
+  if (n_rows == 0) return NYION_OK;
+  const int64_t n = n_rows * ((head_dim + 31) / 32);
+  dequant_kernel<<<(unsigned)((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(src, dst, n_rows,
+                                                                                         head_dim);
+  return check_cuda(cudaGetLastError(), "dequant_q4 launch");
+}
+
+extern "C" size_t nyion_attn_q4_workspace_size(int32_t batch) {
+  return batch > 0 ? ws_layout(batch).total : 0;
+}
+
+extern "C" int32_t nyion_attn_decode_q4_partial(const float* q, const uint8_t* kv_pool,
+                                                int64_t n_pool_pages, const int32_t* page_table,
+                                                int32_t max_pages, const int32_t* tok_begin,
+                                                const int32_t* tok_end, int32_t u_begin,
+                                                int32_t u_end, float* part, int32_t batch,
+                                                int32_t n_heads, int32_t n_kv_heads,
+                                                int32_t head_dim, int32_t page_tokens, float scale,
+                                                void* workspace, size_t workspace_bytes,
+                                                void* stream) {
+  int32_t st = check_shape(n_heads, n_kv_heads, head_dim);
+  if (st) return st;
+  if (!q || !kv_pool || !page_table || !part)
+    return fail(NYION_ERR_INVALID, "decode_q4_partial: null pointer argument");
+  if (page_tokens != PAGE)
+    return fail(NYION_ERR_UNSUPPORTED, "decode_q4_partial: page_tokens must be 16");
+  if (batch <= 0 || max_pages <= 0 || n_pool_pages <= 0)
+    return fail(NYION_ERR_INVALID, "decode_q4_partial: batch, max_pages, n_pool_pages must be > 0");
+  if (reinterpret_cast<uintptr_t>(kv_pool) % 16)
+    return fail(NYION_ERR_INVALID, "decode_q4_partial: kv_pool must be 16-byte aligned");
+  const size_t need = ws_layout(batch).total;
+  if (!workspace) {
+    st = internal_workspace(need, &workspace);
+    if (st) return st;
+  } else if (workspace_bytes < need) {
+    return fail(NYION_ERR_WORKSPACE, "decode_q4_partial: workspace %zu < %zu", workspace_bytes, need);
+  }
+  Params p{};
+  p.pool = kv_pool;
+  p.u_begin = u_begin;
+  p.u_end = u_end;
+  p.max_pages = max_pages;
+  p.n_pool_pages = n_pool_pages;
+  p.qscale = (scale > 0.f ? scale : 1.0f / sqrtf((float)head_dim)) * 1.4426950408889634f;
+  return launch_partial(p, batch, tok_begin, tok_end, q, part, page_table, workspace,
+                        static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int32_t nyion_attn_lse_combine(const float* parts, int32_t n_parts, int64_t rows,
+                                          int32_t head_dim, float* out, void* stream) {
+  if (!parts || !out || n_parts <= 0 || rows <= 0)
+    return fail(NYION_ERR_INVALID, "lse_combine: bad arguments");
+  if (head_dim != HD) return fail(NYION_ERR_UNSUPPORTED, "lse_combine: head_dim must be 64");
+  lse_combine_kernel<<<(unsigned)((rows + 15) / 16), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      parts, n_parts, rows, out);
+  return check_cuda(cudaGetLastError(), "lse_combine launch");
+}
+
+extern "C" int32_t nyion_attn_decode_q4_window_ring(
+    const float* q, const uint8_t* kv_pool, int64_t n_pool_pages, const int32_t* page_table,
+    int32_t max_pages, const int32_t* seq_lens, const float* ring, int32_t ring_tokens,
+    int32_t window, float* out, int32_t batch, int32_t n_heads, int32_t n_kv_heads,
+    int32_t head_dim, int32_t page_tokens, float scale, void* workspace, size_t workspace_bytes,
+    void* stream) {
+  int32_t st = check_shape(n_heads, n_kv_heads, head_dim);
+  if (st) return st;
+  if (!q || !kv_pool || !page_table || !seq_lens || !ring || !out)
+    return fail(NYION_ERR_INVALID, "decode_q4_window_ring: null pointer argument");
+  if (ring_tokens <= 0 || window <= 0 || batch <= 0)
+    return fail(NYION_ERR_INVALID, "decode_q4_window_ring: ring_tokens, window, batch must be > 0");
+  // workspace: [q4 partial workspace][2 partial arrays of batch*H*(HD+2) floats][tok ranges]
+  const size_t q4ws = ws_layout(batch).total;
+  const size_t rows = (size_t)batch * n_heads;
+  const size_t parts_bytes = 2 * rows * (HD + 2) * sizeof(float);
+  const size_t range_bytes = 2 * (size_t)batch * sizeof(int32_t);
+  const size_t need = q4ws + parts_bytes + range_bytes;
+  if (!workspace) {
+    st = internal_workspace(need, &workspace);
+    if (st) return st;
+  } else if (workspace_bytes < need) {
+    return fail(NYION_ERR_WORKSPACE, "decode_q4_window_ring: workspace %zu < %zu", workspace_bytes, need);
+  }
+  uint8_t* w = static_cast<uint8_t*>(workspace);
+  float* parts = reinterpret_cast<float*>(w + q4ws);
+  int32_t* rng = reinterpret_cast<int32_t*>(w + q4ws + parts_bytes);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // Q4 part: [max(0, L - window), max(0, L - ring)) ; ring part: the rest of the window
+  q4_window_ranges<<<(batch + 127) / 128, 128, 0, s>>>(seq_lens, batch, window, ring_tokens, rng, rng + batch);
+  st = check_cuda(cudaGetLastError(), "window ranges");
+  if (st) return st;
+  Params p{};
+  p.pool = kv_pool;
+  p.max_pages = max_pages;
+  p.n_pool_pages = n_pool_pages;
+  const float sc = (scale > 0.f ? scale : 1.0f / sqrtf((float)head_dim));
+  p.qscale = sc * 1.4426950408889634f;
+  st = launch_partial(p, batch, rng, rng + batch, q, parts, page_table, w, s);
+  if (st) return st;
+  ring_partial_kernel<<<batch * NKV, 256, 0, s>>>(q, ring, seq_lens, 0, ring_tokens, window,
+                                                  sc * 1.4426950408889634f, parts + rows * (HD + 2));
+  st = check_cuda(cudaGetLastError(), "ring_partial launch");
+  if (st) return st;
+  return nyion_attn_lse_combine(parts, 2, (int64_t)rows, HD, out, stream);
+}
