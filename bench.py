@@ -181,6 +181,113 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+
+# --------------------------------------------------------------------- configs 3 and 5
+def build_q4_pages(A, torch, n_tokens, dev, gen, page_perm=True):
+    """N(0,1) K/V for n_tokens tokens of 4 KV heads quantized on the GPU by the
+    reference quantizer into a 16-token page pool; returns (pool, table row)."""
+    n_pages = (n_tokens + PT - 1) // PT
+    pool = torch.empty(n_pages, N_KV, 2, PT, 40, dtype=torch.uint8, device=dev)
+    order = torch.randperm(n_pages, device=dev, generator=gen) if page_perm else torch.arange(n_pages, device=dev)
+    step = 4096                                   # pages per slice (64K tokens)
+    for p0 in range(0, n_pages, step):
+        p1 = min(n_pages, p0 + step)
+        src = torch.randn((p1 - p0) * PT, N_KV, 2, D, device=dev, generator=gen)
+        q4 = A.quantize_q4(src).reshape(p1 - p0, PT, N_KV, 2, 40).permute(0, 2, 3, 1, 4)
+        pool[order[p0:p1]] = q4
+    return pool, order.to(torch.int32)
+
+
+def timed_graph(torch, fn, stream, steps, warmup, barrier, dist=None, world=1, dev=None, graph=True):
+    """CUDA-event time of fn() per call (graph replay when capture works), max over ranks."""
+    g = None
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, warmup)):
+            fn()
+    torch.cuda.synchronize()
+    mode = "eager"
+    if graph:
+        try:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                fn()
+            torch.cuda.synchronize()
+            mode = "graph"
+        except Exception as e:  # capture not possible (e.g. a collective): time eagerly
+            g = None
+            mode = f"eager ({type(e).__name__})"
+            torch.cuda.synchronize()
+    run = g.replay if g is not None else fn
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, warmup)):
+            run()
+        torch.cuda.synchronize()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            run()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    ms = e0.elapsed_time(e1) / steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    del g
+    return ms, mode
+
+
+def run_config3(A, torch, dev, stream, args, barrier, dist, world):
+    """Config 3: B=16, window 4096 of 65536, fp32 ring of the last 128 tokens."""
+    B, L, W, R = 16, 65536, 4096, 128
+    mp = L // PT
+    gen = torch.Generator(device=dev).manual_seed(303)
+    pool = torch.empty(B * mp, N_KV, 2, PT, 40, dtype=torch.uint8, device=dev)
+    table = torch.empty(B, mp, dtype=torch.int32, device=dev)
+    for b in range(B):
+        pb, order = build_q4_pages(A, torch, L, dev, gen)
+        table[b] = order + b * mp
+        pool[b * mp:(b + 1) * mp] = pb
+    ring = torch.randn(B, N_KV, 2, R, D, device=dev, generator=gen)
+    q = torch.randn(B, H, D, device=dev, generator=gen)
+    lens = torch.full((B,), L, dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+    ws = A.window_ring_workspace(B, device=dev)
+    fn = lambda: A.decode_q4_window_ring(q, pool, table, lens, ring, W, out=out, workspace=ws, stream=stream)
+    ms, mode = timed_graph(torch, fn, stream, args.steps, args.warmup, barrier, dist, world, dev)
+    q4_bytes = B * 2 * N_KV * (W - R) * 40
+    ring_bytes = B * 2 * N_KV * R * D * 4
+    qo = 2 * B * H * D * 4
+    total = q4_bytes + ring_bytes + qo
+    return {"workload": "config3: B=16, Q4 window 4096 of 65536 + fp32 ring 128", "us_per_layer_step": ms * 1e3,
+            "gbs": total / (ms * 1e-3) / 1e9, "bytes_per_layer_step": total, "timing": mode,
+            "launches_per_step": 2}
+
+
+def run_config5(A, S, torch, dev, stream, args, barrier, dist, world, rank):
+    """Config 5: B=1, 1M-token Q4 context split evenly over the ranks, partials
+    merged by one all-gather + log-sum-exp combine (strong scaling)."""
+    T = 1 << 20
+    dec = S.SplitKVDecoder(rank, world, T)
+    first, last = dec.lo // PT, (dec.hi + PT - 1) // PT
+    gen = torch.Generator(device=dev).manual_seed(505 + rank)
+    pool, order = build_q4_pages(A, torch, dec.hi - dec.lo, dev, gen)
+    table = torch.zeros(1, T // PT, dtype=torch.int32, device=dev)
+    table[0, first:last] = order
+    qg = torch.Generator(device=dev).manual_seed(555)
+    q = torch.randn(1, H, D, device=dev, generator=qg)
+    fn = lambda: dec.step(q, pool, table, stream=stream)
+    ms, mode = timed_graph(torch, fn, stream, args.steps, args.warmup, barrier, dist, world, dev)
+    total = T * 2 * N_KV * 40
+    return {"workload": "config5: B=1, 1M-token Q4 split-KV, NCCL all-gather + LSE combine",
+            "n_gpus": world, "us_per_step": ms * 1e3, "gbs_whole_job": total / (ms * 1e-3) / 1e9,
+            "bytes_per_step": total, "bytes_per_gpu": (dec.hi - dec.lo) * 2 * N_KV * 40,
+            "allgather_bytes_per_gpu": H * (D + 2) * 4, "timing": mode, "scaling": "strong"}
+
+
 # --------------------------------------------------------------------- GPU leg
 def run_gpu(args, rank, world):
     import torch
@@ -191,6 +298,18 @@ def run_gpu(args, rank, world):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     A.lib()
+    if args.only:
+        import torch.distributed as dist_
+        S = __import__("nyion_rs_b200.splitkv", fromlist=["x"])
+        st = torch.cuda.Stream(device=dev)
+        bar = (lambda: dist_.barrier()) if world > 1 else (lambda: None)
+        if args.only == "config3":
+            r = run_config3(A, torch, dev, st, args, bar, dist_, world)
+        else:
+            r = run_config5(A, S, torch, dev, st, args, bar, dist_, world, rank)
+        if rank == 0:
+            print(json.dumps(r), flush=True)
+        return
 
     LAYERS = args.layers
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
@@ -293,6 +412,15 @@ def run_gpu(args, rank, world):
     err = A.device_error(stream)
     del graph
 
+    extra = {}
+    if not args.no_extra:
+        del pool, tables
+        torch.cuda.empty_cache()
+        S = sys.modules.get("nyion_rs_b200.splitkv") or __import__("nyion_rs_b200.splitkv", fromlist=["x"])
+        if world == 1:
+            extra["q4_window_ring"] = run_config3(A, torch, dev, stream, args, barrier, dist, world)
+        extra["split_kv_1m"] = run_config5(A, S, torch, dev, stream, args, barrier, dist, world, rank)
+
     step_bytes = layer_step_bytes() * LAYERS
     if LAYERS != 22:
         print(f"# profiling run with {LAYERS} layers: not a config-2 measurement", file=sys.stderr)
@@ -335,6 +463,7 @@ def run_gpu(args, rank, world):
             "clocks": clocks.summary(),
             "device_error": err,
         }
+        line.update(extra)
         print(json.dumps(line), flush=True)
 
 
@@ -345,6 +474,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the config 3 / config 5 legs")
+    ap.add_argument("--only", choices=["config3", "config5"], default=None,
+                    help="profiling runs: time only this leg (prints its JSON object)")
     ap.add_argument("--cpu-seconds", type=float, default=6.0)
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layers per step (22 = config 2; smaller only for profiling captures)")

@@ -125,14 +125,15 @@ struct Params {
   const int32_t* table;        // [batch][max_pages]
   const int32_t* tok_begin;    // [batch] or null -> u_begin
   const int32_t* tok_end;      // [batch] or null -> u_end
+  const int32_t* seq_lens;     // window mode: [batch] lengths; Q4 range = window minus ring
+  int32_t window, ring_tokens; // window mode when seq_lens != null
   int32_t u_begin, u_end;
   int32_t batch, max_pages;
   int64_t n_pool_pages;
   float qscale;                // scale * log2(e)
-  float* part;                 // [batch][H][HD + 2]: o / l, m (natural log), l
-  int32_t* cnt;                // [batch * NKV]
-  float2* ml;                  // [(MAX_GRID + batch) * 2][NKV][GROUP]
-  float* po;                   // [(MAX_GRID + batch) * 2][NKV][GROUP][HD]
+  float* part;                 // [batch][H][HD + 2] result of the reduce: o / l, m (natural log), l
+  float* cta_part;             // [MAX_GRID + batch][NKV][GROUP][HD + 2]: o (relative to m), m (log2), l
+  int32_t* meta;               // [batch][2]: first and last CTA covering sequence b
   int32_t* err;
 };
 
@@ -253,6 +254,10 @@ __device__ __forceinline__ int perm_dim(int c) {
   return base + ((e & 1) ? 4 : 0) + (e >> 1);
 }
 
+__device__ __forceinline__ void named_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(NC * 32) : "memory");
+}
+
 __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const Params p) {
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -269,8 +274,16 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const Params p) {
     fence_barrier_init();
   }
   for (int b = t; b < p.batch; b += THREADS) {
-    int lo = p.tok_begin ? p.tok_begin[b] : p.u_begin;
-    int hi = p.tok_end ? p.tok_end[b] : p.u_end;
+    int lo, hi;
+    if (p.seq_lens) {
+      // config-3 split: Q4 tokens [max(0, L - window), max(that, L - ring))
+      const int L = p.seq_lens[b];
+      lo = max(0, L - p.window);
+      hi = max(lo, L - p.ring_tokens);
+    } else {
+      lo = p.tok_begin ? p.tok_begin[b] : p.u_begin;
+      hi = p.tok_end ? p.tok_end[b] : p.u_end;
+    }
     lo = max(lo, 0);
     if (hi < lo) hi = lo;
     s.beg[b] = lo;
@@ -307,18 +320,15 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const Params p) {
   }
   __syncthreads();
 
-  // empty ranges: partial = (0, -inf, 0)
-  for (int b = blockIdx.x; b < p.batch; b += gridDim.x) {
-    if (s.end[b] <= s.beg[b]) {
-      for (int e = t; e < H * (HD + 2); e += THREADS) {
-        const int c = e % (HD + 2);
-        p.part[(int64_t)b * H * (HD + 2) + e] = (c == HD) ? -INFINITY : 0.0f;
-      }
-    }
-  }
-
   const int total = s.prefix[p.batch];
   const int W = (total + gridDim.x - 1) / gridDim.x;
+  if (blockIdx.x == 0) {
+    for (int b = t; b < p.batch; b += THREADS) {
+      const int lo = s.prefix[b], hi = s.prefix[b + 1];
+      p.meta[2 * b] = hi > lo ? lo / W : 0;
+      p.meta[2 * b + 1] = hi > lo ? (hi - 1) / W : -1;   // -1: empty range
+    }
+  }
   const int begin = blockIdx.x * W;
   const int end = min(total, begin + W);
   if (begin >= end) return;
@@ -561,7 +571,8 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const Params p) {
       if (lane == 0) mbar_arrive(&s.empty[stage]);
     }
 
-    // ---- segment end: publish (m, l, o) of (b, kvh) for this warp ----
+    // ---- segment end: the two token halves of each KV head merge in shared
+    //      memory, one partial per (CTA, sequence, KV head) goes to the workspace ----
     l += __shfl_xor_sync(0xffffffffu, l, 1);
     l += __shfl_xor_sync(0xffffffffu, l, 2);
 #pragma unroll
@@ -569,133 +580,180 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const Params p) {
       cb[blk] += __shfl_xor_sync(0xffffffffu, cb[blk], 1);
       cb[blk] += __shfl_xor_sync(0xffffffffu, cb[blk], 2);
     }
-    const int pair = b * NKV + kvh;
-    const int pstart = s.prefix[b], pend = s.prefix[b + 1];
-    const int cfirst = pstart / W, clast = (pend - 1) / W;
-    const int contributors = 2 * (clast - cfirst + 1);
-    const int64_t slot = (((int64_t)blockIdx.x + b) * 2 + th) * NKV + kvh;
+    named_sync();                       // every warp is done with its V tile
+    float* mine = reinterpret_cast<float*>(s.vt[warp]);   // [GROUP][HD + 2]
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int c = 8 * nt + 2 * tig + e;
-        const float val = o[nt][e] + o[nt][2 + e] + cb[nt >> 2];
-        __stcg(p.po + (slot * GROUP + g) * HD + perm_dim(c), val);
+        mine[g * (HD + 2) + perm_dim(c)] = o[nt][e] + o[nt][2 + e] + cb[nt >> 2];
       }
-    if (tig == 0) __stcg(&p.ml[slot * GROUP + g], make_float2(m, l));
-    __threadfence();
-    __syncwarp();
-    int last = 0;
-    if (lane == 0) {
-      const int old = atomicAdd(&p.cnt[pair], 1);
-      last = (old == contributors - 1);
-      if (last) atomicExch(&p.cnt[pair], 0);
-      __threadfence();
+    if (tig == 0) {
+      mine[g * (HD + 2) + HD] = m;
+      mine[g * (HD + 2) + HD + 1] = l;
     }
-    if (__shfl_sync(0xffffffffu, last, 0)) {
-      // merge every (CTA, half) partial of (b, kvh): lane -> head lane>>2, dims 16*(lane&3)..
+    named_sync();
+    if (th == 0) {
+      // lane -> head lane>>2, dims 16*(lane&3) .. +15; partner warp holds the other half
+      const float* a0 = reinterpret_cast<const float*>(s.vt[warp]);
+      const float* a1 = reinterpret_cast<const float*>(s.vt[warp + 4]);
       const int mh = lane >> 2, md = 16 * (lane & 3);
-      float M = -INFINITY, den = 0.f;
-      float4 acc[4];
+      const float m0 = a0[mh * (HD + 2) + HD], l0 = a0[mh * (HD + 2) + HD + 1];
+      const float m1 = a1[mh * (HD + 2) + HD], l1 = a1[mh * (HD + 2) + HD + 1];
+      const float M = fmaxf(m0, m1);
+      const float w0 = (l0 > 0.f) ? exp2f(m0 - M) : 0.f, w1 = (l1 > 0.f) ? exp2f(m1 - M) : 0.f;
+      float* dst = p.cta_part + ((((int64_t)blockIdx.x + b) * NKV + kvh) * GROUP + mh) * (HD + 2);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) acc[e] = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int c = cfirst; c <= clast; ++c)
-#pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-          const int64_t sl = (((int64_t)c + b) * 2 + h2) * NKV + kvh;
-          const float2 mlv = __ldcg(&p.ml[sl * GROUP + mh]);
-          if (!(mlv.y > 0.f)) continue;
-          const float Mn = fmaxf(M, mlv.x);
-          const float sa = exp2f(M - Mn), sbw = exp2f(mlv.x - Mn);
-          den = den * sa + mlv.y * sbw;
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float4 ov = ld_cg4(p.po + (sl * GROUP + mh) * HD + md + 4 * e);
-            acc[e].x = fmaf(acc[e].x, sa, ov.x * sbw);
-            acc[e].y = fmaf(acc[e].y, sa, ov.y * sbw);
-            acc[e].z = fmaf(acc[e].z, sa, ov.z * sbw);
-            acc[e].w = fmaf(acc[e].w, sa, ov.w * sbw);
-          }
-          M = Mn;
-        }
-      float* dst = p.part + ((int64_t)b * H + kvh * GROUP + mh) * (HD + 2);
-      const float inv = den > 0.f ? 1.0f / den : 0.f;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        dst[md + 4 * e + 0] = acc[e].x * inv;
-        dst[md + 4 * e + 1] = acc[e].y * inv;
-        dst[md + 4 * e + 2] = acc[e].z * inv;
-        dst[md + 4 * e + 3] = acc[e].w * inv;
+      for (int e = 0; e < 16; ++e) {
+        const float v0 = (l0 > 0.f) ? a0[mh * (HD + 2) + md + e] : 0.f;
+        const float v1 = (l1 > 0.f) ? a1[mh * (HD + 2) + md + e] : 0.f;
+        __stcg(dst + md + e, w0 * v0 + w1 * v1);
       }
       if ((lane & 3) == 0) {
-        dst[HD] = den > 0.f ? M * 0.6931471805599453f : -INFINITY;   // log2 -> natural units
-        dst[HD + 1] = den;
+        __stcg(dst + HD, M);
+        __stcg(dst + HD + 1, w0 * l0 + w1 * l1);
       }
     }
+    named_sync();                       // partner tiles are read before the next segment writes them
     i = seg_hi;
   }
 }
 
 // ============================================================================
-// fp32 ring partial: tokens [max(beg, L - R), L) from ring [batch][NKV][2][R][HD]
+// reduce of the per-CTA partials: one CTA per (sequence, query head) row
 // ============================================================================
-// One CTA per (sequence, KV head): 8 warps = 8 query heads, lane = token
-// stride 32.  The ring is small (R <= 1024): plain coalesced loads.
-__global__ void __launch_bounds__(256) ring_partial_kernel(const float* __restrict__ q,
-                                                          const float* __restrict__ ring,
-                                                          const int32_t* __restrict__ seq_lens,
-                                                          int32_t u_len, int32_t ring_tokens,
-                                                          int32_t window, float qscale,
-                                                          float* __restrict__ part) {
-  const int b = blockIdx.x / NKV, kvh = blockIdx.x % NKV;
-  const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int H = NKV * GROUP;
-  const int L = seq_lens ? seq_lens[b] : u_len;
-  const int lo = max(max(0, L - window), L - ring_tokens), hi = L;
-  float* dst = part + ((int64_t)b * H + kvh * GROUP + h) * (HD + 2);
-  const float* qp = q + ((int64_t)b * H + kvh * GROUP + h) * HD;
-  float qv[HD];
+// 8 warps take the covering CTAs round-robin (lane = 2 dims, four partial
+// loads in flight), then warp 0 folds the 8 warp results.  Output is the
+// partial format (o/l, m natural, l) or, with `final_out`, o/l alone.
+struct RingArgs {
+  const float* q;          // [batch][H][HD]
+  const float* ring;       // [batch][NKV][K|V][ring_tokens][HD]
+  const int32_t* seq_lens; // [batch]
+  int32_t ring_tokens, window;
+  float qscale;            // scale * log2(e)
+};
+
+constexpr int RING_MAX = 256;   // ring tokens folded into the reduce (larger rings: error)
+
+__global__ void __launch_bounds__(256) q4_reduce_kernel(const float* __restrict__ cta_part,
+                                                       const int32_t* __restrict__ meta, int batch,
+                                                       float* __restrict__ part,
+                                                       float* __restrict__ final_out,
+                                                       const RingArgs ra) {
+  __shared__ float red[9][HD + 2];
+  __shared__ float qs_[HD];
+  __shared__ float sc_[RING_MAX];
+  __shared__ float pv_[4][HD];
+  __shared__ float lr_[4];
+  const int row = blockIdx.x;                 // b * 32 + h
+  const int b = row / (NKV * GROUP), h = row % (NKV * GROUP);
+  const int kvh = h / GROUP, hh = h % GROUP;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cf = meta[2 * b], cl = meta[2 * b + 1];
+  float M = -INFINITY, L = 0.f, o0 = 0.f, o1 = 0.f;
+  for (int c0 = cf + warp; c0 <= cl; c0 += 32) {
+    float2 ml[4], ov[4];
 #pragma unroll
-  for (int d = 0; d < HD; ++d) qv[d] = __ldg(qp + d) * qscale;
-  const float* kb = ring + ((int64_t)(b * NKV + kvh) * 2 + 0) * ring_tokens * HD;
-  const float* vb = ring + ((int64_t)(b * NKV + kvh) * 2 + 1) * ring_tokens * HD;
-  float m = -INFINITY, l = 0.f;
-  float o0 = 0.f, o1 = 0.f;   // dims 2*lane, 2*lane+1
-  for (int t0 = lo; t0 < hi; t0 += 32) {
-    const int tt = t0 + lane;
-    float sc = -INFINITY;
-    if (tt < hi) {
-      const float* kr = kb + (int64_t)(tt % ring_tokens) * HD;
+    for (int u = 0; u < 4; ++u) {
+      const int c = c0 + 8 * u;
+      if (c <= cl) {
+        const float* src = cta_part + ((((int64_t)c + b) * NKV + kvh) * GROUP + hh) * (HD + 2);
+        ml[u] = __ldcg(reinterpret_cast<const float2*>(src + HD));
+        ov[u] = __ldcg(reinterpret_cast<const float2*>(src) + lane);
+      } else {
+        ml[u] = make_float2(-INFINITY, 0.f);
+        ov[u] = make_float2(0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (!(ml[u].y > 0.f)) continue;
+      const float Mn = fmaxf(M, ml[u].x);
+      const float sa = exp2f(M - Mn), sb = exp2f(ml[u].x - Mn);
+      L = L * sa + ml[u].y * sb;
+      o0 = o0 * sa + ov[u].x * sb;
+      o1 = o1 * sa + ov[u].y * sb;
+      M = Mn;
+    }
+  }
+  red[warp][2 * lane] = o0;
+  red[warp][2 * lane + 1] = o1;
+  if (lane == 0) {
+    red[warp][HD] = M;
+    red[warp][HD + 1] = L;
+  }
+  int nparts = 8;
+  if (ra.ring) {
+    // fp32 ring tokens [max(max(0, L - window), L - ring), L) at slot pos % ring
+    const int Ls = ra.seq_lens[b];
+    const int lo = max(max(0, Ls - ra.window), Ls - ra.ring_tokens), n = Ls - lo;
+    const int t = threadIdx.x;
+    if (t < HD) qs_[t] = ra.q[((int64_t)b * NKV * GROUP + h) * HD + t] * ra.qscale;
+    __syncthreads();
+    const float* kb = ra.ring + ((int64_t)(b * NKV + kvh) * 2 + 0) * ra.ring_tokens * HD;
+    const float* vb = ra.ring + ((int64_t)(b * NKV + kvh) * 2 + 1) * ra.ring_tokens * HD;
+    for (int j = t; j < n; j += 256) {
+      const float* kr = kb + (int64_t)((lo + j) % ra.ring_tokens) * HD;
       float a = 0.f;
 #pragma unroll
       for (int d = 0; d < HD; d += 4) {
         const float4 kk = __ldg(reinterpret_cast<const float4*>(kr + d));
-        a = fmaf(qv[d], kk.x, a); a = fmaf(qv[d + 1], kk.y, a);
-        a = fmaf(qv[d + 2], kk.z, a); a = fmaf(qv[d + 3], kk.w, a);
+        a = fmaf(qs_[d], kk.x, a); a = fmaf(qs_[d + 1], kk.y, a);
+        a = fmaf(qs_[d + 2], kk.z, a); a = fmaf(qs_[d + 3], kk.w, a);
       }
-      sc = a;
+      sc_[j] = a;
     }
-    const float mx = warp_max(sc);
-    const float mn = fmaxf(m, mx);
-    const float al = exp2f(m - mn);
-    const float pe = exp2f(sc - mn);
-    l = l * al + warp_sum(pe);
-    o0 *= al;
-    o1 *= al;
-    for (int j = 0; j < 32 && t0 + j < hi; ++j) {
-      const float pj = __shfl_sync(0xffffffffu, pe, j);
-      const float2 vv = __ldg(reinterpret_cast<const float2*>(vb + (int64_t)((t0 + j) % ring_tokens) * HD) + lane);
-      o0 = fmaf(pj, vv.x, o0);
-      o1 = fmaf(pj, vv.y, o1);
+    __syncthreads();
+    float mr = -INFINITY;
+    for (int j = lane; j < n; j += 32) mr = fmaxf(mr, sc_[j]);
+    mr = warp_max(mr);
+    // 4 token quarters x 64 dims
+    const int dq = t & 63, qq = t >> 6;
+    float acc = 0.f, lr = 0.f;
+    for (int j = qq; j < n; j += 4) {
+      const float pe = exp2f(sc_[j] - mr);
+      lr += pe;
+      acc = fmaf(pe, __ldg(vb + (int64_t)((lo + j) % ra.ring_tokens) * HD + dq), acc);
     }
-    m = mn;
+    pv_[qq][dq] = acc;
+    if (dq == 0) lr_[qq] = lr;
+    __syncthreads();
+    if (t < HD) {
+      red[8][t] = pv_[0][t] + pv_[1][t] + pv_[2][t] + pv_[3][t];
+      if (t == 0) {
+        const float lsum = lr_[0] + lr_[1] + lr_[2] + lr_[3];
+        red[8][HD] = n > 0 ? mr : -INFINITY;
+        red[8][HD + 1] = n > 0 ? lsum : 0.f;
+      }
+    }
+    nparts = 9;
   }
-  const float inv = l > 0.f ? 1.0f / l : 0.f;
-  dst[2 * lane] = o0 * inv;
-  dst[2 * lane + 1] = o1 * inv;
-  if (lane == 0) {
-    dst[HD] = l > 0.f ? m * 0.6931471805599453f : -INFINITY;
-    dst[HD + 1] = l;
+  __syncthreads();
+  if (warp != 0) return;
+  float Mt = -INFINITY;
+  for (int w = 0; w < nparts; ++w)
+    if (red[w][HD + 1] > 0.f) Mt = fmaxf(Mt, red[w][HD]);
+  float den = 0.f, a0 = 0.f, a1 = 0.f;
+  for (int w = 0; w < nparts; ++w) {
+    if (!(red[w][HD + 1] > 0.f)) continue;
+    const float wt = exp2f(red[w][HD] - Mt);
+    den = fmaf(wt, red[w][HD + 1], den);
+    a0 = fmaf(wt, red[w][2 * lane], a0);
+    a1 = fmaf(wt, red[w][2 * lane + 1], a1);
+  }
+  const float inv = den > 0.f ? 1.0f / den : 0.f;
+  if (final_out) {
+    final_out[(int64_t)row * HD + 2 * lane] = a0 * inv;
+    final_out[(int64_t)row * HD + 2 * lane + 1] = a1 * inv;
+  } else {
+    float* dst = part + (int64_t)row * (HD + 2);
+    dst[2 * lane] = a0 * inv;
+    dst[2 * lane + 1] = a1 * inv;
+    if (lane == 0) {
+      dst[HD] = den > 0.f ? Mt * 0.6931471805599453f : -INFINITY;   // log2 -> natural units
+      dst[HD + 1] = den;
+    }
   }
 }
 
@@ -731,33 +789,19 @@ __global__ void lse_combine_kernel(const float* __restrict__ parts, int G, int64
   *reinterpret_cast<float4*>(out + r * HD + d4) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
 }
 
-// Window split of config 3: Q4 tokens [max(0, L - window), max(that, L - ring)),
-// the fp32 ring covers the rest of the window up to L.
-__global__ void q4_window_ranges(const int32_t* __restrict__ seq_lens, int batch, int window,
-                                 int ring, int32_t* __restrict__ beg, int32_t* __restrict__ end) {
-  const int b = blockIdx.x * blockDim.x + threadIdx.x;
-  if (b >= batch) return;
-  const int L = seq_lens[b];
-  const int w0 = max(0, L - window);
-  beg[b] = w0;
-  end[b] = max(w0, L - ring);
-}
-
 size_t smem_bytes() { return sizeof(Smem) + 1024; }
 
 struct WsLayout {
-  size_t cnt, ml, po, total;
+  size_t meta, cta_part, total;
 };
 
 WsLayout ws_layout(int batch) {
   const int b = batch < MAX_SEQS ? batch : MAX_SEQS;
-  const size_t slots = (size_t)(MAX_GRID + b) * 2 * NKV;
   auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
   WsLayout w;
-  w.cnt = 0;
-  w.ml = al((size_t)b * NKV * sizeof(int32_t));
-  w.po = w.ml + al(slots * GROUP * sizeof(float2));
-  w.total = w.po + al(slots * GROUP * HD * sizeof(float));
+  w.meta = 0;
+  w.cta_part = al((size_t)b * 2 * sizeof(int32_t));
+  w.total = w.cta_part + al((size_t)(MAX_GRID + b) * NKV * GROUP * (HD + 2) * sizeof(float));
   return w;
 }
 
@@ -771,7 +815,7 @@ int32_t check_shape(int32_t n_heads, int32_t n_kv_heads, int32_t head_dim) {
 
 int32_t launch_partial(Params base, int batch, const int32_t* tok_begin, const int32_t* tok_end,
                        const float* q, float* part, const int32_t* table, void* ws,
-                       cudaStream_t stream) {
+                       cudaStream_t stream, float* final_out = nullptr, RingArgs ra = RingArgs{}) {
   DeviceInfo* dev = nullptr;
   int32_t st = device_info(&dev);
   if (st) return st;
@@ -800,12 +844,24 @@ int32_t launch_partial(Params base, int batch, const int32_t* tok_begin, const i
     p.q = q + (int64_t)b0 * NKV * GROUP * HD;
     p.part = part + (int64_t)b0 * NKV * GROUP * (HD + 2);
     p.table = table + (int64_t)b0 * base.max_pages;
-    p.cnt = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws) + w.cnt);
-    p.ml = reinterpret_cast<float2*>(static_cast<uint8_t*>(ws) + w.ml);
-    p.po = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + w.po);
+    p.seq_lens = base.seq_lens ? base.seq_lens + b0 : nullptr;
+    p.meta = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws) + w.meta);
+    p.cta_part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + w.cta_part);
     p.err = dev->err_word;
     decode_q4_kernel<<<grid_cache[di], THREADS, smem, stream>>>(p);
     st = check_cuda(cudaGetLastError(), "decode_q4 launch");
+    if (st) return st;
+    RingArgs r = ra;
+    if (r.ring) {
+      r.q = q + (int64_t)b0 * NKV * GROUP * HD;
+      r.ring = ra.ring + (int64_t)b0 * NKV * 2 * ra.ring_tokens * HD;
+      r.seq_lens = ra.seq_lens + b0;
+    }
+    p.seq_lens = base.seq_lens ? base.seq_lens + b0 : nullptr;
+    q4_reduce_kernel<<<nb * NKV * GROUP, 256, 0, stream>>>(p.cta_part, p.meta, nb, p.part,
+                                                            final_out ? final_out + (int64_t)b0 * NKV * GROUP * HD : nullptr,
+                                                            r);
+    st = check_cuda(cudaGetLastError(), "q4_reduce launch");
     if (st) return st;
   }
   return NYION_OK;
@@ -914,25 +970,27 @@ extern "C" int32_t nyion_attn_decode_q4_window_ring(
   } else if (workspace_bytes < need) {
     return fail(NYION_ERR_WORKSPACE, "decode_q4_window_ring: workspace %zu < %zu", workspace_bytes, need);
   }
+  if (ring_tokens > RING_MAX)
+    return fail(NYION_ERR_UNSUPPORTED, "decode_q4_window_ring: ring_tokens %d > %d", ring_tokens, RING_MAX);
   uint8_t* w = static_cast<uint8_t*>(workspace);
   float* parts = reinterpret_cast<float*>(w + q4ws);
-  int32_t* rng = reinterpret_cast<int32_t*>(w + q4ws + parts_bytes);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // Q4 part: [max(0, L - window), max(0, L - ring)) ; ring part: the rest of the window
-  q4_window_ranges<<<(batch + 127) / 128, 128, 0, s>>>(seq_lens, batch, window, ring_tokens, rng, rng + batch);
-  st = check_cuda(cudaGetLastError(), "window ranges");
-  if (st) return st;
   Params p{};
   p.pool = kv_pool;
   p.max_pages = max_pages;
   p.n_pool_pages = n_pool_pages;
+  p.seq_lens = seq_lens;
+  p.window = window;
+  p.ring_tokens = ring_tokens;
   const float sc = (scale > 0.f ? scale : 1.0f / sqrtf((float)head_dim));
   p.qscale = sc * 1.4426950408889634f;
-  st = launch_partial(p, batch, rng, rng + batch, q, parts, page_table, w, s);
-  if (st) return st;
-  ring_partial_kernel<<<batch * NKV, 256, 0, s>>>(q, ring, seq_lens, 0, ring_tokens, window,
-                                                  sc * 1.4426950408889634f, parts + rows * (HD + 2));
-  st = check_cuda(cudaGetLastError(), "ring_partial launch");
-  if (st) return st;
-  return nyion_attn_lse_combine(parts, 2, (int64_t)rows, HD, out, stream);
+  RingArgs ra{};
+  ra.q = q;
+  ra.ring = ring;
+  ra.seq_lens = seq_lens;
+  ra.ring_tokens = ring_tokens;
+  ra.window = window;
+  ra.qscale = p.qscale;
+  return launch_partial(p, batch, nullptr, nullptr, q, parts, page_table, w, s, out, ra);
 }
+
