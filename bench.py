@@ -65,6 +65,14 @@ def peaks():
         return 6650.0, "fallback"
 
 
+def peaks_all() -> dict:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
 class ClockSampler:
     """nvidia-smi clock/throttle samples during the timed region."""
 
@@ -267,6 +275,57 @@ def run_config3(A, torch, dev, stream, args, barrier, dist, world):
             "launches_per_step": 2}
 
 
+def prefill_flops(total=2048, heads=H, hd=D) -> int:
+    """Algorithmic FLOPs of a causal prefill: per query at position p and head,
+    QK^T and PV over p + 1 tokens, 2 * hd FLOPs each per token."""
+    return 4 * hd * heads * total * (total + 1) // 2
+
+
+def run_config4(A, torch, dev, stream, args):
+    """Config 4: causal chunked prefill, 2048 tokens in 4 chunks of 512,
+    32q/4kv/64, bf16 N(0,1)*0.5; L2 flushed between timed prefills."""
+    T, CH = 2048, 512
+    gen = torch.Generator(device=dev).manual_seed(404)
+    n_pool = T // PT + 9
+    table = torch.randperm(n_pool, device=dev, generator=gen)[:T // PT].to(torch.int32)
+    pool = (torch.randn(n_pool, N_KV, 2, PT, D, device=dev, generator=gen) * 0.5).to(torch.bfloat16)
+    q = (torch.randn(T, H, D, device=dev, generator=gen) * 0.5).to(torch.bfloat16)
+    out = torch.empty(T, H, D, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def prefill():
+        for c in range(T // CH):
+            A.prefill_paged_bf16(q[c * CH:(c + 1) * CH], pool, table, c * CH, out=out[c * CH:(c + 1) * CH],
+                                 stream=stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            prefill()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            prefill()
+        torch.cuda.synchronize()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+        for e0, e1 in evs:
+            flush.fill_(1)
+            e0.record(stream)
+            g.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+    ms = sum(e0.elapsed_time(e1) for e0, e1 in evs) / len(evs)
+    del g
+    fl = prefill_flops(T)
+    peak = float(peaks_all().get("bf16_tflops") or 1590.0)
+    tflops = fl / (ms * 1e-3) / 1e12
+    return {"workload": "config4: causal prefill 2048 tokens = 4 chunks of 512, 32q/4kv/64, bf16 paged cache",
+            "us_per_prefill": ms * 1e3, "tflops": tflops, "flops_per_prefill": fl,
+            "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
+                         "frac": tflops / peak, "peak_source": "measured bf16_tflops (burst)"},
+            "l2": "256 MB flush before every timed prefill", "timing": "graph of 4 launches",
+            "launches_per_step": T // CH, "device_error": A.device_error(stream)}
+
+
 def run_config5(A, S, torch, dev, stream, args, barrier, dist, world, rank):
     """Config 5: B=1, 1M-token Q4 context split evenly over the ranks, partials
     merged by one all-gather + log-sum-exp combine (strong scaling)."""
@@ -305,6 +364,8 @@ def run_gpu(args, rank, world):
         bar = (lambda: dist_.barrier()) if world > 1 else (lambda: None)
         if args.only == "config3":
             r = run_config3(A, torch, dev, st, args, bar, dist_, world)
+        elif args.only == "config4":
+            r = run_config4(A, torch, dev, st, args)
         else:
             r = run_config5(A, S, torch, dev, st, args, bar, dist_, world, rank)
         if rank == 0:
@@ -419,6 +480,7 @@ def run_gpu(args, rank, world):
         S = sys.modules.get("nyion_rs_b200.splitkv") or __import__("nyion_rs_b200.splitkv", fromlist=["x"])
         if world == 1:
             extra["q4_window_ring"] = run_config3(A, torch, dev, stream, args, barrier, dist, world)
+            extra["prefill_2048"] = run_config4(A, torch, dev, stream, args)
         extra["split_kv_1m"] = run_config5(A, S, torch, dev, stream, args, barrier, dist, world, rank)
 
     step_bytes = layer_step_bytes() * LAYERS
@@ -475,7 +537,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the config 3 / config 5 legs")
-    ap.add_argument("--only", choices=["config3", "config5"], default=None,
+    ap.add_argument("--only", choices=["config3", "config4", "config5"], default=None,
                     help="profiling runs: time only this leg (prints its JSON object)")
     ap.add_argument("--cpu-seconds", type=float, default=6.0)
     ap.add_argument("--layers", type=int, default=LAYERS,

@@ -180,6 +180,28 @@ int32_t nyion_attn_decode_zoned_f32(float* out, const float* q, const float* k_a
                                     int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
                                     void* stream);
 
+/* ------------------------------------------------ chunked causal prefill ----
+ * The attention step of prefill_slice (swamp-engine/src/executor.rs:106-138):
+ * for every prompt token t of a chunk the reference calls ops::attention with
+ * seq_len = pos_offset + t + 1 (ops.rs:170-278), after storing the chunk's
+ * K/V at positions pos_offset.. (executor.rs:106-111); chunks are
+ * PREFILL_CHUNK_SIZE = 4096 tokens (executor.rs:185).  This entry computes a
+ * whole chunk at once on the tensor cores from a bf16 paged cache:
+ *   q          [n_q][n_heads][head_dim] bf16, query positions q_start + i;
+ *   kv_pool    [n_pool_pages][n_kv_heads][2 (K,V)][page_tokens][head_dim] bf16,
+ *              already holding positions [0, q_start + n_q);
+ *   page_table [max_pages] int32 page ids of the sequence;
+ *   out        [n_q][n_heads][head_dim] f32.
+ * Query i attends tokens [0, q_start + i]; head h reads KV head
+ * h / (n_heads / n_kv_heads); scale <= 0 means 1/sqrt(head_dim).  This build
+ * takes head_dim 64, GQA group 8, page_tokens 16.  Scores, probabilities and
+ * products run in bf16 x bf16 -> f32 (the reference computes in f32). */
+int32_t nyion_attn_prefill_paged_bf16(const void* q, const void* kv_pool, int64_t n_pool_pages,
+                                      const int32_t* page_table, int32_t max_pages,
+                                      int64_t q_start, int64_t n_q, float* out, int32_t n_heads,
+                                      int32_t n_kv_heads, int32_t head_dim, int32_t page_tokens,
+                                      float scale, void* stream);
+
 /* ---------------------------------------------- reference CUDA C ABI -------
  * Same names, arguments and 0 / -1 results as swamp-gpu/kernels/fused_attention.cu,
  * so the reference's Rust declarations (swamp-gpu/src/lib.rs:586-677) link

@@ -54,7 +54,9 @@ def lib() -> C.CDLL:
             "nyion_attn_lse_combine": (i32, [vp, i32, i64, i32, vp, vp]),
             "nyion_attn_decode_q4_window_ring": (i32, [vp, vp, i64, vp, i32, vp, vp, i32, i32, vp, i32,
                                                        i32, i32, i32, i32, f32, vp, sz, vp]),
-            "gpu_attention_device": (C.c_int, [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int,
+            "nyion_attn_prefill_paged_bf16": (i32, [vp, vp, i64, vp, i32, i64, i64, vp, i32, i32, i32,
+                                                    i32, f32, vp]),
+            "gpu_attention_device": (C.c_int,[vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int,
                                                C.c_int]),
             "gpu_attention_streamed": (C.c_int, [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int,
                                                  C.c_int, C.c_int, vp]),
@@ -251,6 +253,23 @@ def decode_q4_window_ring(q, kv_pool, page_table, seq_lens, ring, window: int, o
 
 def window_ring_workspace(batch: int, n_heads: int = 32, head_dim: int = 64, device=None):
     return Q4Workspace(batch, extra=2 * batch * n_heads * (head_dim + 2) * 4 + 8 * batch + 256, device=device)
+
+
+def prefill_paged_bf16(q, kv_pool, page_table, q_start: int, out=None, scale: float = 0.0,
+                       stream=None):
+    """Causal chunked prefill (nyion_attn_prefill_paged_bf16).
+
+    q [n_q, H, D] bf16 at positions q_start..; kv_pool [pages, n_kv, 2, 16, D]
+    bf16; page_table [max_pages] int32; returns out [n_q, H, D] f32.
+    """
+    torch = _torch()
+    n_q, H, D = q.shape
+    if out is None:
+        out = torch.empty(n_q, H, D, dtype=torch.float32, device=q.device)
+    check(lib().nyion_attn_prefill_paged_bf16(
+        _ptr(q), _ptr(kv_pool), kv_pool.shape[0], _ptr(page_table), page_table.numel(), q_start, n_q,
+        _ptr(out), H, kv_pool.shape[1], D, kv_pool.shape[3], float(scale), _stream_ptr(stream)))
+    return out
 
 
 def device_error(stream=None) -> int:
