@@ -65,6 +65,18 @@ def peaks():
         return 6650.0, "fallback"
 
 
+def profiled_traffic():
+    """DRAM bytes per decode launch (read + write) from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "decode_f32_config2.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":", 1)[1])
+    except (OSError, ValueError):
+        pass
+    return None
+
+
 def peaks_all() -> dict:
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -490,13 +502,7 @@ def run_gpu(args, rank, world):
     per_launch_us = ms * 1e3 / LAYERS
     achieved = layer_step_bytes() / (per_launch_us * 1e-6) / 1e9
     peak, peak_kind = peaks()
-    traffic = None
-    tfile = os.path.join(ROOT, "profiles", "decode_f32_config2_traffic.json")
-    if os.path.exists(tfile):
-        try:
-            traffic = json.load(open(tfile)).get("traffic_bytes_per_launch")
-        except Exception:
-            traffic = None
+    traffic = profiled_traffic()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         c = time_cpu_oracle(budget_s=args.cpu_seconds)

@@ -202,6 +202,33 @@ int32_t nyion_attn_prefill_paged_bf16(const void* q, const void* kv_pool, int64_
                                       int32_t n_kv_heads, int32_t head_dim, int32_t page_tokens,
                                       float scale, void* stream);
 
+/* ------------------------------------------------------- f16 KV caches ----
+ * Decode over f16 caches [n_kv_heads][stride][head_dim] (query head h reads
+ * KV head h / (n_heads / n_kv_heads); scale <= 0 means 1/sqrt(head_dim)).
+ * Split-KV partials go to `workspace` (nyion_attn_f16_workspace_size bytes;
+ * null = library-owned, allocated on first use: not under stream capture).
+ *
+ * nyion_attn_decode_contig_f16: tokens [0, seq_len) of a contiguous half
+ * cache — gpu_attention_streamed_half (fused_attention.cu:534-582) with a
+ * caller workspace.
+ *
+ * nyion_attn_decode_ring_f16: the layer-graph attention node over the f16
+ * ring of `window` slots (kernel_scores_dptr / kernel_softmax_v_dptr,
+ * fused_attention.cu:1505-1556): the length is read from device memory at
+ * run time (*d_seq_len, clamped to [0, window] as scheduler.rs:103-171 does
+ * on the host), so a captured graph replays correctly as it grows. */
+size_t nyion_attn_f16_workspace_size(int32_t n_heads, int32_t max_tokens);
+int32_t nyion_attn_decode_contig_f16(const float* q, const void* k_cache, const void* v_cache,
+                                     float* out, int32_t n_heads, int32_t n_kv_heads,
+                                     int32_t seq_len, int32_t head_dim, int32_t kv_stride,
+                                     float scale, void* workspace, size_t workspace_bytes,
+                                     void* stream);
+int32_t nyion_attn_decode_ring_f16(const float* q, const void* k_ring, const void* v_ring,
+                                   const int32_t* d_seq_len, float* out, int32_t n_heads,
+                                   int32_t n_kv_heads, int32_t head_dim, int32_t window,
+                                   float scale, void* workspace, size_t workspace_bytes,
+                                   void* stream);
+
 /* ---------------------------------------------- reference CUDA C ABI -------
  * Same names, arguments and 0 / -1 results as swamp-gpu/kernels/fused_attention.cu,
  * so the reference's Rust declarations (swamp-gpu/src/lib.rs:586-677) link
@@ -228,10 +255,20 @@ void* gpu_graph_create_attention(const float* d_q, const float* d_k_cache,
                                  const float* d_v_cache, float* d_scores, float* d_output,
                                  int n_heads, int n_kv_heads, int seq_len, int head_dim,
                                  int kv_stride);
-/* fused_attention.cu:669-679 */
+/* fused_attention.cu:669-679 (either kind of graph handle) */
 int gpu_graph_replay_attention(void* graph_handle, void* stream);
-/* fused_attention.cu:682-686 */
+/* fused_attention.cu:682-686 (either kind of graph handle) */
 void gpu_graph_destroy(void* graph_handle);
+/* fused_attention.cu:534-582: f16 K/V cache ([n_kv][kv_stride][head_dim] half;
+ * `void*` here so C callers need no half type) */
+int gpu_attention_streamed_half(const float* d_q, const void* d_k_cache, const void* d_v_cache,
+                                float* d_output, int n_heads, int n_kv_heads, int seq_len,
+                                int head_dim, int kv_stride, void* stream);
+/* fused_attention.cu:687-717 */
+void* gpu_graph_create_attention_half(const float* d_q, const void* d_k_cache,
+                                      const void* d_v_cache, float* d_scores, float* d_output,
+                                      int n_heads, int n_kv_heads, int seq_len, int head_dim,
+                                      int kv_stride);
 
 #ifdef __cplusplus
 }

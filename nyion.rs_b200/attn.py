@@ -65,6 +65,13 @@ def lib() -> C.CDLL:
                                                 C.c_int, C.c_int]),
             "gpu_graph_replay_attention": (C.c_int, [vp, vp]),
             "gpu_graph_destroy": (None, [vp]),
+            "nyion_attn_f16_workspace_size": (sz, [i32, i32]),
+            "nyion_attn_decode_contig_f16": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, f32, vp, sz, vp]),
+            "nyion_attn_decode_ring_f16": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, f32, vp, sz, vp]),
+            "gpu_attention_streamed_half": (C.c_int, [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int,
+                                                      C.c_int, vp]),
+            "gpu_graph_create_attention_half": (vp, [vp, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int,
+                                                     C.c_int, C.c_int]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -269,6 +276,44 @@ def prefill_paged_bf16(q, kv_pool, page_table, q_start: int, out=None, scale: fl
     check(lib().nyion_attn_prefill_paged_bf16(
         _ptr(q), _ptr(kv_pool), kv_pool.shape[0], _ptr(page_table), page_table.numel(), q_start, n_q,
         _ptr(out), H, kv_pool.shape[1], D, kv_pool.shape[3], float(scale), _stream_ptr(stream)))
+    return out
+
+
+class F16Workspace:
+    def __init__(self, n_heads: int, max_tokens: int, device=None):
+        torch = _torch()
+        self.nbytes = int(lib().nyion_attn_f16_workspace_size(n_heads, max_tokens))
+        self.buf = torch.empty(self.nbytes, dtype=torch.uint8, device=device or "cuda")
+
+    def ptr(self) -> int:
+        return int(self.buf.data_ptr())
+
+
+def decode_contig_f16(q, k_cache, v_cache, seq_len: int, out=None, scale: float = 0.0, workspace=None,
+                      stream=None):
+    """q [H, D] f32; k/v_cache [n_kv, stride, D] f16; attends tokens [0, seq_len)."""
+    torch = _torch()
+    H, D = q.shape
+    if out is None:
+        out = torch.empty(H, D, dtype=torch.float32, device=q.device)
+    ws_ptr, ws_bytes = (0, 0) if workspace is None else (workspace.ptr(), workspace.nbytes)
+    check(lib().nyion_attn_decode_contig_f16(_ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(out), H,
+                                             k_cache.shape[0], seq_len, D, k_cache.shape[1], float(scale),
+                                             ws_ptr, ws_bytes, _stream_ptr(stream)))
+    return out
+
+
+def decode_ring_f16(q, k_ring, v_ring, d_seq_len, out=None, scale: float = 0.0, workspace=None,
+                    stream=None):
+    """Layer-graph node: q [H, D] f32; rings [n_kv, window, D] f16; length read on device."""
+    torch = _torch()
+    H, D = q.shape
+    if out is None:
+        out = torch.empty(H, D, dtype=torch.float32, device=q.device)
+    ws_ptr, ws_bytes = (0, 0) if workspace is None else (workspace.ptr(), workspace.nbytes)
+    check(lib().nyion_attn_decode_ring_f16(_ptr(q), _ptr(k_ring), _ptr(v_ring), _ptr(d_seq_len), _ptr(out), H,
+                                           k_ring.shape[0], D, k_ring.shape[1], float(scale), ws_ptr, ws_bytes,
+                                           _stream_ptr(stream)))
     return out
 
 

@@ -847,11 +847,6 @@ done:
   return rc;
 }
 
-struct AttnGraph {
-  cudaGraphExec_t exec;
-  void* ws;
-};
-
 extern "C" void* gpu_graph_create_attention(const float* d_q, const float* d_k_cache,
                                             const float* d_v_cache, float* d_scores,
                                             float* d_output, int n_heads, int n_kv_heads,

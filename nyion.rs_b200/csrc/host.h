@@ -40,4 +40,11 @@ int32_t encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const
 // cudaMemset, so the first call at a given size must not be under capture.
 int32_t internal_workspace(size_t bytes, void** ptr);
 
+// Handle behind gpu_graph_create_attention[_half]: the instantiated graph
+// and the workspace it owns (freed by gpu_graph_destroy).
+struct AttnGraph {
+  cudaGraphExec_t exec;
+  void* ws;
+};
+
 }  // namespace nyion
