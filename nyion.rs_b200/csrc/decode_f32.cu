@@ -602,6 +602,10 @@ WsLayout ws_layout(int batch, int n_kv) {
   w.ml = al(pairs * sizeof(int32_t));
   w.po = w.ml + al(slots * GROUP * sizeof(float2));
   w.total = w.po + al(slots * GROUP * HD * sizeof(float));
+  if (n_kv == 4) {   // the whole-page kernel's layout (decode_pages.cu) is used instead
+    const size_t pw = pages_workspace_bytes(batch);
+    if (pw > w.total) w.total = pw;
+  }
   return w;
 }
 
@@ -720,6 +724,11 @@ extern "C" int32_t nyion_attn_decode_paged_f32(const float* q, const float* kv_p
   } else if (workspace_bytes < need) {
     return fail(NYION_ERR_WORKSPACE, "decode_paged_f32: workspace %zu < %zu bytes", workspace_bytes, need);
   }
+  const float qscale = (scale > 0.f ? scale : 1.0f / sqrtf((float)head_dim)) * 1.4426950408889634f;
+  // 4 KV heads: a page is one 32 KB block, streamed whole (decode_pages.cu)
+  if (n_kv_heads == 4)
+    return launch_pages(q, kv_pool, n_pool_pages, page_table, max_pages, seq_lens, out, batch, qscale,
+                        workspace, static_cast<cudaStream_t>(stream));
   CUtensorMap map;
   st = pool_map(&map, kv_pool, n_pool_pages * n_kv_heads);
   if (st) return st;
@@ -727,7 +736,7 @@ extern "C" int32_t nyion_attn_decode_paged_f32(const float* q, const float* kv_p
   p.n_kv = n_kv_heads;
   p.max_pages = max_pages;
   p.n_pool_pages = n_pool_pages;
-  p.qscale = (scale > 0.f ? scale : 1.0f / sqrtf((float)head_dim)) * 1.4426950408889634f;
+  p.qscale = qscale;
   return launch<kPool>(p, map, map, batch, seq_lens, q, out, page_table, workspace,
                        static_cast<cudaStream_t>(stream));
 }

@@ -40,6 +40,14 @@ int32_t encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const
 // cudaMemset, so the first call at a given size must not be under capture.
 int32_t internal_workspace(size_t bytes, void** ptr);
 
+// Whole-page fp32 paged decode for 4 KV heads (decode_pages.cu): workspace
+// bytes for `batch` sequences, and the launch (workspace zeroed once, left
+// with its counters at zero).
+size_t pages_workspace_bytes(int batch);
+int32_t launch_pages(const float* q, const float* kv_pool, int64_t n_pool_pages, const int32_t* page_table,
+                     int32_t max_pages, const int32_t* seq_lens, float* out, int32_t batch, float qscale,
+                     void* ws, cudaStream_t stream);
+
 // Handle behind gpu_graph_create_attention[_half]: the instantiated graph
 // and the workspace it owns (freed by gpu_graph_destroy).
 struct AttnGraph {
