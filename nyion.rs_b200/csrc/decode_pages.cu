@@ -93,6 +93,10 @@ decode_pages_kernel(const Params p, const __grid_constant__ CUtensorMap map) {
     s.abort_ = 0;
     fence_barrier_init();
   }
+  // programmatic dependent launch: the next grid in the stream may be
+  // scheduled now; nothing global is read before the previous grid completed
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   // ---- sequence lengths and flat page prefix (block scan) ----
   for (int b = t; b < p.batch; b += THREADS) {
@@ -527,8 +531,17 @@ int32_t launch_pages(const float* q, const float* kv_pool, int64_t n_pool_pages,
     p.po = reinterpret_cast<float*>(w + al((size_t)nb * NKV * sizeof(int32_t)) +
                                     al(slots * GROUP * sizeof(float2)));
     p.err = dev->err_word;
-    decode_pages_kernel<<<grid, THREADS, smem, stream>>>(p, map);
-    st = check_cuda(cudaGetLastError(), "decode_pages launch");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    st = check_cuda(cudaLaunchKernelEx(&cfg, decode_pages_kernel, p, map), "decode_pages launch");
     if (st) return st;
   }
   return NYION_OK;
