@@ -17,8 +17,11 @@
 //   * per unit: S = Q K^T and O += P V on mma.sync bf16 with fp32 operands
 //     split hi + lo (all four cross products; ~2^-17 relative residual),
 //     online softmax in the log2 domain;
-//   * per (sequence, KV head) each contributing warp leaves an (m, l, o)
-//     partial; a counter lets the last contributor merge (no inter-CTA wait).
+//   * at each sequence boundary the two parity warps of a KV head fold their
+//     partials in shared memory; a sequence held by one CTA is written there,
+//     otherwise each CTA leaves one (m, l, o) partial and a counter lets the
+//     last CTA's two warps merge them, all loads in flight together (no
+//     inter-CTA wait).
 #include <math.h>
 
 #include "common.cuh"
@@ -49,9 +52,16 @@ struct Params {
   int64_t n_pool_pages;
   float qscale;             // scale * log2(e)
   int32_t* cnt;             // [batch * NKV] merge counters (start at 0, left at 0)
-  float2* ml;               // [(MAX_GRID + batch) * NCW][GROUP] (m, l)
-  float* po;                // [(MAX_GRID + batch) * NCW][GROUP][HD] o relative to m
+  float2* ml;               // [(MAX_GRID + batch) * NKV][GROUP] (m, l) per CTA partial
+  float* po;                // [(MAX_GRID + batch) * NKV][GROUP][HD] o relative to m
   int32_t* err;
+};
+
+// per KV head: the parity-1 warp's partial handed to the parity-0 warp
+struct Xch {
+  float o[GROUP][HD];
+  float2 ml[GROUP];
+  int32_t flag;
 };
 
 struct Smem {
@@ -61,8 +71,13 @@ struct Smem {
   int32_t prefix[MAX_SEQS + 1];      // flat unit index where sequence b starts
   int32_t lens[MAX_SEQS];
   int32_t warp_tot[THREADS / 32];
+  Xch xch[NKV];
   int32_t abort_;
 };
+
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
 
 __device__ __forceinline__ int pages_of(int len) { return (len + PAGE - 1) / PAGE; }
 
@@ -357,108 +372,115 @@ decode_pages_kernel(const Params p, const __grid_constant__ CUtensorMap map) {
     }
 
     i = seg_hi;
-    if (kfirst >= seg_hi - begin) continue;   // no unit of this sequence for this warp
 
-    // ---- publish this warp's partial (plain stores; counted at the end) ----
+    // ---- fold the two parity warps' partials of (b, kvh) in shared memory ----
+    // (a warp without a page of b here contributes l = 0); the parity-0 warp
+    // then writes the result, or publishes one partial per CTA when other
+    // CTAs hold pages of b too
     l += __shfl_xor_sync(0xffffffffu, l, 1);
     l += __shfl_xor_sync(0xffffffffu, l, 2);
-    const int cfirst = pstart / W, clast = (pend - 1) / W;
-    int contributors = 0;   // (CTA, parity) pairs that own at least one page of the sequence
-    for (int c = cfirst; c <= clast; ++c) {
-      const int lo = max(pstart, c * W), hi = min(pend, (c + 1) * W);
-      contributors += min(2, hi - lo);
-    }
-    float* dst = p.out + ((int64_t)b * H + kvh * GROUP) * HD;
-    if (contributors == 1) {
-      const float inv = 1.0f / l;
+    Xch& xc = s.xch[kvh];
+    if (par == 1) {
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt)
-        *reinterpret_cast<float2*>(dst + g * HD + 8 * nt + 2 * tig) =
-            make_float2((o[nt][0] + o[nt][2]) * inv, (o[nt][1] + o[nt][3]) * inv);
-      continue;
+        *reinterpret_cast<float2*>(&xc.o[g][8 * nt + 2 * tig]) =
+            make_float2(o[nt][0] + o[nt][2], o[nt][1] + o[nt][3]);
+      if (tig == 0) xc.ml[g] = make_float2(m, l);
     }
-    const int64_t slot = ((int64_t)blockIdx.x + b) * NCW + warp;
+    named_bar_sync(1 + kvh, 64);
+    if (par == 0) {
+      const float2 ml1 = xc.ml[g];
+      const float M = fmaxf(m, ml1.x);                // finite: one of the two owns a page
+      const float a0 = l > 0.f ? exp2f(m - M) : 0.f, a1 = ml1.y > 0.f ? exp2f(ml1.x - M) : 0.f;
+      const float L = l * a0 + ml1.y * a1;
+      const int cfirst = pstart / W, clast = (pend - 1) / W;
+      if (cfirst == clast) {                          // every page of b is in this CTA
+        const float inv = 1.0f / L;
+        float* dst = p.out + ((int64_t)b * H + kvh * GROUP + g) * HD;
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
-      __stcg(reinterpret_cast<float2*>(p.po + (slot * GROUP + g) * HD + 8 * nt + 2 * tig),
-             make_float2(o[nt][0] + o[nt][2], o[nt][1] + o[nt][3]));
-    if (tig == 0) __stcg(&p.ml[slot * GROUP + g], make_float2(m, l));
+        for (int nt = 0; nt < 8; ++nt) {
+          const float2 o1 = *reinterpret_cast<const float2*>(&xc.o[g][8 * nt + 2 * tig]);
+          *reinterpret_cast<float2*>(dst + 8 * nt + 2 * tig) =
+              make_float2(((o[nt][0] + o[nt][2]) * a0 + o1.x * a1) * inv,
+                          ((o[nt][1] + o[nt][3]) * a0 + o1.y * a1) * inv);
+        }
+      } else {
+        const int64_t slot = ((int64_t)blockIdx.x + b) * NKV + kvh;
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+          const float2 o1 = *reinterpret_cast<const float2*>(&xc.o[g][8 * nt + 2 * tig]);
+          __stcg(reinterpret_cast<float2*>(p.po + (slot * GROUP + g) * HD + 8 * nt + 2 * tig),
+                 make_float2((o[nt][0] + o[nt][2]) * a0 + o1.x * a1, (o[nt][1] + o[nt][3]) * a0 + o1.y * a1));
+        }
+        if (tig == 0) __stcg(&p.ml[slot * GROUP + g], make_float2(M, L));
+      }
+    }
+    named_bar_sync(1 + kvh, 64);                      // the exchange buffer is free again
   }
 
-  // ---- after the last unit: count in, and merge where this warp is last ----
+  // ---- after the last unit: the parity-0 warp of each KV head counts the CTA
+  // in for the (at most two) sequences it shares with other CTAs; where the
+  // CTA is last, both warps of the head merge the CTA partials (heads 4 par ..
+  // 4 par + 3) with every partial's loads in flight together ----
   __threadfence();
-  __syncwarp();
-  for (int i2 = begin; i2 < end;) {
-    const int b = seq_of(s, p.batch, i2);
-    const int pstart = s.prefix[b], pend = s.prefix[b + 1], seg_hi = min(end, pend);
-    const int k0 = i2 - begin;
-    const int kfirst = k0 + ((par - k0) & 1);
-    i2 = seg_hi;
-    if (kfirst >= seg_hi - begin) continue;
+  const int b_first = seq_of(s, p.batch, begin), b_last = seq_of(s, p.batch, end - 1);
+#pragma unroll 1
+  for (int e = 0; e < 2; ++e) {
+    const int b = e == 0 ? b_first : b_last;
+    if (e == 1 && b_last == b_first) break;
+    const int pstart = s.prefix[b], pend = s.prefix[b + 1];
     const int cfirst = pstart / W, clast = (pend - 1) / W;
-    int contributors = 0;
-    for (int c = cfirst; c <= clast; ++c) {
-      const int lo = max(pstart, c * W), hi = min(pend, (c + 1) * W);
-      contributors += min(2, hi - lo);
-    }
-    if (contributors == 1) continue;   // written directly
-    const int pair = b * NKV + kvh;
-    int last = 0;
-    if (lane == 0) {
-      const int old = atomicAdd(&p.cnt[pair], 1);
-      last = (old == contributors - 1);
-      if (last) atomicExch(&p.cnt[pair], 0);
+    if (cfirst == clast) continue;                    // written above
+    if (par == 0 && lane == 0) {
+      const int old = atomicAdd(&p.cnt[b * NKV + kvh], 1);
+      const int last = (old == clast - cfirst);
+      if (last) atomicExch(&p.cnt[b * NKV + kvh], 0);
       __threadfence();
+      s.xch[kvh].flag = last;
     }
-    if (!__shfl_sync(0xffffffffu, last, 0)) continue;
-    float* dst = p.out + ((int64_t)b * H + kvh * GROUP) * HD;
-    // lane -> head lane>>2, dims 16*(lane&3) .. +15; contributors are the
-    // parity warps (kvh, q) of each CTA c in [cfirst, clast] that own a page
-    // of the sequence, folded in one online pass
-    const int mh = lane >> 2, md = 16 * (lane & 3);
+    named_bar_sync(1 + kvh, 64);
+    const int last = s.xch[kvh].flag;
+    named_bar_sync(1 + kvh, 64);
+    if (!last) continue;
+    // lane -> head 4 par + lane / 8, dims 8 (lane % 8) .. +7
+    const int h = 4 * par + (lane >> 3), d = 8 * (lane & 7);
+    constexpr int CB = 6;
     float M = -INFINITY, den = 0.f;
-    float4 acc[4];
+    float acc[8];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) acc[e] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int c = cfirst; c <= clast; ++c) {
-      const int lo = max(pstart, c * W) - c * W, hi = min(pend, (c + 1) * W) - c * W;
-      float2 mlv[2];
-      float4 ov[2][4];
+    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+    for (int cb = cfirst; cb <= clast; cb += CB) {
+      float2 mlv[CB];
+      float4 ov[CB][2];
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const bool has = (hi - lo >= 2) || (u == (lo & 1));   // parity u owns a page here
-        if (has) {
-          const int64_t sl = ((int64_t)c + b) * NCW + u * NKV + kvh;
-          mlv[u] = __ldcg(&p.ml[sl * GROUP + mh]);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) ov[u][e] = ld_cg4(p.po + (sl * GROUP + mh) * HD + md + 4 * e);
+      for (int j = 0; j < CB; ++j) {
+        if (cb + j <= clast) {
+          const int64_t sl = ((int64_t)(cb + j) + b) * NKV + kvh;
+          mlv[j] = __ldcg(&p.ml[sl * GROUP + h]);
+          ov[j][0] = ld_cg4(p.po + (sl * GROUP + h) * HD + d);
+          ov[j][1] = ld_cg4(p.po + (sl * GROUP + h) * HD + d + 4);
         } else {
-          mlv[u] = make_float2(-INFINITY, 0.f);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) ov[u][e] = make_float4(0.f, 0.f, 0.f, 0.f);
+          mlv[j] = make_float2(-INFINITY, 0.f);
+          ov[j][0] = ov[j][1] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
       }
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        if (!(mlv[u].y > 0.f)) continue;
-        const float Mn = fmaxf(M, mlv[u].x);
-        const float sa = exp2f(M - Mn), sbv = exp2f(mlv[u].x - Mn);
-        den = den * sa + mlv[u].y * sbv;
+      for (int j = 0; j < CB; ++j) {
+        if (!(mlv[j].y > 0.f)) continue;
+        const float Mn = fmaxf(M, mlv[j].x);
+        const float sa = exp2f(M - Mn), sbv = exp2f(mlv[j].x - Mn);
+        den = den * sa + mlv[j].y * sbv;
+        const float v[8] = {ov[j][0].x, ov[j][0].y, ov[j][0].z, ov[j][0].w,
+                            ov[j][1].x, ov[j][1].y, ov[j][1].z, ov[j][1].w};
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          acc[e].x = fmaf(acc[e].x, sa, ov[u][e].x * sbv);
-          acc[e].y = fmaf(acc[e].y, sa, ov[u][e].y * sbv);
-          acc[e].z = fmaf(acc[e].z, sa, ov[u][e].z * sbv);
-          acc[e].w = fmaf(acc[e].w, sa, ov[u][e].w * sbv);
-        }
+        for (int q8 = 0; q8 < 8; ++q8) acc[q8] = fmaf(acc[q8], sa, v[q8] * sbv);
         M = Mn;
       }
     }
     const float inv = 1.0f / den;
-#pragma unroll
-    for (int e = 0; e < 4; ++e)
-      *reinterpret_cast<float4*>(dst + mh * HD + md + 4 * e) =
-          make_float4(acc[e].x * inv, acc[e].y * inv, acc[e].z * inv, acc[e].w * inv);
+    float* dst = p.out + ((int64_t)b * H + kvh * GROUP + h) * HD + d;
+    *reinterpret_cast<float4*>(dst) = make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv);
+    *reinterpret_cast<float4*>(dst + 4) = make_float4(acc[4] * inv, acc[5] * inv, acc[6] * inv, acc[7] * inv);
   }
 }
 
@@ -470,7 +492,7 @@ size_t smem_bytes() { return sizeof(Smem) + 1024; }
 
 size_t pages_workspace_bytes(int batch) {
   const size_t b = (size_t)(batch < pages::MAX_SEQS ? batch : pages::MAX_SEQS);
-  const size_t slots = (pages::MAX_GRID + b) * pages::NCW;
+  const size_t slots = (pages::MAX_GRID + b) * pages::NKV;
   auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
   return al(b * pages::NKV * sizeof(int32_t)) + al(slots * pages::GROUP * sizeof(float2)) +
          slots * pages::GROUP * pages::HD * sizeof(float);
@@ -515,7 +537,7 @@ int32_t launch_pages(const float* q, const float* kv_pool, int64_t n_pool_pages,
   auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
   for (int b0 = 0; b0 < batch; b0 += MAX_SEQS) {
     const int nb = batch - b0 < MAX_SEQS ? batch - b0 : MAX_SEQS;
-    const size_t slots = (MAX_GRID + (size_t)nb) * NCW;
+    const size_t slots = (MAX_GRID + (size_t)nb) * NKV;
     Params p{};
     p.q = q + (int64_t)b0 * NKV * GROUP * HD;
     p.out = out + (int64_t)b0 * NKV * GROUP * HD;
