@@ -180,6 +180,38 @@ int32_t nyion_attn_decode_zoned_f32(float* out, const float* q, const float* k_a
                                     int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
                                     void* stream);
 
+/* ---------------------------------- split-KV across GPUs, exchange fused ----
+ * No reference counterpart (the reference has no multi-GPU attention); the
+ * merge is the log-sum-exp identity of attention.mojo:89-96.  One process
+ * per GPU; rank r holds the 4-bit pages of its token range [u_begin, u_end).
+ * Every rank owns a mailbox (nyion_attn_splitkv_mailbox_bytes, allocated and
+ * zeroed by nyion_attn_mailbox_alloc) and opens every other rank's through
+ * CUDA IPC (nyion_attn_ipc_handle gives 64 bytes to send, nyion_attn_ipc_open
+ * maps a received one).  nyion_attn_decode_q4_splitkv then runs the rank's
+ * partial and, in the same reduce kernel, writes each (sequence, head) row's
+ * partial into every rank's mailbox over peer memory as 64-bit words tagged
+ * with the step's epoch, waits (at most timeout_ms; 0 = 2000) until all
+ * ranks' words of the row carry it, and writes the combined attention to
+ * `out` [batch][n_heads][head_dim] on every rank.
+ * `mailboxes` is a host array of `world` device pointers ([rank] = own).
+ * All ranks must call it the same number of times with the same batch;
+ * steps alternate two mailbox halves, so it is graph-replayable.  A wait that
+ * runs out sets NYION_DEVERR_WAIT_TIMEOUT (read with nyion_attn_device_error)
+ * and leaves `out` undefined.  batch <= 512, world <= 8. */
+size_t nyion_attn_splitkv_mailbox_bytes(int32_t batch, int32_t n_heads);
+int32_t nyion_attn_mailbox_alloc(size_t bytes, void** ptr);
+int32_t nyion_attn_mailbox_free(void* ptr);
+int32_t nyion_attn_ipc_handle(void* dev_ptr, void* handle_out /* 64 bytes */);
+int32_t nyion_attn_ipc_open(const void* handle /* 64 bytes */, void** dev_ptr);
+int32_t nyion_attn_ipc_close(void* dev_ptr);
+int32_t nyion_attn_decode_q4_splitkv(const float* q, const uint8_t* kv_pool, int64_t n_pool_pages,
+                                     const int32_t* page_table, int32_t max_pages, int32_t u_begin,
+                                     int32_t u_end, float* out, int32_t batch, int32_t n_heads,
+                                     int32_t n_kv_heads, int32_t head_dim, int32_t page_tokens,
+                                     float scale, void* const* mailboxes, int32_t world, int32_t rank,
+                                     int32_t timeout_ms, void* workspace, size_t workspace_bytes,
+                                     void* stream);
+
 /* ------------------------------------------------ chunked causal prefill ----
  * The attention step of prefill_slice (swamp-engine/src/executor.rs:106-138):
  * for every prompt token t of a chunk the reference calls ops::attention with

@@ -66,6 +66,14 @@ def lib() -> C.CDLL:
             "gpu_graph_replay_attention": (C.c_int, [vp, vp]),
             "gpu_graph_destroy": (None, [vp]),
             "nyion_attn_f16_workspace_size": (sz, [i32, i32]),
+            "nyion_attn_splitkv_mailbox_bytes": (sz, [i32, i32]),
+            "nyion_attn_mailbox_alloc": (i32, [sz, C.POINTER(vp)]),
+            "nyion_attn_mailbox_free": (i32, [vp]),
+            "nyion_attn_ipc_handle": (i32, [vp, C.c_char_p]),
+            "nyion_attn_ipc_open": (i32, [C.c_char_p, C.POINTER(vp)]),
+            "nyion_attn_ipc_close": (i32, [vp]),
+            "nyion_attn_decode_q4_splitkv": (i32, [vp, vp, i64, vp, i32, i32, i32, vp, i32, i32, i32, i32, i32, f32,
+                                                   C.POINTER(vp), i32, i32, i32, vp, sz, vp]),
             "nyion_attn_decode_contig_f16": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, f32, vp, sz, vp]),
             "nyion_attn_decode_ring_f16": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, f32, vp, sz, vp]),
             "gpu_attention_streamed_half": (C.c_int, [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int,
@@ -314,6 +322,55 @@ def decode_ring_f16(q, k_ring, v_ring, d_seq_len, out=None, scale: float = 0.0, 
     check(lib().nyion_attn_decode_ring_f16(_ptr(q), _ptr(k_ring), _ptr(v_ring), _ptr(d_seq_len), _ptr(out), H,
                                            k_ring.shape[0], D, k_ring.shape[1], float(scale), ws_ptr, ws_bytes,
                                            _stream_ptr(stream)))
+    return out
+
+
+class Mailbox:
+    """A split-KV mailbox in device memory (library-allocated so CUDA IPC maps
+    exactly this allocation)."""
+
+    def __init__(self, batch: int, n_heads: int = 32):
+        self.nbytes = int(lib().nyion_attn_splitkv_mailbox_bytes(batch, n_heads))
+        ptr = C.c_void_p()
+        check(lib().nyion_attn_mailbox_alloc(self.nbytes, C.byref(ptr)))
+        self.ptr = ptr.value
+
+    def ipc_handle(self) -> bytes:
+        buf = C.create_string_buffer(64)
+        check(lib().nyion_attn_ipc_handle(C.c_void_p(self.ptr), buf))
+        return buf.raw
+
+    def free(self):
+        if self.ptr:
+            check(lib().nyion_attn_mailbox_free(C.c_void_p(self.ptr)))
+            self.ptr = None
+
+
+def ipc_open(handle: bytes) -> int:
+    ptr = C.c_void_p()
+    check(lib().nyion_attn_ipc_open(handle, C.byref(ptr)))
+    return ptr.value
+
+
+def ipc_close(ptr: int) -> None:
+    check(lib().nyion_attn_ipc_close(C.c_void_p(ptr)))
+
+
+def decode_q4_splitkv(q, kv_pool, page_table, u_begin: int, u_end: int, mailboxes, rank: int, out=None,
+                      scale: float = 0.0, timeout_ms: int = 0, workspace=None, stream=None):
+    """Rank `rank`'s share of a split-KV decode with the exchange fused in:
+    returns the combined attention out [B, H, D] (same on every rank)."""
+    torch = _torch()
+    B, H, D = q.shape
+    if out is None:
+        out = torch.empty(B, H, D, dtype=torch.float32, device=q.device)
+    world = len(mailboxes)
+    arr = (C.c_void_p * world)(*[C.c_void_p(m) for m in mailboxes])
+    ws_ptr, ws_bytes = (0, 0) if workspace is None else (workspace.ptr(), workspace.nbytes)
+    check(lib().nyion_attn_decode_q4_splitkv(
+        _ptr(q), _ptr(kv_pool), kv_pool.shape[0], _ptr(page_table), page_table.shape[1], u_begin, u_end, _ptr(out),
+        B, H, kv_pool.shape[1], D, kv_pool.shape[3], float(scale), arr, world, rank, timeout_ms, ws_ptr, ws_bytes,
+        _stream_ptr(stream)))
     return out
 
 

@@ -24,6 +24,7 @@
 #include <math.h>
 
 #include <mutex>
+#include <string.h>
 
 #include "common.cuh"
 #include "host.h"
@@ -636,11 +637,59 @@ struct RingArgs {
 
 constexpr int RING_MAX = 256;   // ring tokens folded into the reduce (larger rings: error)
 
+// ---- split-KV exchange over peer memory ----------------------------------
+// Every rank owns a mailbox with the same layout.  A rank writes its partial
+// of row r into slot [rank] of EVERY rank's mailbox (stores over NVLink) as
+// 64-bit words: value bits low, the step's epoch high.  An aligned 64-bit
+// store is single-copy atomic, so a reader that sees the epoch in a word sees
+// its value: no fence and no separate flag (the scheme of NCCL's LL
+// protocol).  A reader polls its row's words of every rank until all carry
+// the epoch, then combines.  Each row's epoch is a counter kept by the row's
+// CTA in its own mailbox header; buf = epoch & 1 double-buffers consecutive
+// steps: a rank writes step s+1 only after reading every rank's step-s words,
+// and every rank has read step s-1 before it writes step s.
+constexpr int MAX_RANKS = 8;
+struct Exchange {
+  uint8_t* mbox[MAX_RANKS];   // mailbox of rank r ([rank] = this rank's own)
+  int32_t world, rank, rows;  // world 0: no exchange
+  long long timeout_ns;       // bound on the wait for the other ranks
+};
+__host__ __device__ constexpr size_t mbox_data_off(int rows) {
+  return (size_t(rows) * 4 + 255) & ~size_t(255);          // after the per-row epochs
+}
+__host__ __device__ constexpr size_t mbox_bytes(int rows) {
+  return mbox_data_off(rows) + size_t(2) * MAX_RANKS * rows * (HD + 2) * 8;
+}
+
+__device__ __forceinline__ void st_word(uint64_t* p, float v, uint32_t epoch) {
+  const uint64_t w = ((uint64_t)epoch << 32) | __float_as_uint(v);
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_word(const uint64_t* p) {
+  uint64_t w;
+  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// One CTA per (sequence, query head) row.  The covering CTAs' partials are
+// taken by the 8 warps round-robin with up to RU of them loaded before any is
+// folded (one L2 round trip for up to 8 RU CTAs); the fp32 ring of config 3
+// is folded in; warp 0 combines.  Without an exchange the row is written as
+// the partial format (o/l, m natural, l) or, with `final_out`, o/l alone;
+// with an exchange it is sent to every rank and the ranks' partials of the
+// row are combined into `final_out`.
+constexpr int RU = 20;
 __global__ void __launch_bounds__(256) q4_reduce_kernel(const float* __restrict__ cta_part,
                                                        const int32_t* __restrict__ meta, int batch,
                                                        float* __restrict__ part,
                                                        float* __restrict__ final_out,
-                                                       const RingArgs ra) {
+                                                       const RingArgs ra, const __grid_constant__ Exchange ex,
+                                                       int32_t* err) {
   __shared__ float red[9][HD + 2];
   __shared__ float qs_[HD];
   __shared__ float sc_[RING_MAX];
@@ -652,11 +701,11 @@ __global__ void __launch_bounds__(256) q4_reduce_kernel(const float* __restrict_
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cf = meta[2 * b], cl = meta[2 * b + 1];
   float M = -INFINITY, L = 0.f, o0 = 0.f, o1 = 0.f;
-  for (int c0 = cf + warp; c0 <= cl; c0 += 32) {
-    float2 ml[4], ov[4];
+  for (int cbase = cf; cbase <= cl; cbase += 8 * RU) {
+    float2 ml[RU], ov[RU];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int c = c0 + 8 * u;
+    for (int u = 0; u < RU; ++u) {
+      const int c = cbase + warp + 8 * u;
       if (c <= cl) {
         const float* src = cta_part + ((((int64_t)c + b) * NKV + kvh) * GROUP + hh) * (HD + 2);
         ml[u] = __ldcg(reinterpret_cast<const float2*>(src + HD));
@@ -667,7 +716,7 @@ __global__ void __launch_bounds__(256) q4_reduce_kernel(const float* __restrict_
       }
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < RU; ++u) {
       if (!(ml[u].y > 0.f)) continue;
       const float Mn = fmaxf(M, ml[u].x);
       const float sa = exp2f(M - Mn), sb = exp2f(ml[u].x - Mn);
@@ -743,18 +792,89 @@ __global__ void __launch_bounds__(256) q4_reduce_kernel(const float* __restrict_
     a1 = fmaf(wt, red[w][2 * lane + 1], a1);
   }
   const float inv = den > 0.f ? 1.0f / den : 0.f;
-  if (final_out) {
-    final_out[(int64_t)row * HD + 2 * lane] = a0 * inv;
-    final_out[(int64_t)row * HD + 2 * lane + 1] = a1 * inv;
-  } else {
-    float* dst = part + (int64_t)row * (HD + 2);
-    dst[2 * lane] = a0 * inv;
-    dst[2 * lane + 1] = a1 * inv;
+  const float mnat = den > 0.f ? Mt * 0.6931471805599453f : -INFINITY;   // log2 -> natural units
+  if (ex.world == 0) {
+    if (final_out) {
+      final_out[(int64_t)row * HD + 2 * lane] = a0 * inv;
+      final_out[(int64_t)row * HD + 2 * lane + 1] = a1 * inv;
+    } else {
+      float* dst = part + (int64_t)row * (HD + 2);
+      dst[2 * lane] = a0 * inv;
+      dst[2 * lane + 1] = a1 * inv;
+      if (lane == 0) {
+        dst[HD] = mnat;
+        dst[HD + 1] = den;
+      }
+    }
+    return;
+  }
+
+  // ---- exchange: this rank's row partial to every rank, then combine ----
+  int* epochs = reinterpret_cast<int*>(ex.mbox[ex.rank]);     // [rows] steps done per row
+  uint32_t epoch = 0;
+  if (lane == 0) epoch = (uint32_t)(*reinterpret_cast<volatile int*>(epochs + row)) + 1u;
+  epoch = __shfl_sync(0xffffffffu, epoch, 0);
+  const int buf = epoch & 1;
+  const size_t slot = ((size_t)(buf * MAX_RANKS + ex.rank) * ex.rows + row) * (HD + 2);
+  for (int r = 0; r < ex.world; ++r) {
+    uint64_t* dst = reinterpret_cast<uint64_t*>(ex.mbox[r] + mbox_data_off(ex.rows)) + slot;
+    st_word(dst + 2 * lane, a0 * inv, epoch);
+    st_word(dst + 2 * lane + 1, a1 * inv, epoch);
     if (lane == 0) {
-      dst[HD] = den > 0.f ? Mt * 0.6931471805599453f : -INFINITY;   // log2 -> natural units
-      dst[HD + 1] = den;
+      st_word(dst + HD, mnat, epoch);
+      st_word(dst + HD + 1, den, epoch);
     }
   }
+  // every rank's words of this row, from this rank's own mailbox
+  const uint64_t* box = reinterpret_cast<const uint64_t*>(ex.mbox[ex.rank] + mbox_data_off(ex.rows));
+  float v0[MAX_RANKS], v1[MAX_RANKS], vm[MAX_RANKS], vl[MAX_RANKS];
+  bool ok = true;
+  const unsigned long long t0 = global_ns();
+#pragma unroll
+  for (int r = 0; r < MAX_RANKS; ++r) {
+    v0[r] = v1[r] = 0.f;
+    vm[r] = -INFINITY;
+    vl[r] = 0.f;
+    if (r >= ex.world || !ok) continue;
+    const uint64_t* src = box + ((size_t)(buf * MAX_RANKS + r) * ex.rows + row) * (HD + 2);
+    uint32_t spins = 0;
+    while (true) {
+      const uint64_t w0 = ld_word(src + 2 * lane), w1 = ld_word(src + 2 * lane + 1);
+      const uint64_t wm = ld_word(src + HD), wl = ld_word(src + HD + 1);
+      const bool here = (uint32_t)(w0 >> 32) == epoch && (uint32_t)(w1 >> 32) == epoch &&
+                        (uint32_t)(wm >> 32) == epoch && (uint32_t)(wl >> 32) == epoch;
+      if (__all_sync(0xffffffffu, here)) {
+        v0[r] = __uint_as_float((uint32_t)w0);
+        v1[r] = __uint_as_float((uint32_t)w1);
+        vm[r] = __uint_as_float((uint32_t)wm);
+        vl[r] = __uint_as_float((uint32_t)wl);
+        break;
+      }
+      if (++spins > 32) __nanosleep(64);
+      if ((long long)(global_ns() - t0) > ex.timeout_ns) {
+        ok = false;
+        break;
+      }
+    }
+  }
+  if (!ok && lane == 0) record_error(err, kErrWaitTimeout);
+  float Mr = -INFINITY;
+#pragma unroll
+  for (int r = 0; r < MAX_RANKS; ++r)
+    if (vl[r] > 0.f) Mr = fmaxf(Mr, vm[r]);
+  float dr = 0.f, c0 = 0.f, c1 = 0.f;
+#pragma unroll
+  for (int r = 0; r < MAX_RANKS; ++r) {
+    if (!(vl[r] > 0.f)) continue;
+    const float wt = vl[r] * expf(vm[r] - Mr);
+    dr += wt;
+    c0 = fmaf(wt, v0[r], c0);
+    c1 = fmaf(wt, v1[r], c1);
+  }
+  const float ir = dr > 0.f ? 1.0f / dr : 0.f;
+  final_out[(int64_t)row * HD + 2 * lane] = c0 * ir;
+  final_out[(int64_t)row * HD + 2 * lane + 1] = c1 * ir;
+  if (lane == 0) *reinterpret_cast<volatile int*>(epochs + row) = (int)epoch;
 }
 
 // ============================================================================
@@ -815,7 +935,8 @@ int32_t check_shape(int32_t n_heads, int32_t n_kv_heads, int32_t head_dim) {
 
 int32_t launch_partial(Params base, int batch, const int32_t* tok_begin, const int32_t* tok_end,
                        const float* q, float* part, const int32_t* table, void* ws,
-                       cudaStream_t stream, float* final_out = nullptr, RingArgs ra = RingArgs{}) {
+                       cudaStream_t stream, float* final_out = nullptr, RingArgs ra = RingArgs{},
+                       const Exchange& ex = Exchange{}) {
   DeviceInfo* dev = nullptr;
   int32_t st = device_info(&dev);
   if (st) return st;
@@ -860,7 +981,7 @@ int32_t launch_partial(Params base, int batch, const int32_t* tok_begin, const i
     p.seq_lens = base.seq_lens ? base.seq_lens + b0 : nullptr;
     q4_reduce_kernel<<<nb * NKV * GROUP, 256, 0, stream>>>(p.cta_part, p.meta, nb, p.part,
                                                             final_out ? final_out + (int64_t)b0 * NKV * GROUP * HD : nullptr,
-                                                            r);
+                                                            r, ex, dev->err_word);
     st = check_cuda(cudaGetLastError(), "q4_reduce launch");
     if (st) return st;
   }
@@ -994,3 +1115,95 @@ extern "C" int32_t nyion_attn_decode_q4_window_ring(
   return launch_partial(p, batch, nullptr, nullptr, q, parts, page_table, w, s, out, ra);
 }
 
+
+// ---- split-KV decode with the exchange fused into the reduce ---------------
+
+extern "C" size_t nyion_attn_splitkv_mailbox_bytes(int32_t batch, int32_t n_heads) {
+  if (batch <= 0 || n_heads <= 0) return 0;
+  return q4::mbox_bytes(batch * n_heads);
+}
+
+extern "C" int32_t nyion_attn_mailbox_alloc(size_t bytes, void** ptr) {
+  if (!ptr || bytes == 0) return fail(NYION_ERR_INVALID, "mailbox_alloc: bad arguments");
+  *ptr = nullptr;
+  int32_t st = check_cuda(cudaMalloc(ptr, bytes), "cudaMalloc(mailbox)");
+  if (st) return st;
+  st = check_cuda(cudaMemset(*ptr, 0, bytes), "cudaMemset(mailbox)");
+  if (st) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+  }
+  return st;
+}
+
+extern "C" int32_t nyion_attn_mailbox_free(void* ptr) {
+  return check_cuda(cudaFree(ptr), "cudaFree(mailbox)");
+}
+
+extern "C" int32_t nyion_attn_ipc_handle(void* dev_ptr, void* handle_out) {
+  if (!dev_ptr || !handle_out) return fail(NYION_ERR_INVALID, "ipc_handle: null pointer");
+  cudaIpcMemHandle_t h;
+  int32_t st = check_cuda(cudaIpcGetMemHandle(&h, dev_ptr), "cudaIpcGetMemHandle");
+  if (st) return st;
+  memcpy(handle_out, &h, sizeof(h));
+  return NYION_OK;
+}
+
+extern "C" int32_t nyion_attn_ipc_open(const void* handle, void** dev_ptr) {
+  if (!handle || !dev_ptr) return fail(NYION_ERR_INVALID, "ipc_open: null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  return check_cuda(cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+}
+
+extern "C" int32_t nyion_attn_ipc_close(void* dev_ptr) {
+  return check_cuda(cudaIpcCloseMemHandle(dev_ptr), "cudaIpcCloseMemHandle");
+}
+
+extern "C" int32_t nyion_attn_decode_q4_splitkv(
+    const float* q, const uint8_t* kv_pool, int64_t n_pool_pages, const int32_t* page_table,
+    int32_t max_pages, int32_t u_begin, int32_t u_end, float* out, int32_t batch, int32_t n_heads,
+    int32_t n_kv_heads, int32_t head_dim, int32_t page_tokens, float scale, void* const* mailboxes,
+    int32_t world, int32_t rank, int32_t timeout_ms, void* workspace, size_t workspace_bytes,
+    void* stream) {
+  int32_t st = check_shape(n_heads, n_kv_heads, head_dim);
+  if (st) return st;
+  if (!q || !kv_pool || !page_table || !out || !mailboxes)
+    return fail(NYION_ERR_INVALID, "decode_q4_splitkv: null pointer argument");
+  if (page_tokens != PAGE) return fail(NYION_ERR_UNSUPPORTED, "decode_q4_splitkv: page_tokens must be 16");
+  if (batch <= 0 || batch > MAX_SEQS || max_pages <= 0 || n_pool_pages <= 0)
+    return fail(NYION_ERR_INVALID, "decode_q4_splitkv: batch must be in [1, %d]; max_pages, n_pool_pages > 0",
+                MAX_SEQS);
+  if (world < 1 || world > MAX_RANKS || rank < 0 || rank >= world)
+    return fail(NYION_ERR_INVALID, "decode_q4_splitkv: rank %d of world %d (at most %d ranks)", rank, world,
+                MAX_RANKS);
+  if (reinterpret_cast<uintptr_t>(kv_pool) % 16)
+    return fail(NYION_ERR_INVALID, "decode_q4_splitkv: kv_pool must be 16-byte aligned");
+  Exchange ex{};
+  for (int r = 0; r < world; ++r) {
+    if (!mailboxes[r]) return fail(NYION_ERR_INVALID, "decode_q4_splitkv: mailbox of rank %d is null", r);
+    ex.mbox[r] = static_cast<uint8_t*>(mailboxes[r]);
+  }
+  ex.world = world;
+  ex.rank = rank;
+  ex.rows = batch * n_heads;
+  ex.timeout_ns = (long long)(timeout_ms > 0 ? timeout_ms : 2000) * 1000000LL;
+  const size_t need = ws_layout(batch).total;
+  if (!workspace) {
+    st = internal_workspace(need, &workspace);
+    if (st) return st;
+  } else if (workspace_bytes < need) {
+    return fail(NYION_ERR_WORKSPACE, "decode_q4_splitkv: workspace %zu < %zu", workspace_bytes, need);
+  }
+  Params p{};
+  p.pool = kv_pool;
+  p.u_begin = u_begin;
+  p.u_end = u_end;
+  p.max_pages = max_pages;
+  p.n_pool_pages = n_pool_pages;
+  p.qscale = (scale > 0.f ? scale : 1.0f / sqrtf((float)head_dim)) * 1.4426950408889634f;
+  // the partial buffer is not written in exchange mode; the CTA partials go
+  // to the workspace and the combined rows to `out`
+  return launch_partial(p, batch, nullptr, nullptr, q, out, page_table, workspace,
+                        static_cast<cudaStream_t>(stream), out, RingArgs{}, ex);
+}
