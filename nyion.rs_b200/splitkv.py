@@ -104,10 +104,14 @@ class SplitKVDecoder:
             return A.decode_q4_splitkv(q, pool, page_table, self.lo, self.hi, self._peers, self.rank,
                                        out=self._out, timeout_ms=self.timeout_ms, workspace=self._ws,
                                        stream=stream)
+        import contextlib
+        import torch
         A.decode_q4_partial(q, pool, page_table, u_begin=self.lo, u_end=self.hi, part=self._part,
                             workspace=self._ws, stream=stream)
-        parts = exchange(self._part, self.group)
-        return A.lse_combine(parts, out=self._out, stream=stream)
+        # the collective runs on torch's current stream: make it the caller's
+        with torch.cuda.stream(stream) if stream is not None else contextlib.nullcontext():
+            parts = exchange(self._part, self.group)
+            return A.lse_combine(parts, out=self._out, stream=stream)
 
     def close(self):
         """Unmap the peers' mailboxes and free this rank's (every rank calls it
