@@ -261,6 +261,31 @@ int32_t nyion_attn_decode_ring_f16(const float* q, const void* k_ring, const voi
                                    float scale, void* workspace, size_t workspace_bytes,
                                    void* stream);
 
+/* ------------------------------------------------ swamp-kernels C ABIs ----
+ * Q16.16 softmax (swamp-kernels/src/lib.rs:97-223), bit-exact with the
+ * reference's AVX-512 path: logits -> Q16.16 at temperature T, exp in fixed
+ * point, sum, normalisation (16-wide blocks with the 32-bit wrapping multiply,
+ * tail with the 64-bit one).  Silent on null pointers or n <= 0, like the
+ * reference.  nyion_attn_softmax_padic takes device pointers and a stream;
+ * mojo_softmax_padic has the reference's name and host pointers
+ * (synchronous). */
+int32_t nyion_attn_softmax_padic(const float* logits, float* probs, int32_t n, float temperature,
+                                 void* stream);
+void mojo_softmax_padic(const float* logits, float* probs, int n, float temperature);
+
+/* Stokes KV store (lib.rs:27-85), same names and arguments: keys / values of
+ * head_dim floats per appended token (host pointers), a score per token;
+ * above 4096 tokens the first minimum-score token is removed and the order of
+ * the rest kept.  The rows live in HBM (nyion_attn_stokes_view returns device
+ * pointers [n][head_dim] for the decode entry points); a NaN score, where the
+ * reference panics, skips the eviction and records an error.  Not
+ * thread-safe, like the reference. */
+void* mojo_stokes_init(int head_dim);
+void mojo_stokes_append(void* cache, int token_id, const float* key, const float* value, float score);
+void mojo_stokes_free(void* cache);
+int32_t nyion_attn_stokes_view(void* cache, const float** keys, const float** values, int32_t* n,
+                               int32_t* head_dim);
+
 /* ---------------------------------------------- reference CUDA C ABI -------
  * Same names, arguments and 0 / -1 results as swamp-gpu/kernels/fused_attention.cu,
  * so the reference's Rust declarations (swamp-gpu/src/lib.rs:586-677) link

@@ -66,6 +66,12 @@ def lib() -> C.CDLL:
             "gpu_graph_replay_attention": (C.c_int, [vp, vp]),
             "gpu_graph_destroy": (None, [vp]),
             "nyion_attn_f16_workspace_size": (sz, [i32, i32]),
+            "nyion_attn_softmax_padic": (i32, [vp, vp, i32, f32, vp]),
+            "mojo_softmax_padic": (None, [vp, vp, C.c_int, f32]),
+            "mojo_stokes_init": (vp, [C.c_int]),
+            "mojo_stokes_append": (None, [vp, C.c_int, vp, vp, f32]),
+            "mojo_stokes_free": (None, [vp]),
+            "nyion_attn_stokes_view": (i32, [vp, C.POINTER(vp), C.POINTER(vp), C.POINTER(i32), C.POINTER(i32)]),
             "nyion_attn_splitkv_mailbox_bytes": (sz, [i32, i32]),
             "nyion_attn_mailbox_alloc": (i32, [sz, C.POINTER(vp)]),
             "nyion_attn_mailbox_free": (i32, [vp]),
@@ -372,6 +378,43 @@ def decode_q4_splitkv(q, kv_pool, page_table, u_begin: int, u_end: int, mailboxe
         B, H, kv_pool.shape[1], D, kv_pool.shape[3], float(scale), arr, world, rank, timeout_ms, ws_ptr, ws_bytes,
         _stream_ptr(stream)))
     return out
+
+
+def softmax_padic(logits, temperature: float = 1.0, out=None, stream=None):
+    """Q16.16 softmax of a device f32 vector (nyion_attn_softmax_padic)."""
+    torch = _torch()
+    if out is None:
+        out = torch.empty_like(logits)
+    check(lib().nyion_attn_softmax_padic(_ptr(logits), _ptr(out), logits.numel(), float(temperature),
+                                         _stream_ptr(stream)))
+    return out
+
+
+class StokesStore:
+    """The reference's Stokes KV store, rows in HBM (mojo_stokes_*)."""
+
+    def __init__(self, head_dim: int):
+        self.hd = head_dim
+        self.h = lib().mojo_stokes_init(head_dim)
+        if not self.h:
+            raise NyionError(-1, last_error())
+
+    def append(self, token_id: int, key, value, score: float) -> None:
+        import numpy as np
+        k = np.ascontiguousarray(key, dtype=np.float32)
+        v = np.ascontiguousarray(value, dtype=np.float32)
+        lib().mojo_stokes_append(self.h, token_id, k.ctypes.data, v.ctypes.data, float(score))
+
+    def view(self):
+        """(keys, values) device pointers, token count."""
+        k, v, n, hd = C.c_void_p(), C.c_void_p(), C.c_int32(), C.c_int32()
+        check(lib().nyion_attn_stokes_view(self.h, C.byref(k), C.byref(v), C.byref(n), C.byref(hd)))
+        return k.value, v.value, n.value
+
+    def close(self):
+        if self.h:
+            lib().mojo_stokes_free(self.h)
+            self.h = None
 
 
 def device_error(stream=None) -> int:
