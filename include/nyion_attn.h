@@ -53,6 +53,8 @@ int32_t nyion_attn_device_error(void* stream, int32_t* bits);
  * sequences of `n_kv_heads` KV heads (split-KV partials + per-(seq, kv head)
  * counters).  The counters must start at zero: allocate, then call
  * nyion_attn_workspace_reset once; the kernels leave them at zero again.
+ * The counters sit in a block of fixed size for a given n_kv_heads, so one
+ * workspace serves every batch size up to the one it was sized for.
  * Calls that share one workspace must not overlap on the GPU. */
 size_t nyion_attn_decode_workspace_size(int32_t batch, int32_t n_kv_heads, int32_t n_heads,
                                         int32_t head_dim);
@@ -163,6 +165,47 @@ int32_t nyion_attn_decode_q4_window_ring(const float* q, const uint8_t* kv_pool,
                                          int32_t n_kv_heads, int32_t head_dim, int32_t page_tokens,
                                          float scale, void* workspace, size_t workspace_bytes,
                                          void* stream);
+
+/* ------------------------------------------------ position-list decode -----
+ * Attention over an explicit list of token positions per sequence, the
+ * position-set form of ops::attention_sparse (swamp-engine/src/ops.rs:85-168)
+ * and ops::attention_fugu (ops.rs:445-541; window, sentinel and DSPark
+ * positions concatenated): scores of q against K[pos] for every listed
+ * position (duplicates count twice, as in the reference's loops), softmax over
+ * the set, weighted sum of V[pos].
+ *   kv_format 0: kv_pool f32 [n_pool_pages][n_kv][K|V][16][head_dim]
+ *   kv_format 1: kv_pool Q4  [n_pool_pages][n_kv][K|V][16][2 blocks x 20 B]
+ *   positions [batch][max_positions], n_positions [batch] (device arrays):
+ *   sequence b uses positions[b][0 .. n_positions[b]); an empty set gives 0.
+ *   out [batch][n_heads][head_dim].
+ * A position whose page entry is outside [0, n_pool_pages) is skipped and
+ * raises the page-range bit of the device error word.
+ * workspace: nyion_attn_positions_workspace_size(batch, n_heads,
+ * max_positions) bytes, or NULL.  This build: head_dim 64, GQA group 8. */
+size_t nyion_attn_positions_workspace_size(int32_t batch, int32_t n_heads, int32_t max_positions);
+int32_t nyion_attn_decode_positions(const float* q, const void* kv_pool, int32_t kv_format,
+                                    int64_t n_pool_pages, const int32_t* page_table,
+                                    int32_t max_pages, const int32_t* positions,
+                                    const int32_t* n_positions, int32_t max_positions, float* out,
+                                    int32_t batch, int32_t n_heads, int32_t n_kv_heads,
+                                    int32_t head_dim, int32_t page_tokens, float scale,
+                                    void* workspace, size_t workspace_bytes, void* stream);
+/* ops::attention_sparse_q4 (swamp-engine/src/ops.rs:597-723) on 4-bit pages:
+ * with valid_end = seq_lens[b] - 1 (the reference's min(q_pos, seq_len - 1)),
+ * window_start = valid_end - window + 1 when valid_end > window, else 0, the
+ * position set is { global_stride * gi : gi < min(window_start /
+ * global_stride, 128) } followed by [window_start, valid_end].  The window
+ * runs on the Q4 page kernel (nyion_attn_decode_q4_partial), the global
+ * positions on the position kernel, and the two partials are merged by the
+ * log-sum-exp combine.  Nibbles in the writer's order (cache.rs:637-663).
+ * workspace: nyion_attn_sparse_q4_workspace_size(batch, n_heads) or NULL. */
+size_t nyion_attn_sparse_q4_workspace_size(int32_t batch, int32_t n_heads);
+int32_t nyion_attn_sparse_q4(const float* q, const uint8_t* kv_pool, int64_t n_pool_pages,
+                             const int32_t* page_table, int32_t max_pages, const int32_t* seq_lens,
+                             int32_t window, int32_t global_stride, float* out, int32_t batch,
+                             int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                             int32_t page_tokens, float scale, void* workspace,
+                             size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------- reference-layout fp32 decode ----
  * ops::attention (swamp-engine/src/ops.rs:170-278) with the same argument

@@ -66,6 +66,12 @@ def lib() -> C.CDLL:
             "gpu_graph_replay_attention": (C.c_int, [vp, vp]),
             "gpu_graph_destroy": (None, [vp]),
             "nyion_attn_f16_workspace_size": (sz, [i32, i32]),
+            "nyion_attn_positions_workspace_size": (sz, [i32, i32, i32]),
+            "nyion_attn_decode_positions": (i32, [vp, vp, i32, i64, vp, i32, vp, vp, i32, vp, i32, i32, i32, i32,
+                                                  i32, f32, vp, sz, vp]),
+            "nyion_attn_sparse_q4_workspace_size": (sz, [i32, i32]),
+            "nyion_attn_sparse_q4": (i32, [vp, vp, i64, vp, i32, vp, i32, i32, vp, i32, i32, i32, i32, i32, f32,
+                                           vp, sz, vp]),
             "nyion_attn_softmax_padic": (i32, [vp, vp, i32, f32, vp]),
             "mojo_softmax_padic": (None, [vp, vp, C.c_int, f32]),
             "mojo_stokes_init": (vp, [C.c_int]),
@@ -274,6 +280,60 @@ def decode_q4_window_ring(q, kv_pool, page_table, seq_lens, ring, window: int, o
 
 def window_ring_workspace(batch: int, n_heads: int = 32, head_dim: int = 64, device=None):
     return Q4Workspace(batch, extra=2 * batch * n_heads * (head_dim + 2) * 4 + 8 * batch + 256, device=device)
+
+
+class RawWorkspace:
+    """A zeroed device buffer of `nbytes` for the entries that take one."""
+
+    def __init__(self, nbytes: int, device=None):
+        torch = _torch()
+        self.nbytes = int(nbytes)
+        self.buf = torch.zeros(max(self.nbytes, 1), dtype=torch.uint8, device=device or "cuda")
+
+    def ptr(self) -> int:
+        return int(self.buf.data_ptr())
+
+
+def decode_positions(q, kv_pool, page_table, positions, n_positions, out=None, scale: float = 0.0,
+                     workspace=None, stream=None):
+    """Attention over explicit per-sequence position lists (ops::attention_sparse /
+    attention_fugu's position sets).  kv_pool is f32 [P, n_kv, 2, 16, D] or
+    Q4 uint8 [P, n_kv, 2, 16, 40]; positions int32 [B, max_positions]."""
+    torch = _torch()
+    B, H, D = q.shape
+    if out is None:
+        out = torch.empty_like(q)
+    fmt = 1 if kv_pool.dtype == torch.uint8 else 0
+    ws_ptr, ws_bytes = (0, 0) if workspace is None else (workspace.ptr(), workspace.nbytes)
+    check(lib().nyion_attn_decode_positions(
+        _ptr(q), _ptr(kv_pool), fmt, kv_pool.shape[0], _ptr(page_table), page_table.shape[1],
+        _ptr(positions), _ptr(n_positions), positions.shape[1], _ptr(out), B, H, kv_pool.shape[1], D,
+        kv_pool.shape[3], float(scale), ws_ptr, ws_bytes, _stream_ptr(stream)))
+    return out
+
+
+def positions_workspace(batch: int, n_heads: int, max_positions: int, device=None):
+    return RawWorkspace(lib().nyion_attn_positions_workspace_size(batch, n_heads, max_positions), device)
+
+
+def sparse_q4(q, kv_pool, page_table, seq_lens, window: int, global_stride: int, out=None,
+              scale: float = 0.0, workspace=None, stream=None):
+    """ops::attention_sparse_q4 on Q4 pages: window + every global_stride-th older token
+    (at most 128); seq_lens[b] = min(q_pos, seq_len - 1) + 1."""
+    torch = _torch()
+    B, H, D = q.shape
+    if out is None:
+        out = torch.empty_like(q)
+    ws_ptr, ws_bytes = (0, 0) if workspace is None else (workspace.ptr(), workspace.nbytes)
+    check(lib().nyion_attn_sparse_q4(
+        _ptr(q), _ptr(kv_pool), kv_pool.shape[0], _ptr(page_table), page_table.shape[1], _ptr(seq_lens),
+        int(window), int(global_stride), _ptr(out), B, H, kv_pool.shape[1], D, kv_pool.shape[3],
+        float(scale), ws_ptr, ws_bytes, _stream_ptr(stream)))
+    return out
+
+
+def sparse_q4_workspace(batch: int, n_heads: int = 32, device=None):
+    return RawWorkspace(lib().nyion_attn_sparse_q4_workspace_size(batch, n_heads), device)
 
 
 def prefill_paged_bf16(q, kv_pool, page_table, q_start: int, out=None, scale: float = 0.0,

@@ -599,7 +599,7 @@ WsLayout ws_layout(int batch, int n_kv) {
   auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
   WsLayout w;
   w.cnt = 0;
-  w.ml = al(pairs * sizeof(int32_t));
+  w.ml = al((size_t)MAX_SEQS * n_kv * sizeof(int32_t));   // counters: fixed size, see pages_workspace_bytes
   w.po = w.ml + al(slots * GROUP * sizeof(float2));
   w.total = w.po + al(slots * GROUP * HD * sizeof(float));
   if (n_kv == 4) {   // the whole-page kernel's layout (decode_pages.cu) is used instead
@@ -719,7 +719,8 @@ extern "C" int32_t nyion_attn_decode_paged_f32(const float* q, const float* kv_p
                 (long long)n_pool_pages);
   size_t need = ws_layout(batch, n_kv_heads).total;
   if (!workspace) {
-    st = internal_workspace(need, &workspace);
+    st = internal_workspace(need, &workspace, kWsCounters, ws_layout(batch, n_kv_heads).ml,
+                            static_cast<cudaStream_t>(stream));
     if (st) return st;
   } else if (workspace_bytes < need) {
     return fail(NYION_ERR_WORKSPACE, "decode_paged_f32: workspace %zu < %zu bytes", workspace_bytes, need);
@@ -770,7 +771,8 @@ extern "C" int32_t nyion_attn_decode_zoned_f32(float* out, const float* q, const
   st = rows_map(&mv, v_arena, rows);
   if (st) return st;
   void* ws = nullptr;
-  st = internal_workspace(ws_layout(1, n_kv_heads).total, &ws);
+  st = internal_workspace(ws_layout(1, n_kv_heads).total, &ws, kWsCounters, ws_layout(1, n_kv_heads).ml,
+                          static_cast<cudaStream_t>(stream));
   if (st) return st;
   Params p{};
   p.n_kv = n_kv_heads;
@@ -799,7 +801,8 @@ static int32_t contig_decode(const float* d_q, const float* d_k, const float* d_
   st = rows_map(&mv, d_v, rows);
   if (st) return st;
   if (!ws) {
-    st = internal_workspace(ws_layout(1, n_kv_heads).total, &ws);
+    st = internal_workspace(ws_layout(1, n_kv_heads).total, &ws, kWsCounters, ws_layout(1, n_kv_heads).ml,
+                            stream);
     if (st) return st;
   }
   Params p{};

@@ -494,7 +494,10 @@ size_t pages_workspace_bytes(int batch) {
   const size_t b = (size_t)(batch < pages::MAX_SEQS ? batch : pages::MAX_SEQS);
   const size_t slots = (pages::MAX_GRID + b) * pages::NKV;
   auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
-  return al(b * pages::NKV * sizeof(int32_t)) + al(slots * pages::GROUP * sizeof(float2)) +
+  // the counter block is sized for MAX_SEQS sequences whatever the batch, so
+  // that calls of different batch sizes sharing a workspace (and the chunks
+  // of a batch above MAX_SEQS) keep their counters in the same bytes
+  return al((size_t)pages::MAX_SEQS * pages::NKV * sizeof(int32_t)) + al(slots * pages::GROUP * sizeof(float2)) +
          slots * pages::GROUP * pages::HD * sizeof(float);
 }
 
@@ -549,8 +552,8 @@ int32_t launch_pages(const float* q, const float* kv_pool, int64_t n_pool_pages,
     p.qscale = qscale;
     uint8_t* w = static_cast<uint8_t*>(ws);
     p.cnt = reinterpret_cast<int32_t*>(w);
-    p.ml = reinterpret_cast<float2*>(w + al((size_t)nb * NKV * sizeof(int32_t)));
-    p.po = reinterpret_cast<float*>(w + al((size_t)nb * NKV * sizeof(int32_t)) +
+    p.ml = reinterpret_cast<float2*>(w + al((size_t)MAX_SEQS * NKV * sizeof(int32_t)));
+    p.po = reinterpret_cast<float*>(w + al((size_t)MAX_SEQS * NKV * sizeof(int32_t)) +
                                     al(slots * GROUP * sizeof(float2)));
     p.err = dev->err_word;
     cudaLaunchConfig_t cfg = {};

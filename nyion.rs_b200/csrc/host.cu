@@ -124,19 +124,21 @@ int32_t encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const
 }
 
 struct Workspace {
-  int device = -1;
   void* ptr = nullptr;
   size_t bytes = 0;
+  size_t clean = 0;   // leading bytes known to be zero (the last call's counters)
 };
-static std::vector<Workspace> g_ws;
+static std::vector<Workspace> g_ws;   // [device * kWsKinds + kind]
 
-int32_t internal_workspace(size_t bytes, void** ptr) {
+int32_t internal_workspace(size_t bytes, void** ptr, WsKind kind, size_t zero_prefix, cudaStream_t stream) {
   int dev = -1;
   int32_t st = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
   if (st) return st;
   std::lock_guard<std::mutex> lk(g_dev_mu);
-  if ((int)g_ws.size() <= dev) g_ws.resize(dev + 1);
-  Workspace& w = g_ws[dev];
+  const size_t slot = (size_t)dev * kWsKinds + kind;
+  if (g_ws.size() <= slot) g_ws.resize(slot + 1);
+  Workspace& w = g_ws[slot];
+  if (zero_prefix > bytes) bytes = zero_prefix;
   if (w.bytes < bytes) {
     if (w.ptr) {
       cudaDeviceSynchronize();
@@ -149,7 +151,13 @@ int32_t internal_workspace(size_t bytes, void** ptr) {
     st = check_cuda(cudaMemset(w.ptr, 0, bytes), "cudaMemset(workspace)");
     if (st) return st;
     w.bytes = bytes;
+    w.clean = bytes;
   }
+  if (zero_prefix > w.clean) {
+    st = check_cuda(cudaMemsetAsync(w.ptr, 0, zero_prefix, stream), "clear workspace counters");
+    if (st) return st;
+  }
+  w.clean = zero_prefix;
   *ptr = w.ptr;
   return NYION_OK;
 }

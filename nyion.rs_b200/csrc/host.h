@@ -35,10 +35,18 @@ int32_t encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const
                     const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
                     CUtensorMapSwizzle swizzle);
 
-// Internal workspace for entry points whose reference signature carries none
-// (gpu_attention_device and friends).  Grown with cudaMalloc and zeroed with
-// cudaMemset, so the first call at a given size must not be under capture.
-int32_t internal_workspace(size_t bytes, void** ptr);
+// Internal workspace for entry points called without one (and those whose
+// reference signature carries none: gpu_attention_device and friends).  One
+// buffer per device and kind: kWsCounters for the kernels that keep merge
+// counters at the start of their workspace (they must read zero there; the
+// kernels leave them at zero), kWsScratch for the others, whose partials
+// would otherwise land on those counters.  `zero_prefix` = the counter bytes
+// of this call: when more than the previous call's on that buffer, they are
+// cleared on `stream` first.  Grown with cudaMalloc and zeroed with cudaMemset,
+// so the first call at a given size must not be under capture.
+enum WsKind { kWsScratch = 0, kWsCounters = 1, kWsKinds = 2 };
+int32_t internal_workspace(size_t bytes, void** ptr, WsKind kind = kWsScratch, size_t zero_prefix = 0,
+                           cudaStream_t stream = nullptr);
 
 // Whole-page fp32 paged decode for 4 KV heads (decode_pages.cu): workspace
 // bytes for `batch` sequences, and the launch (workspace zeroed once, left
