@@ -329,6 +329,56 @@ void mojo_stokes_free(void* cache);
 int32_t nyion_attn_stokes_view(void* cache, const float** keys, const float** values, int32_t* n,
                                int32_t* head_dim);
 
+/* ------------------------------------------------------- KV write path ----
+ * The step before attention: RoPE on the new token's q and k, then K and V
+ * saved into the caches, in one launch.
+ * RoPE follows the CPU engine (swamp-engine/src/ops.rs:20-84): table
+ * [max_context][head_dim/2] of (cos, sin), freq = 1 / 10000^(2k/head_dim),
+ * angle = pos * freq; pair (2k, 2k+1) -> (x cos - y sin, x sin + y cos);
+ * position clamped to max_context - 1.  nyion_attn_rope_table builds the
+ * table on the host with the C library's powf / cosf / sinf (what Rust's f32
+ * methods call) and uploads it to `table` (nyion_attn_rope_table_bytes),
+ * synchronously; rotated vectors are then bit-identical to apply_rope_ufc's. */
+size_t nyion_attn_rope_table_bytes(int32_t head_dim, int32_t max_context);
+int32_t nyion_attn_rope_table(float* table, int32_t head_dim, int32_t max_context, void* stream);
+/* Rows = new tokens (a decode batch, or the tokens of a prefill chunk).
+ *   q  [rows][n_heads][head_dim] f32, rotated in place (NULL: no q);
+ *   k  [rows][n_kv_heads][head_dim] f32, rotated in place; v likewise, read;
+ *   positions [rows] absolute positions; row_seq [rows] the sequence (page
+ *   table row, ring row) of each row, NULL = row i is sequence i;
+ *   rope_table NULL = no rotation (a plain save).
+ * Destinations, each optional (NULL skips it), all at position pos of the
+ * row's sequence, page = page_table[seq][pos / 16], slot = pos % 16:
+ *   pool_q4   [n_pool_pages][n_kv][K|V][16][2 x 20 B]: PagedKVCache::save's
+ *             4-bit blocks of a fresh slot (cache.rs:637-663), bit-exact;
+ *   pool_f32  [n_pool_pages][n_kv][K|V][16][head_dim] f32 (save's f32 copy,
+ *             cache.rs:671-677);
+ *   pool_bf16 same layout in bf16 (RNE), the chunked prefill's cache;
+ *   q_bf16    [rows][n_heads][head_dim] bf16 copy of the rotated q;
+ *   ring_f32  [n_seq][n_kv][K|V][ring_tokens][head_dim] at pos % ring_tokens
+ *             (the windowed 4-bit decode's fp32 ring).
+ * A row whose page is missing (pos outside the table, id outside the pool)
+ * writes no page and raises the page-range device error bit.  This build:
+ * head_dim 64, n_kv_heads <= 16. */
+int32_t nyion_attn_kv_write_paged(float* q, float* k, const float* v, const int32_t* positions,
+                                  const int32_t* row_seq, int32_t rows, int32_t n_heads,
+                                  int32_t n_kv_heads, int32_t head_dim, const float* rope_table,
+                                  int32_t max_context, const int32_t* page_table,
+                                  int32_t max_pages, int64_t n_pool_pages, uint8_t* pool_q4,
+                                  float* pool_f32, void* pool_bf16, void* q_bf16,
+                                  float* ring_f32, int32_t ring_tokens, void* stream);
+/* Layer-graph steps RoPE + KV save (swamp-gpu/kernels/fused_attention.cu:
+ * 1438-1472, 1619-1625) for one sequence, graph-capturable: pos =
+ * *d_seq_len - 1 read on the device, slot = *d_wpos (or pos % window when
+ * d_wpos is NULL); k_ring / v_ring [n_kv][window][head_dim] f16 (RNE).  RoPE
+ * as above (the CPU engine's table; the reference's CUDA kernel evaluates
+ * powf / cosf / sinf under --use_fast_math instead). */
+int32_t nyion_attn_kv_write_ring_f16(float* q, float* k, const float* v, const int32_t* d_seq_len,
+                                     const int32_t* d_wpos, void* k_ring, void* v_ring,
+                                     int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                                     int32_t window, const float* rope_table, int32_t max_context,
+                                     void* stream);
+
 /* ---------------------------------------------- reference CUDA C ABI -------
  * Same names, arguments and 0 / -1 results as swamp-gpu/kernels/fused_attention.cu,
  * so the reference's Rust declarations (swamp-gpu/src/lib.rs:586-677) link
@@ -364,6 +414,24 @@ void gpu_graph_destroy(void* graph_handle);
 int gpu_attention_streamed_half(const float* d_q, const void* d_k_cache, const void* d_v_cache,
                                 float* d_output, int n_heads, int n_kv_heads, int seq_len,
                                 int head_dim, int kv_stride, void* stream);
+/* fused_attention.cu:244-258 / 744-762: cudaMalloc of [n_kv][max_seq_len][head_dim]
+ * f32 / f16; NULL on failure. */
+void* gpu_alloc_kv_buffer(int n_kv_heads, int max_seq_len, int head_dim, size_t* out_bytes);
+void* gpu_alloc_kv_buffer_half(int n_kv_heads, int max_seq_len, int head_dim, size_t* out_bytes);
+/* fused_attention.cu:260-285: one (kv_head, pos) row, host -> device, synchronous */
+int gpu_copy_kv_to_buffer(float* d_buf, const float* h_src, int kv_head, int pos, int n_kv_heads,
+                          int max_seq_len, int head_dim);
+/* fused_attention.cu:287-312, 456-481: all KV heads of position pos
+ * (h_src [n_kv][head_dim]) in one strided copy; synchronous / on `stream` */
+int gpu_copy_kv_layer(float* d_buf, const float* h_src, int pos, int n_kv_heads, int max_seq_len,
+                      int head_dim);
+int gpu_copy_kv_layer_async(float* d_buf, const float* h_src, int pos, int n_kv_heads,
+                            int max_seq_len, int head_dim, void* stream);
+/* fused_attention.cu:764-812: host f32 [n_kv][head_dim] -> f16 (RNE) rows of
+ * d_buf [n_kv][max_seq_len][head_dim] at pos, through a library-owned device
+ * staging buffer, on `stream` */
+int gpu_copy_kv_layer_async_half(void* d_buf, const float* h_src, int pos, int n_kv_heads,
+                                 int max_seq_len, int head_dim, void* stream);
 /* fused_attention.cu:687-717 */
 void* gpu_graph_create_attention_half(const float* d_q, const void* d_k_cache,
                                       const void* d_v_cache, float* d_scores, float* d_output,

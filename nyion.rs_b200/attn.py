@@ -67,6 +67,17 @@ def lib() -> C.CDLL:
             "gpu_graph_destroy": (None, [vp]),
             "nyion_attn_f16_workspace_size": (sz, [i32, i32]),
             "nyion_attn_positions_workspace_size": (sz, [i32, i32, i32]),
+            "nyion_attn_rope_table_bytes": (sz, [i32, i32]),
+            "nyion_attn_rope_table": (i32, [vp, i32, i32, vp]),
+            "nyion_attn_kv_write_paged": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, vp, i32, vp, i32, i64, vp, vp,
+                                                vp, vp, vp, i32, vp]),
+            "nyion_attn_kv_write_ring_f16": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp, i32, vp]),
+            "gpu_alloc_kv_buffer": (vp, [C.c_int, C.c_int, C.c_int, C.POINTER(sz)]),
+            "gpu_alloc_kv_buffer_half": (vp, [C.c_int, C.c_int, C.c_int, C.POINTER(sz)]),
+            "gpu_copy_kv_to_buffer": (C.c_int, [vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]),
+            "gpu_copy_kv_layer": (C.c_int, [vp, vp, C.c_int, C.c_int, C.c_int, C.c_int]),
+            "gpu_copy_kv_layer_async": (C.c_int, [vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, vp]),
+            "gpu_copy_kv_layer_async_half": (C.c_int, [vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, vp]),
             "nyion_attn_decode_positions": (i32, [vp, vp, i32, i64, vp, i32, vp, vp, i32, vp, i32, i32, i32, i32,
                                                   i32, f32, vp, sz, vp]),
             "nyion_attn_sparse_q4_workspace_size": (sz, [i32, i32]),
@@ -334,6 +345,42 @@ def sparse_q4(q, kv_pool, page_table, seq_lens, window: int, global_stride: int,
 
 def sparse_q4_workspace(batch: int, n_heads: int = 32, device=None):
     return RawWorkspace(lib().nyion_attn_sparse_q4_workspace_size(batch, n_heads), device)
+
+
+def rope_table(head_dim: int, max_context: int, device=None, stream=None):
+    """Device RoPE table [max_context][head_dim/2][2] (cos, sin) of the CPU engine
+    (ops.rs:20-38), built on the host with libm and uploaded."""
+    torch = _torch()
+    t = torch.empty(max_context, head_dim // 2, 2, dtype=torch.float32, device=device or "cuda")
+    check(lib().nyion_attn_rope_table(_ptr(t), head_dim, max_context, _stream_ptr(stream)))
+    return t
+
+
+def kv_write_paged(k, v, positions, q=None, row_seq=None, rope=None, page_table=None, n_pool_pages: int = 0,
+                   pool_q4=None, pool_f32=None, pool_bf16=None, q_bf16=None, ring_f32=None, stream=None):
+    """RoPE on q / k (in place) and the K / V save into the given caches (nyion_attn_kv_write_paged).
+    k, v [rows, n_kv, D] f32; positions [rows] int32; rope = rope_table(...) or None."""
+    rows, n_kv, D = k.shape
+    n_heads = q.shape[1] if q is not None else 0
+    pools = [x for x in (pool_q4, pool_f32, pool_bf16) if x is not None]
+    if pools and not n_pool_pages:
+        n_pool_pages = pools[0].shape[0]
+    check(lib().nyion_attn_kv_write_paged(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(positions), _ptr(row_seq), rows, n_heads, n_kv, D, _ptr(rope),
+        rope.shape[0] if rope is not None else 0, _ptr(page_table),
+        page_table.shape[-1] if page_table is not None else 0, n_pool_pages, _ptr(pool_q4), _ptr(pool_f32),
+        _ptr(pool_bf16), _ptr(q_bf16), _ptr(ring_f32), ring_f32.shape[3] if ring_f32 is not None else 0,
+        _stream_ptr(stream)))
+
+
+def kv_write_ring_f16(k, v, d_seq_len, k_ring, v_ring, q=None, d_wpos=None, rope=None, stream=None):
+    """Layer-graph RoPE + f16 ring save of one sequence (nyion_attn_kv_write_ring_f16).
+    k, v [n_kv, D] f32; k_ring / v_ring [n_kv, window, D] f16; d_seq_len int32 [1]."""
+    n_kv, D = k.shape
+    n_heads = q.shape[0] if q is not None else 0
+    check(lib().nyion_attn_kv_write_ring_f16(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(d_seq_len), _ptr(d_wpos), _ptr(k_ring), _ptr(v_ring), n_heads, n_kv, D,
+        k_ring.shape[1], _ptr(rope), rope.shape[0] if rope is not None else 0, _stream_ptr(stream)))
 
 
 def prefill_paged_bf16(q, kv_pool, page_table, q_start: int, out=None, scale: float = 0.0,

@@ -592,6 +592,45 @@ void or_attention_sparse_q4(float* out, const float* q, const uint8_t* const* k_
 }
 
 /* ======================================================================= */
+/* RoPE — swamp-engine/src/ops.rs:20-84                                      */
+/* ======================================================================= */
+
+/* init_rope_lut (ops.rs:20-38): freq = 1 / theta^((2k) / head_dim) in f32,
+ * angle = m * freq, (cos, sin) of the angle; libm powf / cosf / sinf are the
+ * functions Rust's f32::powf / cos / sin call. */
+void or_rope_lut(float* lut, int head_dim, int64_t max_seq_len) {
+    int half = head_dim / 2;
+    for (int64_t m = 0; m < max_seq_len; m++) {
+        for (int k = 0; k < half; k++) {
+            float freq = 1.0f / powf(10000.0f, (float)(2 * k) / (float)head_dim);
+            float angle = (float)m * freq;
+            lut[(m * half + k) * 2] = cosf(angle);
+            lut[(m * half + k) * 2 + 1] = sinf(angle);
+        }
+    }
+}
+
+/* apply_rotation_pair (ops.rs:70-84): x' = x cos - y sin, y' = x sin + y cos */
+static void rope_rotate(float* vec, const float* cs, int half) {
+    for (int k = 0; k < half; k++) {
+        float x = vec[2 * k], y = vec[2 * k + 1];
+        float c = cs[2 * k], s = cs[2 * k + 1];
+        vec[2 * k] = x * c - y * s;
+        vec[2 * k + 1] = x * s + y * c;
+    }
+}
+
+/* apply_rope_ufc (ops.rs:42-68): position clamped to max_context - 1 */
+void or_apply_rope(float* q, float* k, int64_t pos, int n_q_heads, int n_kv_heads, int head_dim,
+                   int64_t max_context, const float* lut) {
+    int half = head_dim / 2;
+    if (pos > max_context - 1) pos = max_context - 1;
+    const float* cs = lut + pos * half * 2;
+    for (int h = 0; h < n_q_heads; h++) rope_rotate(q + (int64_t)h * head_dim, cs, half);
+    for (int h = 0; h < n_kv_heads; h++) rope_rotate(k + (int64_t)h * head_dim, cs, half);
+}
+
+/* ======================================================================= */
 /* Q16.16 softmax — swamp-kernels/src/lib.rs:97-223 (AVX-512 path)          */
 /* ======================================================================= */
 

@@ -85,6 +85,14 @@ void or_attention_sparse_q4(float* out, const float* q,
 int64_t or_sparse_positions(int64_t seq_len, int64_t q_pos, int64_t window,
                             int64_t global_stride, int64_t* positions, int64_t cap);
 
+/* ---- RoPE of the CPU engine (swamp-engine/src/ops.rs:20-84) ---- */
+/* lut [max_seq_len][head_dim/2][2] = (cos, sin) of pos * 10000^(-2k/head_dim) */
+void or_rope_lut(float* lut, int head_dim, int64_t max_seq_len);
+/* rotates q [n_q_heads][head_dim] and k [n_kv_heads][head_dim] in place at
+ * min(pos, max_context - 1) */
+void or_apply_rope(float* q, float* k, int64_t pos, int n_q_heads, int n_kv_heads, int head_dim,
+                   int64_t max_context, const float* lut);
+
 /* ---- Q16.16 softmax (swamp-kernels/src/lib.rs:97-223) ---- */
 int32_t or_exp_q16_16(int32_t x_fixed);
 void    or_softmax_padic(const float* logits, float* probs, int n, float temperature);

@@ -62,6 +62,8 @@ def lib():
             "or_attention_sparse_q4": (None, [f32p, f32p, C.c_void_p, C.c_void_p, i32, i32, i64, i64, i32, i32, i32, i64, i64, i32]),
             "or_sparse_positions": (i64, [i64, i64, i64, i64, i64p, i64]),
             "or_exp_q16_16": (C.c_int32, [C.c_int32]),
+            "or_rope_lut": (None, [f32p, i32, i64]),
+            "or_apply_rope": (None, [f32p, f32p, i64, i32, i32, i32, i64, f32p]),
             "or_softmax_padic": (None, [f32p, f32p, i32, f32]),
             "or_stokes_init": (C.c_void_p, [i32]),
             "or_stokes_append": (None, [C.c_void_p, i32, f32p, f32p, f32]),
@@ -257,6 +259,24 @@ def sparse_positions(seq_len, q_pos, window, global_stride) -> np.ndarray:
     buf = np.zeros(cap, np.int64)
     n = lib().or_sparse_positions(seq_len, q_pos, window, global_stride, buf, cap)
     return buf[:n].copy()
+
+
+# ---------------------------------------------------------------- rope
+def rope_lut(head_dim: int, max_seq_len: int) -> np.ndarray:
+    """[max_seq_len][head_dim/2][2] (cos, sin), ops.rs:20-38."""
+    lut = np.zeros((max_seq_len, head_dim // 2, 2), np.float32)
+    lib().or_rope_lut(lut.reshape(-1), head_dim, max_seq_len)
+    return lut
+
+
+def apply_rope(q, k, pos: int, max_context: int, lut: np.ndarray):
+    """Rotated copies of q [n_q][hd] and k [n_kv][hd] (ops.rs:42-84)."""
+    q = _c(q, np.float32).copy()
+    k = _c(k, np.float32).copy()
+    hd = q.shape[-1]
+    lib().or_apply_rope(q.reshape(-1), k.reshape(-1), int(pos), q.size // hd, k.size // hd, hd, int(max_context),
+                        _c(lut, np.float32).reshape(-1))
+    return q, k
 
 
 # ---------------------------------------------------------------- softmax / stokes

@@ -421,3 +421,30 @@ def test_lse_combine_matches_full():
     whole = O.lse_combine(O.decode_q4_partial(q, pool, table, 0, T, n_kv, hd, pt)[None])
     assert np.abs(merged - whole).max() < 1e-5
     assert full.shape == merged.shape
+
+
+def test_rope_restatement_properties():
+    """ops.rs:20-84: position 0 is the identity, positions past max_context use
+    max_context - 1, the table equals cos / sin of the f32 angle m * freq to a
+    few f32 ulps, and a rotation keeps every pair's norm."""
+    hd, ctx = 64, 3000
+    lut = O.rope_lut(hd, ctx)
+    rng = np.random.default_rng(5)
+    q = rng.standard_normal((32, hd)).astype(np.float32)
+    k = rng.standard_normal((4, hd)).astype(np.float32)
+    q0, k0 = O.apply_rope(q, k, 0, ctx, lut)
+    assert np.array_equal(q0, q) and np.array_equal(k0, k)
+    qa, _ = O.apply_rope(q, k, 10 ** 7, ctx, lut)
+    qb, _ = O.apply_rope(q, k, ctx - 1, ctx, lut)
+    assert np.array_equal(qa, qb)
+    kk = np.arange(hd // 2, dtype=np.float32)
+    freq = (np.float32(1.0) / np.power(np.float32(10000.0), (2 * kk) / np.float32(hd))).astype(np.float32)
+    ang = (np.arange(ctx, dtype=np.float32)[:, None] * freq[None]).astype(np.float32).astype(np.float64)
+    # freq may differ from numpy's power by an ulp, which moves large angles by ulps of the angle
+    tol = 1e-6 + 4 * np.spacing(ang.astype(np.float32)).astype(np.float64)
+    assert (np.abs(lut[..., 0] - np.cos(ang)) <= tol).all()
+    assert (np.abs(lut[..., 1] - np.sin(ang)) <= tol).all()
+    qr, _ = O.apply_rope(q, k, 1234, ctx, lut)
+    n0 = np.hypot(q[:, 0::2].astype(np.float64), q[:, 1::2])
+    n1 = np.hypot(qr[:, 0::2].astype(np.float64), qr[:, 1::2])
+    assert np.abs(n0 - n1).max() < 1e-5
