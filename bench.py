@@ -67,7 +67,7 @@ def peaks():
 
 def profiled_traffic():
     """DRAM bytes per decode launch (read + write) from the committed ncu summary."""
-    path = os.path.join(ROOT, "profiles", "decode_f32_config2.md")
+    path = os.path.join(ROOT, "profiles", "decode_pages_config2.md")
     try:
         for line in open(path):
             if line.startswith("traffic_bytes_per_launch:"):

@@ -222,6 +222,17 @@ int32_t nyion_attn_decode_zoned_f32(float* out, const float* q, const float* k_a
                                     int32_t layer_idx, int64_t seq_len, int64_t q_pos,
                                     int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
                                     void* stream);
+/* ops::attention_tracked (ops.rs:283-401): the same decode plus, for every
+ * position t in [0, min(q_pos, seq_len - 1)], importance[t] += sum over the
+ * query heads of the softmax weight p_h(t) (double, device array of seq_len;
+ * masked positions are left unchanged, as adding 0 leaves them).  The weights
+ * are recomputed from the scores in two small launches after the decode
+ * (the path the executor takes for short sequences). */
+int32_t nyion_attn_decode_zoned_f32_tracked(float* out, const float* q, const float* k_arena,
+                                            const float* v_arena, int64_t n_arena_pages,
+                                            int32_t n_layers, int32_t layer_idx, int64_t seq_len,
+                                            int64_t q_pos, int32_t n_heads, int32_t n_kv_heads,
+                                            int32_t head_dim, double* importance, void* stream);
 
 /* ---------------------------------- split-KV across GPUs, exchange fused ----
  * No reference counterpart (the reference has no multi-GPU attention); the
@@ -378,6 +389,34 @@ int32_t nyion_attn_kv_write_ring_f16(float* q, float* k, const float* v, const i
                                      int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
                                      int32_t window, const float* rope_table, int32_t max_context,
                                      void* stream);
+
+/* ------------------------------------------------------- cold-tier pages ----
+ * The reference's NVMe cold slot (swamp-engine/src/cache.rs:251-276, 440-483,
+ * 485-529): [K q4 page][V q4 page], a q4 page = [n_layers][n_kv][block_slots]
+ * [ceil(head_dim/32) x 20 B] (cache.rs:681-747), block_slots 32 / 128 / 1024
+ * for zones 0 / 1 / 2; the reference reads and writes slot s of a zone at
+ * file offset s * 2 * q4_page_bytes(zone) (nyion_attn_cold_slot_offset).
+ * nyion_attn_cold_to_pool scatters one slot into per-layer 4-bit page pools
+ * [n_pool_pages][n_kv][K|V][16][40] (the format the Q4 kernels read):
+ * layer_pools = host array of n_layers device pool pointers (8-byte aligned,
+ * n_layers <= 128), page_ids = device [n_layers][block_slots / 16]
+ * destination page of each 16-slot run.  `slot` may be HBM or pinned host
+ * memory mapped into the device address space (read over the bus); every
+ * pointer is checked with cudaPointerGetAttributes before the launch.
+ * nyion_attn_pool_to_cold gathers the same pages back into a slot image
+ * (eviction).  Page ids outside [0, n_pool_pages) raise the page-range bit
+ * and move nothing for those rows.  This build: head_dim 64. */
+size_t nyion_attn_cold_q4_page_bytes(int32_t block_slots, int32_t n_layers, int32_t n_kv_heads,
+                                     int32_t head_dim);
+int64_t nyion_attn_cold_slot_offset(int64_t slot, int32_t block_slots, int32_t n_layers,
+                                    int32_t n_kv_heads, int32_t head_dim);
+int32_t nyion_attn_cold_to_pool(const uint8_t* slot, int32_t block_slots, int32_t n_layers,
+                                int32_t n_kv_heads, int32_t head_dim, uint8_t* const* layer_pools,
+                                const int32_t* page_ids, int64_t n_pool_pages, void* stream);
+int32_t nyion_attn_pool_to_cold(uint8_t* const* layer_pools, const int32_t* page_ids,
+                                int32_t block_slots, int32_t n_layers, int32_t n_kv_heads,
+                                int32_t head_dim, int64_t n_pool_pages, uint8_t* slot,
+                                void* stream);
 
 /* ---------------------------------------------- reference CUDA C ABI -------
  * Same names, arguments and 0 / -1 results as swamp-gpu/kernels/fused_attention.cu,

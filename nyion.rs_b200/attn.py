@@ -67,6 +67,12 @@ def lib() -> C.CDLL:
             "gpu_graph_destroy": (None, [vp]),
             "nyion_attn_f16_workspace_size": (sz, [i32, i32]),
             "nyion_attn_positions_workspace_size": (sz, [i32, i32, i32]),
+            "nyion_attn_decode_zoned_f32_tracked": (i32, [vp, vp, vp, vp, i64, i32, i32, i64, i64, i32, i32, i32,
+                                                          vp, vp]),
+            "nyion_attn_cold_q4_page_bytes": (sz, [i32, i32, i32, i32]),
+            "nyion_attn_cold_slot_offset": (i64, [i64, i32, i32, i32, i32]),
+            "nyion_attn_cold_to_pool": (i32, [vp, i32, i32, i32, i32, vp, vp, i64, vp]),
+            "nyion_attn_pool_to_cold": (i32, [vp, vp, i32, i32, i32, i32, i64, vp, vp]),
             "nyion_attn_rope_table_bytes": (sz, [i32, i32]),
             "nyion_attn_rope_table": (i32, [vp, i32, i32, vp]),
             "nyion_attn_kv_write_paged": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, vp, i32, vp, i32, i64, vp, vp,
@@ -193,6 +199,17 @@ def decode_paged_f32(q, kv_pool, page_table, seq_lens, out=None, scale: float = 
     return out
 
 
+def _zone_pages(k_arena, n_layers: int, n_kv: int, D: int) -> int:
+    per_slot = n_layers * n_kv * D
+    n = k_arena.numel()
+    z0 = min(n // (per_slot * 32), 128)
+    rest = n - z0 * per_slot * 32
+    z1 = min(rest // (per_slot * 128), 992) if z0 == 128 else 0
+    rest -= z1 * per_slot * 128
+    z2 = rest // (per_slot * 1024) if z1 == 992 else 0
+    return z0 + z1 + z2
+
+
 def decode_zoned_f32(q, k_arena, v_arena, n_layers: int, layer: int, seq_len: int, q_pos: int,
                      out=None, stream=None):
     """ops::attention over reference-layout zone pages (nyion_attn_decode_zoned_f32).
@@ -203,19 +220,27 @@ def decode_zoned_f32(q, k_arena, v_arena, n_layers: int, layer: int, seq_len: in
     torch = _torch()
     H, D = q.shape
     n_kv = H // 8
-    per_slot = n_layers * n_kv * D
-    n = k_arena.numel()
-    z0 = min(n // (per_slot * 32), 128)
-    rest = n - z0 * per_slot * 32
-    z1 = min(rest // (per_slot * 128), 992) if z0 == 128 else 0
-    rest -= z1 * per_slot * 128
-    z2 = rest // (per_slot * 1024) if z1 == 992 else 0
-    n_pages = z0 + z1 + z2
     if out is None:
         out = torch.empty_like(q)
     check(lib().nyion_attn_decode_zoned_f32(_ptr(out), _ptr(q), _ptr(k_arena), _ptr(v_arena),
-                                            n_pages, n_layers, layer, seq_len, q_pos, H, n_kv, D,
-                                            _stream_ptr(stream)))
+                                            _zone_pages(k_arena, n_layers, n_kv, D), n_layers, layer, seq_len,
+                                            q_pos, H, n_kv, D, _stream_ptr(stream)))
+    return out
+
+
+def decode_zoned_f32_tracked(q, k_arena, v_arena, n_layers: int, layer: int, seq_len: int, q_pos: int,
+                             importance, out=None, stream=None):
+    """ops::attention_tracked: decode_zoned_f32 plus importance[t] += sum_h p_h(t)
+    (importance: float64 device tensor of seq_len)."""
+    torch = _torch()
+    H, D = q.shape
+    n_kv = H // 8
+    assert importance.dtype == torch.float64 and importance.numel() >= seq_len
+    if out is None:
+        out = torch.empty_like(q)
+    check(lib().nyion_attn_decode_zoned_f32_tracked(
+        _ptr(out), _ptr(q), _ptr(k_arena), _ptr(v_arena), _zone_pages(k_arena, n_layers, n_kv, D), n_layers,
+        layer, seq_len, q_pos, H, n_kv, D, _ptr(importance), _stream_ptr(stream)))
     return out
 
 
@@ -345,6 +370,29 @@ def sparse_q4(q, kv_pool, page_table, seq_lens, window: int, global_stride: int,
 
 def sparse_q4_workspace(batch: int, n_heads: int = 32, device=None):
     return RawWorkspace(lib().nyion_attn_sparse_q4_workspace_size(batch, n_heads), device)
+
+
+def cold_to_pool(slot, block_slots: int, layer_pools, page_ids, stream=None):
+    """Scatter one reference cold slot (uint8, HBM or pinned host) into per-layer
+    4-bit pools (list of [P, n_kv, 2, 16, 40] uint8 tensors); page_ids int32
+    [n_layers, block_slots / 16] on the device."""
+    n_layers = len(layer_pools)
+    n_kv = layer_pools[0].shape[1]
+    ptrs = (C.c_void_p * n_layers)(*[p.data_ptr() for p in layer_pools])
+    check(lib().nyion_attn_cold_to_pool(_ptr(slot), block_slots, n_layers, n_kv, 64, ptrs, _ptr(page_ids),
+                                        layer_pools[0].shape[0], _stream_ptr(stream)))
+
+
+def pool_to_cold(layer_pools, page_ids, block_slots: int, slot, stream=None):
+    n_layers = len(layer_pools)
+    n_kv = layer_pools[0].shape[1]
+    ptrs = (C.c_void_p * n_layers)(*[p.data_ptr() for p in layer_pools])
+    check(lib().nyion_attn_pool_to_cold(ptrs, _ptr(page_ids), block_slots, n_layers, n_kv, 64,
+                                        layer_pools[0].shape[0], _ptr(slot), _stream_ptr(stream)))
+
+
+def cold_q4_page_bytes(block_slots: int, n_layers: int, n_kv: int, head_dim: int = 64) -> int:
+    return int(lib().nyion_attn_cold_q4_page_bytes(block_slots, n_layers, n_kv, head_dim))
 
 
 def rope_table(head_dim: int, max_context: int, device=None, stream=None):

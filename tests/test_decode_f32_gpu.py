@@ -169,3 +169,24 @@ def test_unsupported_shape_is_an_error(cuda_device):
     rc = L.gpu_attention_device(x.data_ptr(), x.data_ptr(), x.data_ptr(), x.data_ptr(),
                                 4, 4, 1, 128, 1)
     assert rc == -1 and "head_dim" in A.last_error()
+
+
+@pytest.mark.parametrize("ctx,qpos,prior", [(1, 0, 0.0), (128, 127, 0.0), (300, 200, 0.5), (512, 511, 0.0),
+                                            (4200, 4199, 0.25)])
+def test_attention_tracked_importance(cuda_device, ctx, qpos, prior):
+    """ops::attention_tracked (ops.rs:283-401): same output as the decode, and
+    importance[t] += sum over heads of the softmax weights (positions past
+    q_pos keep their value); the oracle sums the f32 weights in double."""
+    gen = torch.Generator().manual_seed(ctx + qpos)
+    zp = _zoned_store(1, ctx, gen)
+    q = torch.randn(H, D, generator=gen)
+    k, v = _arenas(zp, cuda_device)
+    imp = torch.full((ctx,), prior, dtype=torch.float64, device=cuda_device)
+    out = A.decode_zoned_f32_tracked(q.to(cuda_device), k, v, 1, 0, ctx, qpos, imp)
+    ref_out, ref_imp = O.attention(zp, q.numpy(), 0, ctx, qpos, H, tracked=True)
+    assert np.abs(out.cpu().numpy() - ref_out).max() < TOL
+    got = imp.cpu().numpy() - prior
+    assert np.abs(got - ref_imp).max() < 1e-5
+    assert abs(got.sum() - H) < 1e-4                        # each head's weights sum to 1
+    assert not got[qpos + 1:].any()
+    assert A.device_error() == 0
