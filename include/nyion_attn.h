@@ -418,6 +418,35 @@ int32_t nyion_attn_pool_to_cold(uint8_t* const* layer_pools, const int32_t* page
                                 int32_t head_dim, int64_t n_pool_pages, uint8_t* slot,
                                 void* stream);
 
+/* ------------------------------------------------- O-projection Q4_K GEMV ----
+ * The layer graph's GEMV (swamp-gpu/kernels/fused_attention.cu:858-925) so
+ * the attention output stays on the device: w = Q4_K super-blocks of 256
+ * columns (144 B: f16 d, f16 dmin, 12 B of 6-bit scales/mins, 128 B of
+ * nibbles), column-major at super-block level (block b of row r at
+ * (b * n_rows + r) * 144, as gpu_upload_weights_transposed stores them),
+ * weight = d (nib - 8) scale_sb + dmin min_sb as the reference kernel
+ * computes it.  x [batch][n_blocks * 256] f32, out [batch][n_rows] f32;
+ * w 16-byte aligned. */
+int32_t nyion_attn_gemv_q4k(const uint8_t* w, const float* x, float* out, int32_t n_rows,
+                            int32_t n_blocks, int32_t batch, void* stream);
+/* fused_attention.cu:916-925, same name and arguments (batch 1). */
+void gpu_gemv_q4k(const uint8_t* d_w, const float* d_x, float* d_out, int n_rows, int n_blocks,
+                  void* stream);
+
+/* ----------------------------------------------------------- Mojo FFI -----
+ * swamp-gpu/kernels/attention.mojo:122-152 `sparse_attention_q4`, with the
+ * argument list its Rust binding declares (swamp-gpu/src/mojo.rs:5, 65-97):
+ * raw host pointers q [n_heads][head_dim] f32, k_q4 / v_q4 rows of
+ * ceil(head_dim/32) blocks x 20 f32 [d, dmin, 16 byte values, 2 unused]
+ * indexed by position, positions [n_sparse] int32, out [n_heads][head_dim];
+ * window and global_stride unused (as in the Mojo kernel).  Tiles of 64
+ * positions with the kernel's running (m, d) per tile and no rescaling of
+ * earlier tiles, weights < 1e-8 skipped — as written.  Only the listed rows
+ * are copied to the GPU; synchronous.  head_dim <= 256. */
+void sparse_attention_q4(uint64_t q, uint64_t k_q4, uint64_t v_q4, uint64_t positions, uint64_t out,
+                         int32_t n_heads, int32_t head_dim, int32_t n_sparse, int32_t window,
+                         int32_t global_stride);
+
 /* ---------------------------------------------- reference CUDA C ABI -------
  * Same names, arguments and 0 / -1 results as swamp-gpu/kernels/fused_attention.cu,
  * so the reference's Rust declarations (swamp-gpu/src/lib.rs:586-677) link

@@ -73,6 +73,9 @@ def lib() -> C.CDLL:
             "nyion_attn_cold_slot_offset": (i64, [i64, i32, i32, i32, i32]),
             "nyion_attn_cold_to_pool": (i32, [vp, i32, i32, i32, i32, vp, vp, i64, vp]),
             "nyion_attn_pool_to_cold": (i32, [vp, vp, i32, i32, i32, i32, i64, vp, vp]),
+            "sparse_attention_q4": (None, [C.c_uint64] * 5 + [i32] * 5),
+            "nyion_attn_gemv_q4k": (i32, [vp, vp, vp, i32, i32, i32, vp]),
+            "gpu_gemv_q4k": (None, [vp, vp, vp, C.c_int, C.c_int, vp]),
             "nyion_attn_rope_table_bytes": (sz, [i32, i32]),
             "nyion_attn_rope_table": (i32, [vp, i32, i32, vp]),
             "nyion_attn_kv_write_paged": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, vp, i32, vp, i32, i64, vp, vp,
@@ -393,6 +396,18 @@ def pool_to_cold(layer_pools, page_ids, block_slots: int, slot, stream=None):
 
 def cold_q4_page_bytes(block_slots: int, n_layers: int, n_kv: int, head_dim: int = 64) -> int:
     return int(lib().nyion_attn_cold_q4_page_bytes(block_slots, n_layers, n_kv, head_dim))
+
+
+def gemv_q4k(w, x, n_rows: int, out=None, stream=None):
+    """Q4_K GEMV of the layer graph: w uint8 column-major super-blocks, x [B, n_cols] f32."""
+    torch = _torch()
+    x2 = x.reshape(-1, x.shape[-1])
+    n_blocks = x2.shape[1] // 256
+    if out is None:
+        out = torch.empty(x2.shape[0], n_rows, dtype=torch.float32, device=x.device)
+    check(lib().nyion_attn_gemv_q4k(_ptr(w), _ptr(x2), _ptr(out), n_rows, n_blocks, x2.shape[0],
+                                    _stream_ptr(stream)))
+    return out
 
 
 def rope_table(head_dim: int, max_context: int, device=None, stream=None):

@@ -631,6 +631,93 @@ void or_apply_rope(float* q, float* k, int64_t pos, int n_q_heads, int n_kv_head
 }
 
 /* ======================================================================= */
+/* Mojo sparse_attention_q4 — swamp-gpu/kernels/attention.mojo:40-152       */
+/* ======================================================================= */
+
+static float mojo_dequant(const float* blk, int i) {        /* attention.mojo:70-78 */
+    int byte = (int)blk[2 + i / 2];
+    int nib = (byte >> ((i % 2) * 4)) & 0x0F;
+    return blk[0] * (float)nib + blk[1];
+}
+
+/* flash_attn_head (attention.mojo:40-118) for every head (:122-152) */
+void or_mojo_sparse_attention_q4(const float* q, const float* k_q4, const float* v_q4,
+                                 const int32_t* positions, float* out, int n_heads, int head_dim,
+                                 int n_sparse) {
+    const int blocks = (head_dim + 31) / 32, blk_f = blocks * 20;
+    const float scale = 1.0f / sqrtf((float)head_dim);
+    float scores[64];
+    for (int h = 0; h < n_heads; h++) {
+        const float* qh = q + (int64_t)h * head_dim;
+        float* oh = out + (int64_t)h * head_dim;
+        float m = -1e10f, d = 0.0f;
+        for (int i = 0; i < head_dim; i++) oh[i] = 0.0f;
+        for (int t0 = 0; t0 < n_sparse; t0 += 64) {
+            int n_tile = n_sparse - t0 < 64 ? n_sparse - t0 : 64;
+            float max_score = -1e10f;
+            for (int p = 0; p < n_tile; p++) {
+                const float* kr = k_q4 + (int64_t)positions[t0 + p] * blk_f;
+                float dot = 0.0f;
+                for (int b = 0; b < blocks; b++)
+                    for (int i = 0; i < 32 && b * 32 + i < head_dim; i++)
+                        dot += mojo_dequant(kr + b * 20, i) * qh[b * 32 + i];
+                float sc = dot * scale;
+                scores[p] = sc;
+                if (sc > max_score) max_score = sc;
+            }
+            float tile_d = 0.0f;
+            for (int p = 0; p < n_tile; p++) tile_d += expf(scores[p] - max_score);
+            float new_m = fmaxf(m, max_score);
+            d = d * expf(m - new_m) + tile_d * expf(max_score - new_m);
+            m = new_m;
+            for (int p = 0; p < n_tile; p++) {
+                float w = expf(scores[p] - m) / d;
+                if (w < 1e-8f) continue;
+                const float* vr = v_q4 + (int64_t)positions[t0 + p] * blk_f;
+                for (int b = 0; b < blocks; b++)
+                    for (int i = 0; i < 32 && b * 32 + i < head_dim; i++)
+                        oh[b * 32 + i] += mojo_dequant(vr + b * 20, i) * w;
+            }
+        }
+    }
+}
+
+/* ======================================================================= */
+/* Q4_K GEMV — swamp-gpu/kernels/fused_attention.cu:858-914                  */
+/* ======================================================================= */
+
+void or_gemv_q4k(const uint8_t* w, const float* x, float* out, int n_rows, int n_blocks) {
+    for (int row = 0; row < n_rows; row++) {
+        float total = 0.0f;
+        for (int blk = 0; blk < n_blocks; blk++) {
+            const uint8_t* b = w + ((size_t)blk * n_rows + row) * 144;
+            float d = or_f16_to_f32((uint16_t)(b[0] | (b[1] << 8)));
+            float dmin = or_f16_to_f32((uint16_t)(b[2] | (b[3] << 8)));
+            float scales[8], mins[8];
+            for (int j = 0; j < 4; j++) {
+                scales[j] = (float)(b[4 + j] & 63);
+                mins[j] = (float)(b[8 + j] & 63);
+            }
+            for (int j = 4; j < 8; j++) {
+                scales[j] = (float)((b[8 + j] & 0xF) | ((b[4 + j - 4] >> 6) << 4));
+                mins[j] = (float)((b[8 + j] >> 4) | ((b[4 + j] >> 6) << 4));
+            }
+            const uint8_t* qs = b + 16;
+            float dot = 0.0f;
+            for (int sb = 0; sb < 8; sb++) {
+                for (int k = 0; k < 32; k++) {
+                    int nib = (qs[sb * 16 + k / 2] >> ((k % 2) * 4)) & 0x0F;
+                    float xk = x[blk * 256 + sb * 32 + k];
+                    dot += (d * (float)(nib - 8) * scales[sb] + dmin * mins[sb]) * xk;
+                }
+            }
+            total += dot;
+        }
+        out[row] = total;
+    }
+}
+
+/* ======================================================================= */
 /* Q16.16 softmax — swamp-kernels/src/lib.rs:97-223 (AVX-512 path)          */
 /* ======================================================================= */
 

@@ -93,6 +93,18 @@ void or_rope_lut(float* lut, int head_dim, int64_t max_seq_len);
 void or_apply_rope(float* q, float* k, int64_t pos, int n_q_heads, int n_kv_heads, int head_dim,
                    int64_t max_context, const float* lut);
 
+/* ---- Mojo sparse_attention_q4 (swamp-gpu/kernels/attention.mojo:40-152) ----
+ * rows of ceil(hd/32) blocks x 20 floats [d, dmin, 16 byte values, 2 unused];
+ * tiles of 64 positions; earlier tiles are not rescaled (as written). */
+void or_mojo_sparse_attention_q4(const float* q, const float* k_q4, const float* v_q4,
+                                 const int32_t* positions, float* out, int n_heads, int head_dim,
+                                 int n_sparse);
+
+/* ---- Q4_K GEMV of the layer graph (swamp-gpu/kernels/fused_attention.cu:858-914) ----
+ * w column-major super-blocks (block b of row r at (b * n_rows + r) * 144),
+ * x [n_blocks * 256], out [n_rows]; the kernel's formula as written. */
+void or_gemv_q4k(const uint8_t* w, const float* x, float* out, int n_rows, int n_blocks);
+
 /* ---- Q16.16 softmax (swamp-kernels/src/lib.rs:97-223) ---- */
 int32_t or_exp_q16_16(int32_t x_fixed);
 void    or_softmax_padic(const float* logits, float* probs, int n, float temperature);

@@ -63,6 +63,8 @@ def lib():
             "or_sparse_positions": (i64, [i64, i64, i64, i64, i64p, i64]),
             "or_exp_q16_16": (C.c_int32, [C.c_int32]),
             "or_rope_lut": (None, [f32p, i32, i64]),
+            "or_gemv_q4k": (None, [u8p, f32p, f32p, i32, i32]),
+            "or_mojo_sparse_attention_q4": (None, [f32p, f32p, f32p, i32p, f32p, i32, i32, i32]),
             "or_apply_rope": (None, [f32p, f32p, i64, i32, i32, i32, i64, f32p]),
             "or_softmax_padic": (None, [f32p, f32p, i32, f32]),
             "or_stokes_init": (C.c_void_p, [i32]),
@@ -277,6 +279,36 @@ def apply_rope(q, k, pos: int, max_context: int, lut: np.ndarray):
     lib().or_apply_rope(q.reshape(-1), k.reshape(-1), int(pos), q.size // hd, k.size // hd, hd, int(max_context),
                         _c(lut, np.float32).reshape(-1))
     return q, k
+
+
+def gemv_q4k(w, x, n_rows: int, n_blocks: int) -> np.ndarray:
+    """fused_attention.cu:858-914 Q4_K GEMV (column-major super-blocks)."""
+    out = np.zeros(n_rows, np.float32)
+    lib().or_gemv_q4k(_c(w, np.uint8).reshape(-1), _c(x, np.float32).reshape(-1), out, n_rows, n_blocks)
+    return out
+
+
+def mojo_sparse_attention_q4(q, k_rows, v_rows, positions):
+    """attention.mojo:40-152 as written: q [H][hd]; k_rows / v_rows [n][blocks*20] f32."""
+    q = _c(q, np.float32)
+    H, hd = q.shape
+    out = np.zeros((H, hd), np.float32)
+    pos = _c(positions, np.int32)
+    lib().or_mojo_sparse_attention_q4(q.reshape(-1), _c(k_rows, np.float32).reshape(-1),
+                                      _c(v_rows, np.float32).reshape(-1), pos, out.reshape(-1), H, hd, pos.size)
+    return out
+
+
+def mojo_rows_from_q4(rows_u8: np.ndarray) -> np.ndarray:
+    """20-byte blocks [f16 d][f16 dmin][16 B] -> the Mojo kernel's 20-float blocks."""
+    r = _c(rows_u8, np.uint8)
+    nblk = r.shape[-1] // 20
+    b = r.reshape(r.shape[:-1] + (nblk, 20))
+    out = np.zeros(b.shape, np.float32)
+    out[..., 0] = b[..., 0:2].copy().view(np.float16)[..., 0].astype(np.float32)
+    out[..., 1] = b[..., 2:4].copy().view(np.float16)[..., 0].astype(np.float32)
+    out[..., 2:18] = b[..., 4:20].astype(np.float32)
+    return out.reshape(r.shape[:-1] + (nblk * 20,))
 
 
 # ---------------------------------------------------------------- softmax / stokes

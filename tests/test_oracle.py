@@ -448,3 +448,45 @@ def test_rope_restatement_properties():
     n0 = np.hypot(q[:, 0::2].astype(np.float64), q[:, 1::2])
     n1 = np.hypot(qr[:, 0::2].astype(np.float64), qr[:, 1::2])
     assert np.abs(n0 - n1).max() < 1e-5
+
+
+def _mojo_quirk_f64(q, k, v, positions):
+    """attention.mojo:40-118 in float64 from dequantized rows k, v [n][hd]."""
+    H, hd = q.shape
+    out = np.zeros((H, hd))
+    for h in range(H):
+        m, d = -1e10, 0.0
+        for t0 in range(0, len(positions), 64):
+            idx = positions[t0:t0 + 64]
+            s = (k[idx] @ q[h].astype(np.float64)) / np.sqrt(hd)
+            mx = max(-1e10, s.max())
+            td = np.exp(s - mx).sum()
+            nm = max(m, mx)
+            d = d * np.exp(m - nm) + td * np.exp(mx - nm)
+            m = nm
+            w = np.exp(s - m) / d
+            keep = w >= 1e-8
+            out[h] += (w[keep, None] * v[idx][keep]).sum(0)
+    return out
+
+
+@pytest.mark.parametrize("hd,n", [(64, 1), (64, 64), (64, 65), (32, 300), (96, 130)])
+def test_mojo_sparse_attention_restatement(hd, n):
+    """The Mojo kernel as written (tiles of 64, earlier tiles not rescaled):
+    the C restatement equals a float64 statement of the same recurrence, and a
+    single tile is plain softmax attention."""
+    rng = np.random.default_rng(hd + n)
+    T = 400
+    kf = rng.standard_normal((T, hd)).astype(np.float32)
+    vf = rng.standard_normal((T, hd)).astype(np.float32)
+    kq, vq = O.q4_quantize_rows(kf, hd), O.q4_quantize_rows(vf, hd)
+    kd, vd = O.q4_dequant_rows(kq, hd), O.q4_dequant_rows(vq, hd)
+    q = rng.standard_normal((4, hd)).astype(np.float32)
+    pos = rng.integers(0, T, n).astype(np.int32)
+    got = O.mojo_sparse_attention_q4(q, O.mojo_rows_from_q4(kq), O.mojo_rows_from_q4(vq), pos)
+    want = _mojo_quirk_f64(q, kd.astype(np.float64), vd.astype(np.float64), pos)
+    assert np.abs(got - want).max() < 1e-4
+    if n <= 64:
+        for h in range(4):
+            ref = _fp64_attention(q[h], kd[pos], vd[pos], 1 / np.sqrt(hd))
+            assert np.abs(got[h] - ref).max() < 1e-4
