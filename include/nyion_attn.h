@@ -153,7 +153,8 @@ int32_t nyion_attn_lse_combine(const float* parts, int32_t n_parts, int64_t rows
 /* 4-bit windowed decode with an fp32 ring: sequence b of
  * length L = seq_lens[b] attends [max(0, L - window), L); the newest
  * min(ring_tokens, window) tokens come from the fp32 ring
- * ring [batch][4][K|V][ring_tokens][head_dim] at slot pos % ring_tokens, the
+ * ring [batch][4][K|V][ring_tokens][head_dim] at slot pos % ring_tokens
+ * (ring_tokens <= 128), the
  * older ones from the Q4 pages.  out [batch][n_heads][head_dim].
  * workspace: nyion_attn_q4_workspace_size(batch) + 2 * batch * n_heads *
  * (head_dim + 2) * 4 + 8 * batch bytes, or NULL. */

@@ -24,6 +24,13 @@ enum : int32_t {
 // below this is several seconds, far above any legal TMA latency.
 constexpr uint32_t kSpinLimit = 1u << 22;
 
+// Programmatic dependent launch: let the next grid in the stream be scheduled,
+// then wait until the previous grid has completed and its writes are visible.
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -42,7 +42,7 @@ constexpr int PAGE_KV = 2 * PAGE * ROWB;      // 1280 B: K rows then V rows of o
 constexpr int PAGE_BYTES = NKV * PAGE_KV;     // 5120 B: one whole page
 constexpr int CHUNK = 64;               // tokens per stage (4 pages)
 constexpr int STAGE_BYTES = 4 * PAGE_BYTES;   // 20 KB
-constexpr int STAGES = 8;
+constexpr int STAGES = 3;                // x 2 CTAs per SM
 constexpr int NC = 8;                   // consumer warps: 4 KV heads x 2 token halves
 constexpr int THREADS = (NC + 1) * 32;
 constexpr int MAX_SEQS = 512;
@@ -141,6 +141,8 @@ struct Params {
 struct Smem {
   uint8_t kv[STAGES][STAGE_BYTES];
   uint8_t vt[NC][32 * 128];          // per warp: V chunk as fp16 [32 tokens][64], swizzled
+  float hdr[NC][32][8];              // per warp and token: K factors | V factors, halves swapped for
+                                     // tokens with bit 2 set (conflict-free 16-byte accesses)
   uint64_t full[STAGES], empty[STAGES];
   int32_t prefix[MAX_SEQS + 1];      // flat chunk index where sequence b starts
   int32_t c0[MAX_SEQS];              // first chunk (absolute, in 64-token units) of sequence b
@@ -244,6 +246,17 @@ __device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
   return v;
 }
 
+__device__ __forceinline__ float4 lds_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ void sts_f4(uint32_t addr, float4 v) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+
 __device__ __forceinline__ void sts_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
                : "memory");
@@ -259,10 +272,10 @@ __device__ __forceinline__ void named_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(NC * 32) : "memory");
 }
 
-__global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const Params p) {
+__global__ void __launch_bounds__(THREADS, 2) decode_q4_kernel(const Params p) {
   extern __shared__ uint8_t smem_raw[];
-  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                     ~uintptr_t(1023));
+  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
+                                     ~uintptr_t(127));
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int H = NKV * GROUP;
 
@@ -274,6 +287,11 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const Params p) {
     s.abort_ = 0;
     fence_barrier_init();
   }
+  // programmatic dependent launch: nothing global is read before the previous grid
+  // in the stream completed, and the next grid (the ring partial or the reduce) is
+  // released only after that, so it may read this kernel's inputs without waiting
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   for (int b = t; b < p.batch; b += THREADS) {
     int lo, hi;
     if (p.seq_lens) {
@@ -383,6 +401,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const Params p) {
   const int kvh = warp & 3, th = warp >> 2;
   const int g = lane >> 2, tig = lane & 3;
   const uint32_t vt = smem_u32(s.vt[warp]);
+  const uint32_t hd = smem_u32(s.hdr[warp]);
   // ldmatrix.trans row addresses of the V tile for k-step kt, n-tile pair np:
   // matrix m = lane>>3: tokens 16kt + 8(m&1) + (lane&7), 16-B chunk 2np + (m>>1)
   uint32_t voff[2][4];
@@ -464,10 +483,21 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const Params p) {
               sts_v4(vt + lane * 128 + (((ch ^ lane) & 7) << 4), nib2h<6>(w), nib2h<2>(w),
                      nib2h<-2>(w), nib2h<-6>(w));
             }
+          // block headers of token `lane` as the fp32 factors the score and P.V steps use:
+          // score = sum_blk 16 d (q.(1 + n/16)) + (dmin - 16 d) qs; zero for masked tokens
+          const uint32_t kr = vr - PAGE * ROWB;
+          const float2 k0 = hdr2f(lds_u32(kr)), k1 = hdr2f(lds_u32(kr + BLK));
+          const float2 v0 = hdr2f(lds_u32(vr)), v1 = hdr2f(lds_u32(vr + BLK));
+          const bool live = (pos0 + lane >= sb) && (pos0 + lane < se);
+          const float a0 = 16.0f * k0.x, a1 = 16.0f * k1.x, b0 = 16.0f * v0.x, b1 = 16.0f * v1.x;
+          const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+          const uint32_t sw = ((lane >> 2) & 1) << 4;
+          sts_f4(hd + lane * 32 + sw, live ? make_float4(a0, k0.y - a0, a1, k1.y - a1) : zero);
+          sts_f4(hd + lane * 32 + (sw ^ 16), live ? make_float4(b0, v0.y - b0, b1, v1.y - b1) : zero);
         }
+        __syncwarp();   // V tile rows and headers written by all lanes
         // ---- S = Q K^T: 4 n-tiles of 8 tokens, 2 blocks x 2 k-steps ----
         float sc[4][2][4];
-        float kd[4][2][2], km[4][2][2];   // K (d, dmin) for tokens 8nt + 2tig + {0,1}
 #pragma unroll
         for (int nt = 0; nt < 4; ++nt) {
           const int tk = 8 * nt + g;
@@ -480,31 +510,18 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const Params p) {
             mma_f16(sc[nt][blk], qa[blk][0], nib2h<6>(w), nib2h<2>(w));
             mma_f16(sc[nt][blk], qa[blk][1], nib2h<-2>(w), nib2h<-6>(w));
           }
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int tt = 8 * nt + 2 * tig + e;
-            const uint32_t hr = kb + (tt >> 4) * PAGE_BYTES + (tt & 15) * ROWB;
-#pragma unroll
-            for (int blk = 0; blk < 2; ++blk) {
-              const float2 h = hdr2f(lds_u32(hr + blk * BLK));
-              kd[nt][blk][e] = h.x;
-              km[nt][blk][e] = h.y;
-            }
-          }
         }
         float sv[4][2];
 #pragma unroll
         for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            float acc = 0.f;
-#pragma unroll
-            for (int blk = 0; blk < 2; ++blk) {
-              const float dot = sc[nt][blk][e] + sc[nt][blk][2 + e];      // sum q (1 + n/16)
-              acc = fmaf(kd[nt][blk][e] * 16.0f, dot - qs[blk], acc);
-              acc = fmaf(km[nt][blk][e], qs[blk], acc);
-            }
-            const int pos = pos0 + 8 * nt + 2 * tig + e;
+            const int tt = 8 * nt + 2 * tig + e;
+            const float4 h = lds_f4(hd + tt * 32 + (((tt >> 2) & 1) << 4));   // a0, c0, a1, c1
+            const float t0 = sc[nt][0][e] + sc[nt][0][2 + e];            // sum q (1 + n/16), hi + lo rows
+            const float t1 = sc[nt][1][e] + sc[nt][1][2 + e];
+            const float acc = fmaf(h.x, t0, fmaf(h.z, t1, fmaf(h.y, qs[0], h.w * qs[1])));
+            const int pos = pos0 + tt;
             sv[nt][e] = (pos >= sb && pos < se) ? acc : -INFINITY;
           }
         // ---- online softmax ----
@@ -513,23 +530,28 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const Params p) {
         for (int nt = 0; nt < 4; ++nt) mx = fmaxf(mx, fmaxf(sv[nt][0], sv[nt][1]));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        const float mn = fmaxf(m, mx);
-        const float al = exp2f(m - mn);
+        // lazy rescale: the reference max m moves only when the chunk max passes it by
+        // more than 2 (log2 units), so p <= 4 and most chunks skip the rescale
+        if (mx > m + 2.0f) {
+          const float al = exp2f(m - mx);                               // m = -inf: 0
+          l *= al;
+#pragma unroll
+          for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) o[nt][j] *= al;
+          cb[0] *= al;
+          cb[1] *= al;
+          m = mx;
+        }
+        const float mref = m == -INFINITY ? 0.f : m;                    // all masked so far: p = 0
         float ps = 0.f;
 #pragma unroll
         for (int nt = 0; nt < 4; ++nt) {
-          sv[nt][0] = exp2f(sv[nt][0] - mn);
-          sv[nt][1] = exp2f(sv[nt][1] - mn);
+          sv[nt][0] = exp2f(sv[nt][0] - mref);
+          sv[nt][1] = exp2f(sv[nt][1] - mref);
           ps += sv[nt][0] + sv[nt][1];
         }
-        l = fmaf(l, al, ps);
-        m = mn;
-#pragma unroll
-        for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) o[nt][j] *= al;
-        cb[0] *= al;
-        cb[1] *= al;
+        l += ps;
         // ---- P'_blk = 16 p d_V (A operand), correction terms ----
         uint32_t pa[2][2][4];   // [blk][kt]
 #pragma unroll
@@ -540,14 +562,13 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const Params p) {
             const int nt = 2 * kt + (e >> 1);
             const int tt = 8 * nt + 2 * tig + (e & 1);
             const float pe = sv[nt][e & 1];
-            const uint32_t hr = kb + (tt >> 4) * PAGE_BYTES + PAGE * ROWB + (tt & 15) * ROWB;
-#pragma unroll
-            for (int blk = 0; blk < 2; ++blk) {
-              const float2 h = hdr2f(lds_u32(hr + blk * BLK));
-              // masked tokens (p = 0) may sit on stale bytes: keep their headers out
-              pv[blk][e] = pe > 0.f ? pe * h.x * 16.0f : 0.f;
-              if (pe > 0.f) cb[blk] = fmaf(pe, h.y - 16.0f * h.x, cb[blk]);
-            }
+            // 16 d_V and dmin_V - 16 d_V of both blocks (zero for masked tokens, whose
+            // stage bytes may be stale)
+            const float4 h = lds_f4(hd + tt * 32 + ((((tt >> 2) & 1) ^ 1) << 4));
+            pv[0][e] = pe * h.x;
+            pv[1][e] = pe * h.z;
+            cb[0] = fmaf(pe, h.y, cb[0]);
+            cb[1] = fmaf(pe, h.w, cb[1]);
           }
 #pragma unroll
           for (int blk = 0; blk < 2; ++blk) {
@@ -555,7 +576,6 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const Params p) {
             split_f16x2(pv[blk][2], pv[blk][3], pa[blk][kt][2], pa[blk][kt][3]);
           }
         }
-        __syncwarp();   // V tile rows written by all lanes
         // ---- O += P' V': k = 16 tokens, n-tiles of 8 (permuted) dims ----
 #pragma unroll
         for (int kt = 0; kt < 2; ++kt)
@@ -633,9 +653,122 @@ struct RingArgs {
   const int32_t* seq_lens; // [batch]
   int32_t ring_tokens, window;
   float qscale;            // scale * log2(e)
+  float* ring_part;        // [batch][H][HD + 2]: o (relative to m), m (log2), l of the ring tokens
 };
 
-constexpr int RING_MAX = 256;   // ring tokens folded into the reduce (larger rings: error)
+constexpr int RING_MAX = 128;   // ring tokens of one sequence (larger rings: error)
+
+// fp32 ring tokens [max(max(0, L - window), L - ring), L) of config 3 (slot pos %
+// ring): CTA = (sequence, KV head, 128-token part), all 8 query heads of the group.
+// Scores: thread = (token, half row): one batch of eight 16-byte K loads, dots for
+// the 8 heads against q in shared memory, halves joined by a shuffle.  Softmax:
+// warp = head.  P.V: thread = (dim pair, 16-token group): one batch of sixteen
+// 8-byte V loads, 8 heads accumulated, the 8 groups summed through shared memory.
+// Launched after the 4-bit decode with programmatic dependent launch: its CTAs
+// start as decode CTAs leave the SMs (its inputs are complete: the decode
+// releases it only after its own wait on the grid before it), and it waits for
+// the decode to complete before it exits, so the reduce that waits on it sees
+// both.  The reduce folds its partial in.
+__global__ void __launch_bounds__(256) ring_partial_kernel(const RingArgs ra) {
+  constexpr int TOK = 128;
+  __shared__ float qs[GROUP][HD];
+  __shared__ float ps[GROUP][TOK];
+  __shared__ float red[8][GROUP][HD];
+  __shared__ float mls[GROUP][2];
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int b = blockIdx.x / NKV, kvh = blockIdx.x % NKV;
+  const int t = threadIdx.x, w = t >> 5, lane = t & 31;
+  const int Ls = ra.seq_lens[b];
+  const int lo = max(max(0, Ls - ra.window), Ls - ra.ring_tokens);
+  const int n = min(max(0, Ls - lo), TOK);
+  const float* qb = ra.q + ((int64_t)b * NKV * GROUP + kvh * GROUP) * HD;
+  for (int i = t; i < GROUP * HD; i += 256) qs[i / HD][i % HD] = qb[i] * ra.qscale;
+  __syncthreads();
+  const float* kb = ra.ring + ((int64_t)(b * NKV + kvh) * 2 + 0) * ra.ring_tokens * HD;
+  const float* vb = ra.ring + ((int64_t)(b * NKV + kvh) * 2 + 1) * ra.ring_tokens * HD;
+  {
+    const int j = t >> 1, half = t & 1;
+    float acc[GROUP];
+#pragma unroll
+    for (int h = 0; h < GROUP; ++h) acc[h] = 0.f;
+    if (j < n) {
+      const float4* kr = reinterpret_cast<const float4*>(kb + (int64_t)((lo + j) % ra.ring_tokens) * HD + 32 * half);
+      float4 k[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) k[c] = __ldg(kr + c);
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+#pragma unroll
+        for (int h = 0; h < GROUP; ++h) {
+          const float* qq = &qs[h][32 * half + 4 * c];
+          acc[h] = fmaf(qq[0], k[c].x, fmaf(qq[1], k[c].y, fmaf(qq[2], k[c].z, fmaf(qq[3], k[c].w, acc[h]))));
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < GROUP; ++h) {
+      const float s = acc[h] + __shfl_xor_sync(0xffffffffu, acc[h], 1);
+      if (half == 0 && j < TOK) ps[h][j] = j < n ? s : -INFINITY;
+    }
+  }
+  __syncthreads();
+  {  // softmax of head w over the tokens
+    float mx = -INFINITY;
+    for (int j = lane; j < TOK; j += 32) mx = fmaxf(mx, ps[w][j]);
+    mx = warp_max(mx);
+    float l = 0.f;
+    for (int j = lane; j < TOK; j += 32) {
+      const float pe = mx > -INFINITY ? exp2f(ps[w][j] - mx) : 0.f;
+      ps[w][j] = pe;
+      l += pe;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      mls[w][0] = mx;
+      mls[w][1] = l;
+    }
+  }
+  __syncthreads();
+  {
+    const int dp = lane, tg = w;                 // dims 2dp, 2dp+1; tokens 16tg .. 16tg+15
+    float2 acc[GROUP];
+#pragma unroll
+    for (int h = 0; h < GROUP; ++h) acc[h] = make_float2(0.f, 0.f);
+    float2 v[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      const int j = 16 * tg + u;
+      v[u] = j < n ? __ldg(reinterpret_cast<const float2*>(vb + (int64_t)((lo + j) % ra.ring_tokens) * HD) + dp)
+                   : make_float2(0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < 16; ++u)
+#pragma unroll
+      for (int h = 0; h < GROUP; ++h) {
+        const float pe = ps[h][16 * tg + u];
+        acc[h].x = fmaf(pe, v[u].x, acc[h].x);
+        acc[h].y = fmaf(pe, v[u].y, acc[h].y);
+      }
+#pragma unroll
+    for (int h = 0; h < GROUP; ++h) {
+      red[tg][h][2 * dp] = acc[h].x;
+      red[tg][h][2 * dp + 1] = acc[h].y;
+    }
+  }
+  __syncthreads();
+  for (int i = t; i < GROUP * HD; i += 256) {
+    const int h = i / HD, d = i % HD;
+    float o = 0.f;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) o += red[g][h][d];
+    ra.ring_part[((int64_t)b * NKV * GROUP + kvh * GROUP + h) * (HD + 2) + d] = o;
+  }
+  if (t < GROUP) {
+    float* dst = ra.ring_part + ((int64_t)b * NKV * GROUP + kvh * GROUP + t) * (HD + 2);
+    dst[HD] = n > 0 ? mls[t][0] : -INFINITY;
+    dst[HD + 1] = n > 0 ? mls[t][1] : 0.f;
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");   // the decode before it has completed
+}
 
 // ---- split-KV exchange over peer memory ----------------------------------
 // Every rank owns a mailbox with the same layout.  A rank writes its partial
@@ -691,10 +824,7 @@ __global__ void __launch_bounds__(256) q4_reduce_kernel(const float* __restrict_
                                                        const RingArgs ra, const __grid_constant__ Exchange ex,
                                                        int32_t* err) {
   __shared__ float red[9][HD + 2];
-  __shared__ float qs_[HD];
-  __shared__ float sc_[RING_MAX];
-  __shared__ float pv_[4][HD];
-  __shared__ float lr_[4];
+  pdl_wait();
   const int row = blockIdx.x;                 // b * 32 + h
   const int b = row / (NKV * GROUP), h = row % (NKV * GROUP);
   const int kvh = h / GROUP, hh = h % GROUP;
@@ -734,48 +864,9 @@ __global__ void __launch_bounds__(256) q4_reduce_kernel(const float* __restrict_
   }
   int nparts = 8;
   if (ra.ring) {
-    // fp32 ring tokens [max(max(0, L - window), L - ring), L) at slot pos % ring
-    const int Ls = ra.seq_lens[b];
-    const int lo = max(max(0, Ls - ra.window), Ls - ra.ring_tokens), n = Ls - lo;
-    const int t = threadIdx.x;
-    if (t < HD) qs_[t] = ra.q[((int64_t)b * NKV * GROUP + h) * HD + t] * ra.qscale;
-    __syncthreads();
-    const float* kb = ra.ring + ((int64_t)(b * NKV + kvh) * 2 + 0) * ra.ring_tokens * HD;
-    const float* vb = ra.ring + ((int64_t)(b * NKV + kvh) * 2 + 1) * ra.ring_tokens * HD;
-    for (int j = t; j < n; j += 256) {
-      const float* kr = kb + (int64_t)((lo + j) % ra.ring_tokens) * HD;
-      float a = 0.f;
-#pragma unroll
-      for (int d = 0; d < HD; d += 4) {
-        const float4 kk = __ldg(reinterpret_cast<const float4*>(kr + d));
-        a = fmaf(qs_[d], kk.x, a); a = fmaf(qs_[d + 1], kk.y, a);
-        a = fmaf(qs_[d + 2], kk.z, a); a = fmaf(qs_[d + 3], kk.w, a);
-      }
-      sc_[j] = a;
-    }
-    __syncthreads();
-    float mr = -INFINITY;
-    for (int j = lane; j < n; j += 32) mr = fmaxf(mr, sc_[j]);
-    mr = warp_max(mr);
-    // 4 token quarters x 64 dims
-    const int dq = t & 63, qq = t >> 6;
-    float acc = 0.f, lr = 0.f;
-    for (int j = qq; j < n; j += 4) {
-      const float pe = exp2f(sc_[j] - mr);
-      lr += pe;
-      acc = fmaf(pe, __ldg(vb + (int64_t)((lo + j) % ra.ring_tokens) * HD + dq), acc);
-    }
-    pv_[qq][dq] = acc;
-    if (dq == 0) lr_[qq] = lr;
-    __syncthreads();
-    if (t < HD) {
-      red[8][t] = pv_[0][t] + pv_[1][t] + pv_[2][t] + pv_[3][t];
-      if (t == 0) {
-        const float lsum = lr_[0] + lr_[1] + lr_[2] + lr_[3];
-        red[8][HD] = n > 0 ? mr : -INFINITY;
-        red[8][HD + 1] = n > 0 ? lsum : 0.f;
-      }
-    }
+    // the ring tokens' partial (ring_partial_kernel) as a ninth part
+    const float* src = ra.ring_part + (int64_t)row * (HD + 2);
+    if (threadIdx.x < HD + 2) red[8][threadIdx.x] = src[threadIdx.x];
     nparts = 9;
   }
   __syncthreads();
@@ -909,7 +1000,9 @@ __global__ void lse_combine_kernel(const float* __restrict__ parts, int G, int64
   *reinterpret_cast<float4*>(out + r * HD + d4) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
 }
 
-size_t smem_bytes() { return sizeof(Smem) + 1024; }
+size_t smem_bytes() { return sizeof(Smem) + 128; }
+// two CTAs per SM: 2 x (dynamic + 1 KB reserved) within the 228 KB of an SM
+static_assert(sizeof(Smem) + 128 + 1024 <= 114 * 1024, "decode_q4 shared memory must allow 2 CTAs per SM");
 
 struct WsLayout {
   size_t meta, cta_part, total;
@@ -969,20 +1062,25 @@ int32_t launch_partial(Params base, int batch, const int32_t* tok_begin, const i
     p.meta = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws) + w.meta);
     p.cta_part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + w.cta_part);
     p.err = dev->err_word;
-    decode_q4_kernel<<<grid_cache[di], THREADS, smem, stream>>>(p);
-    st = check_cuda(cudaGetLastError(), "decode_q4 launch");
+    st = check_cuda(launch_pdl(decode_q4_kernel, dim3(grid_cache[di]), dim3(THREADS), smem, stream, p),
+                    "decode_q4 launch");
     if (st) return st;
     RingArgs r = ra;
     if (r.ring) {
       r.q = q + (int64_t)b0 * NKV * GROUP * HD;
       r.ring = ra.ring + (int64_t)b0 * NKV * 2 * ra.ring_tokens * HD;
       r.seq_lens = ra.seq_lens + b0;
+      r.ring_part = ra.ring_part + (int64_t)b0 * NKV * GROUP * (HD + 2);
+      st = check_cuda(launch_pdl(ring_partial_kernel, dim3(nb * NKV), dim3(256), 0, stream, r), "ring_partial launch");
+      if (st) return st;
     }
     p.seq_lens = base.seq_lens ? base.seq_lens + b0 : nullptr;
-    q4_reduce_kernel<<<nb * NKV * GROUP, 256, 0, stream>>>(p.cta_part, p.meta, nb, p.part,
-                                                            final_out ? final_out + (int64_t)b0 * NKV * GROUP * HD : nullptr,
-                                                            r, ex, dev->err_word);
-    st = check_cuda(cudaGetLastError(), "q4_reduce launch");
+    float* fo = final_out ? final_out + (int64_t)b0 * NKV * GROUP * HD : nullptr;
+    const float* cp = p.cta_part;
+    const int32_t* mt = p.meta;
+    st = check_cuda(launch_pdl(q4_reduce_kernel, dim3(nb * NKV * GROUP), dim3(256), 0, stream, cp, mt, nb, p.part,
+                               fo, r, ex, dev->err_word),
+                    "q4_reduce launch");
     if (st) return st;
   }
   return NYION_OK;
@@ -1112,6 +1210,7 @@ extern "C" int32_t nyion_attn_decode_q4_window_ring(
   ra.ring_tokens = ring_tokens;
   ra.window = window;
   ra.qscale = p.qscale;
+  ra.ring_part = parts + rows * (HD + 2);
   return launch_partial(p, batch, nullptr, nullptr, q, parts, page_table, w, s, out, ra);
 }
 

@@ -48,6 +48,26 @@ enum WsKind { kWsScratch = 0, kWsCounters = 1, kWsKinds = 2 };
 int32_t internal_workspace(size_t bytes, void** ptr, WsKind kind = kWsScratch, size_t zero_prefix = 0,
                            cudaStream_t stream = nullptr);
 
+// Launch with programmatic dependent launch allowed: the grid may be scheduled
+// while the previous grid in the stream runs; the kernel itself calls
+// griddepcontrol.wait (pdl_wait) before it touches global memory that grid
+// may write.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
 // Whole-page fp32 paged decode for 4 KV heads (decode_pages.cu): workspace
 // bytes for `batch` sequences, and the launch (workspace zeroed once, left
 // with its counters at zero).
