@@ -452,18 +452,39 @@ def run_gpu(args, rank, world):
 
     # ---- end to end through the public API: pinned host Q in, host O out ----
     # Every step copies that step's Q (all layers) from pinned host memory and
-    # reads every layer's output back; the copies and calls are captured in a
-    # CUDA graph like the device-only leg (an eager Python loop is reported
-    # beside it).
+    # reads every layer's output back.  The copies run on their own streams and
+    # overlap the decode (layer l waits only for its own Q; layer l's output
+    # is read back while layer l + 1 decodes); the step ends when the last
+    # output is on the host.  Captured in a CUDA graph like the device-only leg
+    # (an eager Python loop is reported beside it).
     qh = q.cpu().pin_memory()
     oh = torch.empty_like(qh).pin_memory()
     qd = torch.empty_like(q)
+    h2d, d2h = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
 
     def e2e_step(s):
+        start = torch.cuda.Event()
+        start.record(s)
+        h2d.wait_event(start)
+        d2h.wait_event(start)
+        q_ready = []
+        with torch.cuda.stream(h2d):
+            for l in range(LAYERS):
+                qd[l].copy_(qh[l], non_blocking=True)
+                e = torch.cuda.Event()
+                e.record(h2d)
+                q_ready.append(e)
         for l in range(LAYERS):
-            qd[l].copy_(qh[l], non_blocking=True)
+            s.wait_event(q_ready[l])
             A.decode_paged_f32(qd[l], pool, tables[l], lens, out=out[l], workspace=ws, stream=s)
-            oh[l].copy_(out[l], non_blocking=True)
+            done = torch.cuda.Event()
+            done.record(s)
+            d2h.wait_event(done)
+            with torch.cuda.stream(d2h):
+                oh[l].copy_(out[l], non_blocking=True)
+        end = torch.cuda.Event()
+        end.record(d2h)
+        s.wait_event(end)
 
     def timed(fn):
         with torch.cuda.stream(stream):
