@@ -22,7 +22,8 @@
 //     shared memory at the end;
 //   * warps 8 and 10 copy K and V pages (TMA, 6-stage ring; page ids read a
 //     block of 32 ahead), warp 9 allocates TMEM and one of its threads issues
-//     the MMAs with a single commit per tile (a commit stalls the tensor pipe);
+//     the MMAs: S(j+2) as soon as group j%2 has read S(j) out of TMEM, PV(j)
+//     as soon as P(j) is written, polling both so the two groups overlap;
 //     the softmax group that consumed a tile releases its ring stage.
 //     Every wait is bounded; TMEM is released on every path.
 #include <cuda_bf16.h>
@@ -53,7 +54,8 @@ struct Smem {
   uint8_t k[STAGES][BN * ROWB];  // K tiles, 16 KB each
   uint8_t v[STAGES][BN * ROWB];  // V tiles, 16 KB each
   uint64_t q_full, kv_full[STAGES], kv_empty[STAGES], done;
-  uint64_t ready[2], p_full[2];   // per softmax group
+  // per softmax group: S(j) written | S(j) read out | P(j) written | PV(j) retired
+  uint64_t s_ready[2], s_free[2], p_full[2], pv_done[2];
   uint32_t tmem_base;
   int32_t abort_;
 };
@@ -255,8 +257,10 @@ prefill_kernel(const Params p, const __grid_constant__ CUtensorMap map_q,
       mbar_init(&s.kv_empty[i], 1);
     }
     for (int g = 0; g < 2; ++g) {
-      mbar_init(&s.ready[g], 1);
+      mbar_init(&s.s_ready[g], 1);
+      mbar_init(&s.s_free[g], 4);
       mbar_init(&s.p_full[g], 128);
+      mbar_init(&s.pv_done[g], 1);
     }
     mbar_init(&s.done, 1);
     s.abort_ = 0;
@@ -346,30 +350,56 @@ prefill_kernel(const Params p, const __grid_constant__ CUtensorMap map_q,
           umma(tmem + S_COL + 128 * (j & 1), smem_desc(qa + ks * 32, 16, 1024), smem_desc(kb + ks * 32, 16, 1024),
                IQK, ks > 0);
       };
-      // one commit per tile (a commit stalls the tensor pipe): ready[g]
-      // completes when S(j+2) is written and PV(j) has retired
+      // S(j+2) is computed as soon as group g has read S(j) out of TMEM, and
+      // PV(j) as soon as P(j) is written, whichever comes first: the issuer
+      // polls both (QK in tile order, PV in tile order), so the two softmax
+      // groups work at the same time.  Two commits per tile: s_ready[g] (S
+      // written) and pv_done[g] (PV retired).  A group is never more than one
+      // phase ahead of a poll here.  The poll is bounded like every wait.
       wait(&s.q_full, 0);
       for (int j = 0; j < 2 && j < nt; ++j) {
         wait(&s.kv_full[j], 0);
         tc_fence_after();
         issue_qk(j);
-        umma_commit(&s.ready[j]);
+        umma_commit(&s.s_ready[j]);
       }
-      for (int j = 0; j < nt; ++j) {
-        const int g = j & 1;
-        wait(&s.p_full[g], (uint32_t)((j >> 1) & 1));   // P(j) written, S(j) consumed
-        tc_fence_after();
-        const uint32_t vb = smem_u32(s.v[j % STAGES]);
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)
-          umma_ts(tmem + O_COL + 64 * g, tmem + P_COL + 64 * g + 8 * kk, smem_desc(vb + kk * 2048, 8192, 1024),
-                  IPV, (kk > 0 || j >= 2) ? 1u : 0u);
-        if (j + 2 < nt) {
-          wait(&s.kv_full[(j + 2) % STAGES], (uint32_t)(((j + 2) / STAGES) & 1));
-          tc_fence_after();
-          issue_qk(j + 2);
+      int qn = 2, pn = 0;                                // next tile for QK / for PV
+      uint32_t idle = 0;
+      while (pn < nt && !*reinterpret_cast<volatile int32_t*>(&s.abort_)) {
+        bool progress = false;
+        if (qn < nt) {
+          const int g = qn & 1;
+          if (mbar_try_wait(&s.s_free[g], (uint32_t)(((qn - 2) >> 1) & 1)) &&
+              mbar_try_wait(&s.kv_full[qn % STAGES], (uint32_t)((qn / STAGES) & 1))) {
+            tc_fence_after();
+            issue_qk(qn);
+            umma_commit(&s.s_ready[g]);
+            ++qn;
+            progress = true;
+          }
         }
-        umma_commit(&s.ready[g]);
+        {
+          const int g = pn & 1;
+          if (mbar_try_wait(&s.p_full[g], (uint32_t)((pn >> 1) & 1))) {
+            tc_fence_after();
+            const uint32_t vb = smem_u32(s.v[pn % STAGES]);
+#pragma unroll
+            for (int kk = 0; kk < BN / 16; ++kk)
+              umma_ts(tmem + O_COL + 64 * g, tmem + P_COL + 64 * g + 8 * kk,
+                      smem_desc(vb + kk * 2048, 8192, 1024), IPV, (kk > 0 || pn >= 2) ? 1u : 0u);
+            umma_commit(&s.pv_done[g]);
+            ++pn;
+            progress = true;
+          }
+        }
+        if (progress) {
+          idle = 0;
+        } else if (++idle > kSpinLimit) {
+          record_error(p.err, kErrWaitTimeout);
+          atomicExch(&s.abort_, 1);
+        } else if (idle > 64) {
+          __nanosleep(32);
+        }
       }
       umma_commit(&s.done);
       mbar_wait_bounded(&s.done, 0);   // every MMA has retired before TMEM is released
@@ -390,15 +420,18 @@ prefill_kernel(const Params p, const __grid_constant__ CUtensorMap map_q,
     float m = -INFINITY, l = 0.f;
     int i = 0;
     for (int j = g; j < nt; j += 2, ++i) {
-      wait(&s.ready[g], (uint32_t)(i & 1));           // S(j) written, PV(j-2) retired
+      wait(&s.s_ready[g], (uint32_t)(i & 1));         // S(j) written
       __syncwarp();                                   // tcgen05.ld is warp-collective
       tc_fence_after();
-      if (j >= 2 && r == 0) mbar_arrive(&s.kv_empty[(j - 2) % STAGES]);   // tile j-2's K/V stage
       float sv[BN];
 #pragma unroll
       for (int q = 0; q < BN / 32; ++q) tmem_ld32(s_addr + 32 * q, *reinterpret_cast<float(*)[32]>(&sv[32 * q]));
 #pragma unroll
       for (int q = 0; q < BN / 32; ++q) tmem_wait_ld32(*reinterpret_cast<float(*)[32]>(&sv[32 * q]));
+      // S(j) is in registers: its TMEM columns may take S(j+2) now
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.s_free[g]);
       // causal mask (token <= position) on tiles that cross this M tile's diagonal
       const int64_t t0 = (int64_t)j * BN;
       if (t0 + BN - 1 > pos0) {
@@ -423,7 +456,13 @@ prefill_kernel(const Params p, const __grid_constant__ CUtensorMap map_q,
       }
       const float mref = (m == -INFINITY) ? 0.f : m;  // a row with nothing visible yet: P = 0
       if (i > 0) {
-        // PV of this group's previous tile has retired: O may be rescaled
+        // PV of this group's previous tile has retired (issued a whole tile ago):
+        // its P and O columns are free, O may be rescaled, and that tile's K/V
+        // stage goes back
+        wait(&s.pv_done[g], (uint32_t)((i - 1) & 1));
+        __syncwarp();
+        tc_fence_after();
+        if (r == 0) mbar_arrive(&s.kv_empty[(j - 2) % STAGES]);
         if (__any_sync(0xffffffffu, need)) {
 #pragma unroll 1
           for (int q = 0; q < HD / 16; ++q) {
@@ -469,7 +508,7 @@ prefill_kernel(const Params p, const __grid_constant__ CUtensorMap map_q,
       mbar_arrive(&s.p_full[g]);
     }
     if (i > 0) {
-      wait(&s.ready[g], (uint32_t)(i & 1));           // the group's last PV has retired
+      wait(&s.pv_done[g], (uint32_t)((i - 1) & 1));   // the group's last PV has retired
       __syncwarp();
       tc_fence_after();
     }
