@@ -455,10 +455,28 @@ prefill_kernel(const Params p, const __grid_constant__ CUtensorMap map_q,
         l *= alpha;
       }
       const float mref = (m == -INFINITY) ? 0.f : m;  // a row with nothing visible yet: P = 0
+      // P row r as bf16 pairs (token 2c in the low half of column c).  The first
+      // half is computed before waiting for PV(j-2) (whose P columns it
+      // overwrites), so the exponentials overlap that MMA.
+      const float2 sl2v = make_float2(p.sl2, p.sl2), negm = make_float2(-mref, -mref);
+      float2 acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      auto p_words = [&](int c16, uint32_t (&w)[8]) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          float2 x = __ffma2_rn(make_float2(sv[16 * c16 + 2 * e], sv[16 * c16 + 2 * e + 1]), sl2v, negm);
+          x.x = ex2(x.x);
+          x.y = ex2(x.y);
+          acc[e & 1] = __fadd2_rn(acc[e & 1], x);
+          const __nv_bfloat162 h2 = __floats2bfloat162_rn(x.x, x.y);
+          w[e] = *reinterpret_cast<const uint32_t*>(&h2);
+        }
+      };
+      uint32_t first[4][8];
+#pragma unroll
+      for (int c16 = 0; c16 < 4; ++c16) p_words(c16, first[c16]);
       if (i > 0) {
-        // PV of this group's previous tile has retired (issued a whole tile ago):
-        // its P and O columns are free, O may be rescaled, and that tile's K/V
-        // stage goes back
+        // PV of this group's previous tile has retired: its P and O columns are
+        // free, O may be rescaled, and that tile's K/V stage goes back
         wait(&s.pv_done[g], (uint32_t)((i - 1) & 1));
         __syncwarp();
         tc_fence_after();
@@ -475,26 +493,15 @@ prefill_kernel(const Params p, const __grid_constant__ CUtensorMap map_q,
           }
         }
       }
-      // P row r -> TMEM as bf16 pairs (token 2c in the low half of column c)
-      {
-        const float2 sl2v = make_float2(p.sl2, p.sl2), negm = make_float2(-mref, -mref);
-        float2 acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-        for (int c16 = 0; c16 < BN / 16; ++c16) {
-          uint32_t w[8];
+      for (int c16 = 0; c16 < 4; ++c16) tmem_st8(p_addr + 8 * c16, first[c16]);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            float2 x = __ffma2_rn(make_float2(sv[16 * c16 + 2 * e], sv[16 * c16 + 2 * e + 1]), sl2v, negm);
-            x.x = ex2(x.x);
-            x.y = ex2(x.y);
-            acc[e & 1] = __fadd2_rn(acc[e & 1], x);
-            const __nv_bfloat162 h2 = __floats2bfloat162_rn(x.x, x.y);
-            w[e] = *reinterpret_cast<const uint32_t*>(&h2);
-          }
-          tmem_st8(p_addr + 8 * c16, w);
-        }
-        l += (acc[0].x + acc[0].y) + (acc[1].x + acc[1].y);
+      for (int c16 = 4; c16 < BN / 16; ++c16) {
+        uint32_t w[8];
+        p_words(c16, w);
+        tmem_st8(p_addr + 8 * c16, w);
       }
+      l += (acc[0].x + acc[0].y) + (acc[1].x + acc[1].y);
       tmem_wait_st();
       // V rows past the visible tokens may hold anything: zero them (P is 0 there)
       if (t0 + BN > kv_len && t0 + r >= kv_len) {
