@@ -260,6 +260,48 @@ def timed_graph(torch, fn, stream, steps, warmup, barrier, dist=None, world=1, d
     return ms, mode
 
 
+def run_config1(A, torch, dev, stream, args, barrier, dist, world, with_cpu):
+    """Config 1: one layer, B=1, ctx 128, fp32 N(0,1) seed 0 in the reference's
+    zone-page layout (4 pages of 32 slots); ops::attention through
+    nyion_attn_decode_zoned_f32.  Latency-bound: microseconds per call."""
+    ctx, slots = 128, 32
+    gen = torch.Generator(device=dev).manual_seed(0)
+    pages = ctx // slots
+    k = torch.randn(pages * N_KV * slots * D, device=dev, generator=gen)
+    v = torch.randn(pages * N_KV * slots * D, device=dev, generator=gen)
+    q = torch.randn(H, D, device=dev, generator=gen)
+    out = torch.empty_like(q)
+    calls = 22   # one call per layer of a 22-layer step, captured together like config 2
+
+    def fn():
+        for _ in range(calls):
+            A.decode_zoned_f32(q, k, v, 1, 0, ctx, ctx - 1, out=out, stream=stream)
+
+    ms, mode = timed_graph(torch, fn, stream, max(args.steps, 20), args.warmup, barrier, dist, world, dev)
+    r = {"workload": "config1: 1 layer, B=1, ctx 128, reference zone-page layout", "us_per_call": ms * 1e3 / calls,
+         "timing": f"{mode} of {calls} calls", "launches_per_step": 1}
+    if with_cpu:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O   # CPU baseline leg only
+        zp = O.ZonedPages(1, N_KV, D, ctx)
+        kh = k.view(pages, N_KV, slots, D).cpu().numpy()
+        vh = v.view(pages, N_KV, slots, D).cpu().numpy()
+        zp.ensure_f32(pages - 1)
+        for pid in range(pages):
+            zp.k_f32[pid][:] = kh[pid].reshape(-1)
+            zp.v_f32[pid][:] = vh[pid].reshape(-1)
+        qh = q.cpu().numpy()
+        ref = O.attention(zp, qh, 0, ctx, ctx - 1, H)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 0.5:
+            O.attention(zp, qh, 0, ctx, ctx - 1, H)
+            n += 1
+        r["cpu_oracle_us_per_call"] = (time.perf_counter() - t0) / n * 1e6
+        torch.cuda.synchronize()
+        r["max_abs_vs_oracle"] = float(abs(out.cpu().numpy() - ref).max())
+    return r
+
+
 def run_config3(A, torch, dev, stream, args, barrier, dist, world):
     """Config 3: B=16, window 4096 of 65536, fp32 ring of the last 128 tokens."""
     B, L, W, R = 16, 65536, 4096, 128
@@ -526,6 +568,8 @@ def run_gpu(args, rank, world):
         torch.cuda.empty_cache()
         S = sys.modules.get("nyion_rs_b200.splitkv") or __import__("nyion_rs_b200.splitkv", fromlist=["x"])
         if world == 1:
+            extra["reference_layout_128"] = run_config1(A, torch, dev, stream, args, barrier, dist, world,
+                                                        not args.no_cpu)
             extra["q4_window_ring"] = run_config3(A, torch, dev, stream, args, barrier, dist, world)
             extra["prefill_2048"] = run_config4(A, torch, dev, stream, args)
         extra["split_kv_1m"] = run_config5(A, S, torch, dev, stream, args, barrier, dist, world, rank)

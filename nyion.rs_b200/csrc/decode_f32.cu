@@ -684,6 +684,100 @@ int32_t check_common(int32_t n_heads, int32_t n_kv_heads, int32_t head_dim) {
   return NYION_OK;
 }
 
+// ---- short contexts in the zone layout (ops::attention at <= 256 tokens) ----
+// The executor's Full strategy runs up to 512 tokens and config 1 is 128: a
+// one-launch kernel with no split-KV merge.  CTA = KV head, 256 threads.
+// Scores: thread = token (its 256-byte K row in one batch of 16-byte loads),
+// dots for the 8 query heads against q in shared memory.  Softmax: warp =
+// head.  P.V: thread = (dim pair, 32-token group), all 32 V loads in flight,
+// the 8 groups summed through shared memory.  Tokens < 256 all sit in zone 0
+// (pages of 32 slots, [layer][kv head][slot][64] per page).
+constexpr int SMALL_TOK = 256;
+
+__global__ void __launch_bounds__(256) zoned_small_kernel(const float* __restrict__ q, const float* __restrict__ k_arena,
+                                                          const float* __restrict__ v_arena, float* __restrict__ out,
+                                                          int n, int n_layers, int layer, int n_kv, float sl2) {
+  __shared__ float qs[GROUP][HD];
+  __shared__ float ps[GROUP][SMALL_TOK];
+  __shared__ float red[8][GROUP][HD];
+  __shared__ float ls[GROUP];
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int kvh = blockIdx.x, t = threadIdx.x, w = t >> 5, lane = t & 31;
+  for (int i = t; i < GROUP * HD; i += 256) qs[i / HD][i % HD] = q[(int64_t)kvh * GROUP * HD + i] * sl2;
+  __syncthreads();
+  const int64_t lp = (int64_t)n_layers * n_kv;
+  auto row = [&](int tok) { return ((int64_t)(tok >> 5) * lp * 32 + ((int64_t)layer * n_kv + kvh) * 32 + (tok & 31)) * HD; };
+  {
+    float acc[GROUP];
+#pragma unroll
+    for (int h = 0; h < GROUP; ++h) acc[h] = 0.f;
+    if (t < n) {
+      const float4* kr = reinterpret_cast<const float4*>(k_arena + row(t));
+      float4 kk[HD / 4];
+#pragma unroll
+      for (int c = 0; c < HD / 4; ++c) kk[c] = __ldg(kr + c);
+#pragma unroll
+      for (int c = 0; c < HD / 4; ++c)
+#pragma unroll
+        for (int h = 0; h < GROUP; ++h) {
+          const float* qq = &qs[h][4 * c];
+          acc[h] = fmaf(qq[0], kk[c].x, fmaf(qq[1], kk[c].y, fmaf(qq[2], kk[c].z, fmaf(qq[3], kk[c].w, acc[h]))));
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < GROUP; ++h) ps[h][t] = t < n ? acc[h] : -INFINITY;
+  }
+  __syncthreads();
+  {
+    float mx = -INFINITY;
+    for (int j = lane; j < SMALL_TOK; j += 32) mx = fmaxf(mx, ps[w][j]);
+    mx = warp_max(mx);
+    float l = 0.f;
+    for (int j = lane; j < SMALL_TOK; j += 32) {
+      const float pe = exp2f(ps[w][j] - mx);
+      ps[w][j] = pe;
+      l += pe;
+    }
+    l = warp_sum(l);
+    if (lane == 0) ls[w] = l;
+  }
+  __syncthreads();
+  {
+    const int dp = lane, tg = w;                      // dims 2dp, 2dp+1; tokens 32 tg .. 32 tg + 31
+    float2 acc[GROUP];
+#pragma unroll
+    for (int h = 0; h < GROUP; ++h) acc[h] = make_float2(0.f, 0.f);
+    float2 vv[32];
+#pragma unroll
+    for (int u = 0; u < 32; ++u) {
+      const int j = 32 * tg + u;
+      vv[u] = j < n ? __ldg(reinterpret_cast<const float2*>(v_arena + row(j)) + dp) : make_float2(0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < 32; ++u)
+#pragma unroll
+      for (int h = 0; h < GROUP; ++h) {
+        const float pe = ps[h][32 * tg + u];
+        acc[h].x = fmaf(pe, vv[u].x, acc[h].x);
+        acc[h].y = fmaf(pe, vv[u].y, acc[h].y);
+      }
+#pragma unroll
+    for (int h = 0; h < GROUP; ++h) {
+      red[tg][h][2 * dp] = acc[h].x;
+      red[tg][h][2 * dp + 1] = acc[h].y;
+    }
+  }
+  __syncthreads();
+  for (int i = t; i < GROUP * HD; i += 256) {
+    const int h = i / HD, d = i % HD;
+    float o = 0.f;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) o += red[g][h][d];
+    out[((int64_t)kvh * GROUP + h) * HD + d] = o / ls[h];
+  }
+}
+
 }  // namespace f32dec
 }  // namespace nyion
 
@@ -758,6 +852,18 @@ extern "C" int32_t nyion_attn_decode_zoned_f32(float* out, const float* q, const
   // ops.rs:183 valid_end = min(q_pos, seq_len - 1): tokens [0, valid_end] are attended
   int64_t valid_end = q_pos < seq_len - 1 ? q_pos : seq_len - 1;
   if (valid_end + 1 > (1ll << 30)) return fail(NYION_ERR_INVALID, "decode_zoned_f32: context too long");
+  if (valid_end + 1 <= SMALL_TOK) {
+    // short context: one launch, all pages in zone 0
+    const int64_t pages = (valid_end + 1 + 31) / 32;
+    if (pages > n_arena_pages)
+      return fail(NYION_ERR_INVALID, "decode_zoned_f32: %lld tokens need %lld pages, the arena has %lld",
+                  (long long)(valid_end + 1), (long long)pages, (long long)n_arena_pages);
+    const float sl2 = (1.0f / sqrtf((float)head_dim)) * 1.4426950408889634f;
+    return check_cuda(launch_pdl(zoned_small_kernel, dim3((unsigned)n_kv_heads), dim3(256), 0,
+                                 static_cast<cudaStream_t>(stream), q, k_arena, v_arena, out,
+                                 (int)(valid_end + 1), (int)n_layers, (int)layer_idx, (int)n_kv_heads, sl2),
+                      "decode_zoned_f32 small launch");
+  }
   // rows in the arena: zone pages [0, n_arena_pages) of 32 / 128 / 1024 slots
   const int64_t lp = (int64_t)n_layers * n_kv_heads;
   int64_t z0 = n_arena_pages < 128 ? n_arena_pages : 128;
