@@ -684,21 +684,26 @@ int32_t check_common(int32_t n_heads, int32_t n_kv_heads, int32_t head_dim) {
   return NYION_OK;
 }
 
-// ---- short contexts in the zone layout (ops::attention at <= 256 tokens) ----
+// ---- short contexts in the zone layout (ops::attention at <= 512 tokens) ----
 // The executor's Full strategy runs up to 512 tokens and config 1 is 128: a
 // one-launch kernel with no split-KV merge.  CTA = KV head, 256 threads.
-// Scores: thread = token (its 256-byte K row in one batch of 16-byte loads),
-// dots for the 8 query heads against q in shared memory.  Softmax: warp =
-// head.  P.V: thread = (dim pair, 32-token group), all 32 V loads in flight,
-// the 8 groups summed through shared memory.  Tokens < 256 all sit in zone 0
-// (pages of 32 slots, [layer][kv head][slot][64] per page).
-constexpr int SMALL_TOK = 256;
+// Scores: thread = token (its 256-byte K row in one batch of 16-byte loads,
+// two rounds above 256 tokens), dots for the 8 query heads against q in shared
+// memory.  Softmax: warp = head.  P.V: thread = (dim pair, token group), 32
+// V loads in flight per round, the 8 groups summed through shared memory.
+// With `importance` (ops::attention_tracked) each token's weights of the 8
+// heads are added to importance[t] (double atomics: the 4 KV-head CTAs).
+// Tokens < 4096 all sit in zone 0 (pages of 32 slots, [layer][kv head][slot]
+// [64] per page).
+constexpr int SMALL_TOK = 512;
 
+template <int MAXT>
 __global__ void __launch_bounds__(256) zoned_small_kernel(const float* __restrict__ q, const float* __restrict__ k_arena,
                                                           const float* __restrict__ v_arena, float* __restrict__ out,
-                                                          int n, int n_layers, int layer, int n_kv, float sl2) {
+                                                          double* __restrict__ importance, int n, int n_layers,
+                                                          int layer, int n_kv, float sl2) {
   __shared__ float qs[GROUP][HD];
-  __shared__ float ps[GROUP][SMALL_TOK];
+  __shared__ float ps[GROUP][MAXT];
   __shared__ float red[8][GROUP][HD];
   __shared__ float ls[GROUP];
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -708,12 +713,12 @@ __global__ void __launch_bounds__(256) zoned_small_kernel(const float* __restric
   __syncthreads();
   const int64_t lp = (int64_t)n_layers * n_kv;
   auto row = [&](int tok) { return ((int64_t)(tok >> 5) * lp * 32 + ((int64_t)layer * n_kv + kvh) * 32 + (tok & 31)) * HD; };
-  {
+  for (int tok = t; tok < MAXT; tok += 256) {
     float acc[GROUP];
 #pragma unroll
     for (int h = 0; h < GROUP; ++h) acc[h] = 0.f;
-    if (t < n) {
-      const float4* kr = reinterpret_cast<const float4*>(k_arena + row(t));
+    if (tok < n) {
+      const float4* kr = reinterpret_cast<const float4*>(k_arena + row(tok));
       float4 kk[HD / 4];
 #pragma unroll
       for (int c = 0; c < HD / 4; ++c) kk[c] = __ldg(kr + c);
@@ -726,15 +731,15 @@ __global__ void __launch_bounds__(256) zoned_small_kernel(const float* __restric
         }
     }
 #pragma unroll
-    for (int h = 0; h < GROUP; ++h) ps[h][t] = t < n ? acc[h] : -INFINITY;
+    for (int h = 0; h < GROUP; ++h) ps[h][tok] = tok < n ? acc[h] : -INFINITY;
   }
   __syncthreads();
   {
     float mx = -INFINITY;
-    for (int j = lane; j < SMALL_TOK; j += 32) mx = fmaxf(mx, ps[w][j]);
+    for (int j = lane; j < MAXT; j += 32) mx = fmaxf(mx, ps[w][j]);
     mx = warp_max(mx);
     float l = 0.f;
-    for (int j = lane; j < SMALL_TOK; j += 32) {
+    for (int j = lane; j < MAXT; j += 32) {
       const float pe = exp2f(ps[w][j] - mx);
       ps[w][j] = pe;
       l += pe;
@@ -743,25 +748,41 @@ __global__ void __launch_bounds__(256) zoned_small_kernel(const float* __restric
     if (lane == 0) ls[w] = l;
   }
   __syncthreads();
+  if (importance) {
+    for (int tok = t; tok < n; tok += 256) {
+      double a = 0.0;
+#pragma unroll
+      for (int h = 0; h < GROUP; ++h) a += (double)(ps[h][tok] * (1.0f / ls[h]));
+      atomicAdd(importance + tok, a);
+    }
+  }
   {
-    const int dp = lane, tg = w;                      // dims 2dp, 2dp+1; tokens 32 tg .. 32 tg + 31
+    const int dp = lane, tg = w;                      // dims 2dp, 2dp+1; tokens tg * n_per .. + n_per
+    const int n_per = MAXT <= 256 ? 32 : (n + 7) / 8;
     float2 acc[GROUP];
 #pragma unroll
     for (int h = 0; h < GROUP; ++h) acc[h] = make_float2(0.f, 0.f);
-    float2 vv[32];
+    for (int u0 = 0; u0 < n_per; u0 += 32) {
+      float2 vv[32];
 #pragma unroll
-    for (int u = 0; u < 32; ++u) {
-      const int j = 32 * tg + u;
-      vv[u] = j < n ? __ldg(reinterpret_cast<const float2*>(v_arena + row(j)) + dp) : make_float2(0.f, 0.f);
-    }
-#pragma unroll
-    for (int u = 0; u < 32; ++u)
-#pragma unroll
-      for (int h = 0; h < GROUP; ++h) {
-        const float pe = ps[h][32 * tg + u];
-        acc[h].x = fmaf(pe, vv[u].x, acc[h].x);
-        acc[h].y = fmaf(pe, vv[u].y, acc[h].y);
+      for (int u = 0; u < 32; ++u) {
+        const int j = tg * n_per + u0 + u;
+        vv[u] = (u0 + u < n_per && j < n) ? __ldg(reinterpret_cast<const float2*>(v_arena + row(j)) + dp)
+                                          : make_float2(0.f, 0.f);
       }
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        const int j = tg * n_per + u0 + u;
+        if (u0 + u < n_per && j < n) {
+#pragma unroll
+          for (int h = 0; h < GROUP; ++h) {
+            const float pe = ps[h][j];
+            acc[h].x = fmaf(pe, vv[u].x, acc[h].x);
+            acc[h].y = fmaf(pe, vv[u].y, acc[h].y);
+          }
+        }
+      }
+    }
 #pragma unroll
     for (int h = 0; h < GROUP; ++h) {
       red[tg][h][2 * dp] = acc[h].x;
@@ -836,6 +857,25 @@ extern "C" int32_t nyion_attn_decode_paged_f32(const float* q, const float* kv_p
                        static_cast<cudaStream_t>(stream));
 }
 
+namespace nyion {
+int64_t zoned_small_max() { return f32dec::SMALL_TOK; }
+
+int32_t zoned_small(float* out, const float* q, const float* k_arena, const float* v_arena, int64_t n_arena_pages,
+                    int32_t n_layers, int32_t layer_idx, int64_t n_tokens, int32_t n_kv_heads, int32_t head_dim,
+                    double* importance, void* stream) {
+  const int64_t pages = (n_tokens + 31) / 32;
+  if (pages > n_arena_pages)
+    return fail(NYION_ERR_INVALID, "decode_zoned_f32: %lld tokens need %lld pages, the arena has %lld",
+                (long long)n_tokens, (long long)pages, (long long)n_arena_pages);
+  const float sl2 = (1.0f / sqrtf((float)head_dim)) * 1.4426950408889634f;
+  auto kern = n_tokens <= 256 ? f32dec::zoned_small_kernel<256> : f32dec::zoned_small_kernel<f32dec::SMALL_TOK>;
+  return check_cuda(launch_pdl(kern, dim3((unsigned)n_kv_heads), dim3(256), 0, static_cast<cudaStream_t>(stream), q,
+                               k_arena, v_arena, out, importance, (int)n_tokens, (int)n_layers, (int)layer_idx,
+                               (int)n_kv_heads, sl2),
+                    "decode_zoned_f32 short-context launch");
+}
+}  // namespace nyion
+
 extern "C" int32_t nyion_attn_decode_zoned_f32(float* out, const float* q, const float* k_arena,
                                                const float* v_arena, int64_t n_arena_pages,
                                                int32_t n_layers, int32_t layer_idx,
@@ -852,18 +892,9 @@ extern "C" int32_t nyion_attn_decode_zoned_f32(float* out, const float* q, const
   // ops.rs:183 valid_end = min(q_pos, seq_len - 1): tokens [0, valid_end] are attended
   int64_t valid_end = q_pos < seq_len - 1 ? q_pos : seq_len - 1;
   if (valid_end + 1 > (1ll << 30)) return fail(NYION_ERR_INVALID, "decode_zoned_f32: context too long");
-  if (valid_end + 1 <= SMALL_TOK) {
-    // short context: one launch, all pages in zone 0
-    const int64_t pages = (valid_end + 1 + 31) / 32;
-    if (pages > n_arena_pages)
-      return fail(NYION_ERR_INVALID, "decode_zoned_f32: %lld tokens need %lld pages, the arena has %lld",
-                  (long long)(valid_end + 1), (long long)pages, (long long)n_arena_pages);
-    const float sl2 = (1.0f / sqrtf((float)head_dim)) * 1.4426950408889634f;
-    return check_cuda(launch_pdl(zoned_small_kernel, dim3((unsigned)n_kv_heads), dim3(256), 0,
-                                 static_cast<cudaStream_t>(stream), q, k_arena, v_arena, out,
-                                 (int)(valid_end + 1), (int)n_layers, (int)layer_idx, (int)n_kv_heads, sl2),
-                      "decode_zoned_f32 small launch");
-  }
+  if (valid_end + 1 <= zoned_small_max())
+    return zoned_small(out, q, k_arena, v_arena, n_arena_pages, n_layers, layer_idx, valid_end + 1, n_kv_heads,
+                       head_dim, nullptr, stream);
   // rows in the arena: zone pages [0, n_arena_pages) of 32 / 128 / 1024 slots
   const int64_t lp = (int64_t)n_layers * n_kv_heads;
   int64_t z0 = n_arena_pages < 128 ? n_arena_pages : 128;

@@ -68,6 +68,15 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
 }
 
+// Zoned decode of short contexts (decode_f32.cu): one launch for up to
+// zoned_small_max() tokens, optionally adding the importance weights of
+// ops::attention_tracked.  Arguments as nyion_attn_decode_zoned_f32, with the
+// attended token count instead of seq_len / q_pos.
+int64_t zoned_small_max();
+int32_t zoned_small(float* out, const float* q, const float* k_arena, const float* v_arena, int64_t n_arena_pages,
+                    int32_t n_layers, int32_t layer_idx, int64_t n_tokens, int32_t n_kv_heads, int32_t head_dim,
+                    double* importance, void* stream);
+
 // Whole-page fp32 paged decode for 4 KV heads (decode_pages.cu): workspace
 // bytes for `batch` sequences, and the launch (workspace zeroed once, left
 // with its counters at zero).

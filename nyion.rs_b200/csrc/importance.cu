@@ -7,7 +7,9 @@
 // (decode_f32.cu); this file adds the per-position weights.
 //
 // The executor takes this path for short sequences (the Full strategy, up to
-// 512 tokens), so it is built for latency, not bandwidth: two small launches.
+// 512 tokens): there the short-context zoned kernel (decode_f32.cu) computes
+// output and weights in one launch.  Longer contexts take two small launches
+// after the zoned decode:
 //   scores_kernel     grid (KV head, 256-position chunk), warp = query head of
 //                     the group, lane = position: s = q.K_t * scale * log2(e)
 //                     (fp32), stored [H][T], plus the chunk's (max, sum 2^(s-max))
@@ -173,6 +175,13 @@ extern "C" int32_t nyion_attn_decode_zoned_f32_tracked(float* out, const float* 
   if (!importance) return fail(NYION_ERR_INVALID, "decode_zoned_f32_tracked: importance is required");
   if (n_heads > MAX_HEADS)
     return fail(NYION_ERR_UNSUPPORTED, "decode_zoned_f32_tracked: at most %d query heads", MAX_HEADS);
+  if (seq_len > 0 && q_pos >= 0) {
+    const int64_t ve = q_pos < seq_len - 1 ? q_pos : seq_len - 1;
+    if (ve + 1 <= zoned_small_max() && head_dim == HD && n_kv_heads > 0 && n_heads == n_kv_heads * GROUP &&
+        n_layers > 0 && layer_idx >= 0 && layer_idx < n_layers && out && q && k_arena && v_arena)
+      return zoned_small(out, q, k_arena, v_arena, n_arena_pages, n_layers, layer_idx, ve + 1, n_kv_heads, head_dim,
+                         importance, stream);   // one launch: output and weights
+  }
   int32_t st = nyion_attn_decode_zoned_f32(out, q, k_arena, v_arena, n_arena_pages, n_layers, layer_idx, seq_len,
                                            q_pos, n_heads, n_kv_heads, head_dim, stream);
   if (st) return st;
