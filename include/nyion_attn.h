@@ -93,8 +93,9 @@ int32_t nyion_attn_decode_paged_f32(const float* q, const float* kv_pool, int64_
  * capture, a serving loop that cannot afford cudaFree's device-wide
  * synchronisation, a host whose HBM is fully owned by its own arena).  The
  * split-KV scratch is a fixed 8 MiB device array inside the library, reserved
- * on every GPU that loads it; the call allocates nothing.  Limit:
- * batch <= 512 and (148 + batch * n_kv_heads) * 6 partial slots of 2112 bytes
+ * on every GPU that loads it; the call allocates nothing.  Limit: batch <= 512;
+ * with 4 KV heads (the whole-page kernel of the main entry) every such batch
+ * fits; otherwise (148 + batch * n_kv_heads) * 6 partial slots of 2112 bytes
  * must fit the 8 MiB (about batch * n_kv_heads <= 500 on B200); larger calls
  * return NYION_ERR_WORKSPACE.  The first call on a device resolves the
  * array's address (cudaGetSymbolAddress): make it before any stream capture.

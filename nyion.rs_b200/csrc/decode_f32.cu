@@ -1088,6 +1088,7 @@ struct NoAllocDevice {
   uint8_t* scratch = nullptr;   // device address of g_noalloc_scratch
   int32_t* err = nullptr;       // device address of g_noalloc_err
   int grid = 0;
+  int sms = 0;
 };
 static NoAllocDevice g_noalloc_dev[64];
 static std::mutex g_noalloc_mu;
@@ -1125,6 +1126,7 @@ static int32_t noalloc_setup(NoAllocDevice** out) {
     d.err = static_cast<int32_t*>(ep);
     d.grid = sms * (occ > 0 ? occ : 1);
     if (d.grid > MAX_GRID) d.grid = MAX_GRID;
+    d.sms = sms;
     d.ready = true;
   }
   *out = &d;
@@ -1154,6 +1156,15 @@ extern "C" int32_t nyion_attn_decode_paged_f32_noalloc(
   NoAllocDevice* d = nullptr;
   st = noalloc_setup(&d);
   if (st) return st;
+  cudaStream_t s0 = static_cast<cudaStream_t>(stream);
+  if (n_kv_heads == 4 && pages_workspace_bytes(batch) <= kNoAllocScratchBytes) {
+    // 4 KV heads: the whole-page kernel on the static scratch, counters cleared first
+    st = check_cuda(cudaMemsetAsync(d->scratch, 0, pages_counter_bytes(), s0), "clear merge counters");
+    if (st) return st;
+    const float qscale = (scale > 0.f ? scale : 1.0f / sqrtf((float)head_dim)) * 1.4426950408889634f;
+    return launch_pages(q, kv_pool, n_pool_pages, page_table, max_pages, seq_lens, out, batch, qscale, d->scratch,
+                        s0, d->err, d->sms);
+  }
   // scratch layout for this launch: counters | (m, l) partials | o partials
   const size_t pairs = (size_t)batch * n_kv_heads;
   const size_t slots = ((size_t)d->grid + pairs) * NC;

@@ -41,7 +41,7 @@ constexpr int THREADS = (NCW + 1) * 32;
 constexpr int BLOCK = 8192;                  // one KV head of a page: K 0-31 | K 32-63 | V 0-31 | V 32-63
 constexpr int STAGE_BYTES = NKV * BLOCK;
 constexpr int MAX_SEQS = 512;
-constexpr int MAX_GRID = 1024;
+constexpr int MAX_GRID = 296;          // one CTA per SM on B200 (148), with room
 
 struct Params {
   const float* q;           // [batch][32][64]
@@ -501,13 +501,27 @@ size_t pages_workspace_bytes(int batch) {
          slots * pages::GROUP * pages::HD * sizeof(float);
 }
 
+size_t pages_counter_bytes() {
+  return ((size_t)pages::MAX_SEQS * pages::NKV * sizeof(int32_t) + 255) & ~size_t(255);
+}
+
 int32_t launch_pages(const float* q, const float* kv_pool, int64_t n_pool_pages, const int32_t* page_table,
                      int32_t max_pages, const int32_t* seq_lens, float* out, int32_t batch, float qscale,
-                     void* ws, cudaStream_t stream) {
+                     void* ws, cudaStream_t stream, int32_t* err_word, int num_sms) {
   using namespace pages;
-  DeviceInfo* dev = nullptr;
-  int32_t st = device_info(&dev);
-  if (st) return st;
+  // the allocation-free entry passes its own error word and SM count (device_info may allocate)
+  DeviceInfo local{};
+  DeviceInfo* dev = &local;
+  int32_t st = NYION_OK;
+  if (err_word) {
+    st = check_cuda(cudaGetDevice(&local.device), "cudaGetDevice");
+    if (st) return st;
+    local.num_sms = num_sms;
+    local.err_word = err_word;
+  } else {
+    st = device_info(&dev);
+    if (st) return st;
+  }
   if ((uint64_t)n_pool_pages * NKV > (1ull << 31))
     return fail(NYION_ERR_INVALID, "decode_paged_f32: pool too large");
   CUtensorMap map;

@@ -83,7 +83,9 @@ int32_t zoned_small(float* out, const float* q, const float* k_arena, const floa
 size_t pages_workspace_bytes(int batch);
 int32_t launch_pages(const float* q, const float* kv_pool, int64_t n_pool_pages, const int32_t* page_table,
                      int32_t max_pages, const int32_t* seq_lens, float* out, int32_t batch, float qscale,
-                     void* ws, cudaStream_t stream);
+                     void* ws, cudaStream_t stream, int32_t* err_word = nullptr, int num_sms = 0);
+// Leading bytes of the page kernel's workspace that hold its merge counters.
+size_t pages_counter_bytes();
 
 // Handle behind gpu_graph_create_attention[_half]: the instantiated graph
 // and the workspace it owns (freed by gpu_graph_destroy).
