@@ -293,8 +293,10 @@ int32_t nyion_attn_prefill_paged_bf16(const void* q, const void* kv_pool, int64_
 /* ------------------------------------------------------- f16 KV caches ----
  * Decode over f16 caches [n_kv_heads][stride][head_dim] (query head h reads
  * KV head h / (n_heads / n_kv_heads); scale <= 0 means 1/sqrt(head_dim)).
- * Split-KV partials go to `workspace` (nyion_attn_f16_workspace_size bytes;
- * null = library-owned, allocated on first use: not under stream capture).
+ * Split-KV partials and per-KV-head merge counters go to `workspace`
+ * (nyion_attn_f16_workspace_size bytes, reset once with
+ * nyion_attn_workspace_reset and left with its counters at zero; null =
+ * library-owned, allocated on first use: not under stream capture).
  *
  * nyion_attn_decode_contig_f16: tokens [0, seq_len) of a contiguous half
  * cache — gpu_attention_streamed_half (fused_attention.cu:534-582) with a

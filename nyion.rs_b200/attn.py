@@ -468,6 +468,7 @@ class F16Workspace:
         torch = _torch()
         self.nbytes = int(lib().nyion_attn_f16_workspace_size(n_heads, max_tokens))
         self.buf = torch.empty(self.nbytes, dtype=torch.uint8, device=device or "cuda")
+        check(lib().nyion_attn_workspace_reset(self.ptr(), self.nbytes, None))   # merge counters start at 0
 
     def ptr(self) -> int:
         return int(self.buf.data_ptr())

@@ -1,4 +1,7 @@
-// decode_f32.cu — fp32 GQA decode attention over paged, contiguous or zoned KV.
+// decode_f32.cu — fp32 GQA decode attention over a paged KV pool (any number
+// of KV heads; 4 KV heads take the whole-page kernel of decode_pages.cu), the
+// short-context zone-arena kernel, and the reference's CUDA C ABI entry points
+// (their single-sequence row-cache work runs in decode_contig.cu).
 //
 // Restates the maths of ops::attention (swamp-engine/src/ops.rs:170-278):
 // s_t = scale * <q_h, K_t>, p = softmax(s), o_h = sum_t p_t V_t, query head h
@@ -56,18 +59,13 @@ constexpr int MAX_SEQS = 512;         // sequences per launch
 constexpr int MAX_GRID = 1024;
 constexpr int RING = 32;              // chunks per page-row prefetch batch
 
-enum Mode { kPool = 0, kContig = 1, kZoned = 2 };
-
 struct Params {
   const float* q;           // [batch][n_kv*GROUP][HD]
   float* out;               // [batch][n_kv*GROUP][HD]
   const int32_t* table;     // pool: [batch][max_pages]
-  const int32_t* seq_lens;  // [batch] or null (use uniform_len)
-  int32_t uniform_len;
+  const int32_t* seq_lens;  // [batch]
   int32_t batch, n_kv, max_pages;
   int64_t n_pool_pages;
-  int32_t kv_stride;        // contiguous: rows per KV head
-  int32_t n_layers, layer;  // zoned: layers per page, layer read
   float qscale;             // scale * log2(e)
   int32_t* cnt;             // [batch*n_kv] merge counters (start at 0, left at 0)
   float2* ml;               // [(MAX_GRID + pairs) * NC][GROUP] (m, l) partials
@@ -114,7 +112,6 @@ struct RowJob {
   int64_t page[2];
 };
 
-template <int MODE>
 __device__ __forceinline__ void rows_start(RowJob& j, const Smem& s, const Params& p, int i, int end) {
   j.valid = i < end;
   if (!j.valid) return;
@@ -125,19 +122,15 @@ __device__ __forceinline__ void rows_start(RowJob& j, const Smem& s, const Param
   j.tok0 = c.chunk * CHUNK;
   j.npg = (c.len - j.tok0 > PAGE) ? 2 : 1;
   j.page[0] = j.page[1] = -1;
-  if (MODE == kPool) {
 #pragma unroll
-    for (int pg = 0; pg < 2; ++pg) {
-      const int pidx = j.tok0 / PAGE + pg;
-      if (pg < j.npg && pidx < p.max_pages) j.page[pg] = p.table[(int64_t)c.b * p.max_pages + pidx];
-    }
+  for (int pg = 0; pg < 2; ++pg) {
+    const int pidx = j.tok0 / PAGE + pg;
+    if (pg < j.npg && pidx < p.max_pages) j.page[pg] = p.table[(int64_t)c.b * p.max_pages + pidx];
   }
 }
 
-// Stores per chunk: copy coordinate of page 0, page 1, page count.  Pool mode
-// stores the (page * n_kv + kv head) block index of the 5-D map; the other
-// modes store the first row (of 256 B) in the K and V arenas.
-template <int MODE>
+// Stores per chunk: the (page * n_kv + kv head) block index of the 5-D map
+// for page 0 and page 1, and the page count.
 __device__ __forceinline__ void rows_finish(Smem& s, const Params& p, const RowJob& j, int slot,
                                             int lane) {
   if (!j.valid) return;
@@ -145,63 +138,30 @@ __device__ __forceinline__ void rows_finish(Smem& s, const Params& p, const RowJ
 #pragma unroll
   for (int pg = 0; pg < 2; ++pg) {
     if (pg >= j.npg) continue;
-    if (MODE == kPool) {
-      const int64_t page = j.page[pg];
-      if (page < 0 || page >= p.n_pool_pages) {
-        record_error(p.err, kErrPageRange);
-        continue;   // negative coordinate: the TMA box is zero-filled
-      }
-      r[pg] = (int32_t)(page * p.n_kv + j.kvh);
-    } else if (MODE == kZoned) {
-      // cache.rs:185-237, 681-747: zone z holds pages of bs_z slots laid out
-      // [layer][kv_head][slot][head_dim]; pages are consecutive in the arena.
-      const int zone = j.tok0 < 4096 ? 0 : (j.tok0 < 131072 ? 1 : 2);
-      const int64_t bs = zone == 0 ? 32 : (zone == 1 ? 128 : 1024);
-      const int64_t zs = zone == 0 ? 0 : (zone == 1 ? 4096 : 131072);
-      const int64_t zpage = zone == 0 ? 0 : (zone == 1 ? 128 : 1120);
-      const int64_t lp = p.n_layers * (int64_t)p.n_kv;
-      const int64_t zrow = zone == 0 ? 0 : (zone == 1 ? 128 * lp * 32 : 128 * lp * 32 + 992 * lp * 128);
-      const int64_t local = (j.tok0 - zs) / bs, slot = (j.tok0 - zs) % bs;
-      if (zpage + local >= p.n_pool_pages) {
-        record_error(p.err, kErrPageRange);
-        continue;
-      }
-      r[pg] = (int32_t)(zrow + local * lp * bs + ((int64_t)p.layer * p.n_kv + j.kvh) * bs + slot +
-                        pg * PAGE);
-    } else {
-      r[pg] = j.kvh * p.kv_stride + j.tok0 + pg * PAGE;
+    const int64_t page = j.page[pg];
+    if (page < 0 || page >= p.n_pool_pages) {
+      record_error(p.err, kErrPageRange);
+      continue;   // negative coordinate: the TMA box is zero-filled
     }
+    r[pg] = (int32_t)(page * p.n_kv + j.kvh);
   }
   s.rows[slot][lane][0] = r[0];
   s.rows[slot][lane][1] = r[1];
   s.rows[slot][lane][2] = j.npg;
 }
 
-template <int MODE>
-__device__ __forceinline__ void issue(Smem& s, int stage, int k, const CUtensorMap* mk,
-                                      const CUtensorMap* mv) {
+__device__ __forceinline__ void issue(Smem& s, int stage, int k, const CUtensorMap* map) {
   const int32_t* e = s.rows[(k / RING) & 1][k % RING];
   const int npg = e[2];
   uint8_t* base = s.kv[stage];
   fence_proxy_async_smem();
   mbar_arrive_expect_tx(&s.full[stage], (uint32_t)(npg * PAGE_BYTES));
-  for (int pg = 0; pg < npg; ++pg) {
-    uint8_t* d = base + pg * PAGE_BYTES;
-    if (MODE == kPool) {
-      // (x, slot row, 128-B half, K/V, block): K_lo, K_hi, V_lo, V_hi subtiles
-      tma_load_5d(d, mk, 0, 0, 0, 0, e[pg], &s.full[stage]);
-    } else {
-      // (x, row, 128-B half) boxes of 16 rows: K then V
-      tma_load_3d(d, mk, 0, e[pg], 0, &s.full[stage]);
-      tma_load_3d(d + PAGE_BYTES / 2, mv, 0, e[pg], 0, &s.full[stage]);
-    }
-  }
+  // (x, slot row, 128-B half, K/V, block): K_lo, K_hi, V_lo, V_hi subtiles
+  for (int pg = 0; pg < npg; ++pg) tma_load_5d(base + pg * PAGE_BYTES, map, 0, 0, 0, 0, e[pg], &s.full[stage]);
 }
 
-template <int MODE>
 __global__ void __launch_bounds__(THREADS, 1)
-decode_f32_kernel(const Params p, const __grid_constant__ CUtensorMap map_k,
-                  const __grid_constant__ CUtensorMap map_v) {
+decode_f32_kernel(const Params p, const __grid_constant__ CUtensorMap map) {
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                      ~uintptr_t(1023));
@@ -209,8 +169,7 @@ decode_f32_kernel(const Params p, const __grid_constant__ CUtensorMap map_k,
   const int H = p.n_kv * GROUP;
 
   if (t == 0) {
-    prefetch_tensormap(&map_k);
-    prefetch_tensormap(&map_v);
+    prefetch_tensormap(&map);
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&s.full[i], 1);
       mbar_init(&s.empty[i], 1);
@@ -221,7 +180,7 @@ decode_f32_kernel(const Params p, const __grid_constant__ CUtensorMap map_k,
 
   // ---- sequence lengths and flat chunk prefix (block scan) ----
   for (int b = t; b < p.batch; b += THREADS) {
-    int L = p.seq_lens ? p.seq_lens[b] : p.uniform_len;
+    int L = p.seq_lens[b];
     s.lens[b] = L > 0 ? L : 0;
   }
   __syncthreads();
@@ -269,18 +228,18 @@ decode_f32_kernel(const Params p, const __grid_constant__ CUtensorMap map_k,
   if (warp == NC) {
     // ================= producer warp =================
     RowJob job;
-    rows_start<MODE>(job, s, p, begin + lane, end);
-    rows_finish<MODE>(s, p, job, 0, lane);
-    rows_start<MODE>(job, s, p, begin + RING + lane, end);
+    rows_start(job, s, p, begin + lane, end);
+    rows_finish(s, p, job, 0, lane);
+    rows_start(job, s, p, begin + RING + lane, end);
     __syncwarp();
     for (int k = 0; k < n; ++k) {
       const int stage = k % STAGES;
       if (k % RING == RING / 2) {
         // rows for chunks [k - RING/2 + RING, ... + RING) into the other slot
-        rows_finish<MODE>(s, p, job, ((k / RING) + 1) & 1, lane);
+        rows_finish(s, p, job, ((k / RING) + 1) & 1, lane);
         __syncwarp();
       } else if (k % RING == 0 && k > 0) {
-        rows_start<MODE>(job, s, p, begin + k + RING + lane, end);
+        rows_start(job, s, p, begin + k + RING + lane, end);
       }
       bool ok = true;
       if (k >= STAGES) ok = mbar_wait_bounded(&s.empty[stage], (uint32_t)(((k / STAGES) - 1) & 1));
@@ -294,7 +253,7 @@ decode_f32_kernel(const Params p, const __grid_constant__ CUtensorMap map_k,
         }
         return;
       }
-      if (lane == 0) issue<MODE>(s, stage, k, &map_k, &map_v);
+      if (lane == 0) issue(s, stage, k, &map);
       __syncwarp();
     }
     return;
@@ -609,8 +568,7 @@ WsLayout ws_layout(int batch, int n_kv) {
   return w;
 }
 
-template <int MODE>
-int32_t launch(const Params& base, const CUtensorMap& mk, const CUtensorMap& mv, int batch,
+int32_t launch(const Params& base, const CUtensorMap& map, int batch,
                const int32_t* seq_lens, const float* q, float* out, const int32_t* table,
                void* ws, cudaStream_t stream) {
   DeviceInfo* dev = nullptr;
@@ -620,12 +578,12 @@ int32_t launch(const Params& base, const CUtensorMap& mk, const CUtensorMap& mv,
   int di = dev->device < 64 ? dev->device : 0;
   size_t smem = smem_bytes();
   if (!occ_cache[di]) {
-    st = check_cuda(cudaFuncSetAttribute(decode_f32_kernel<MODE>,
+    st = check_cuda(cudaFuncSetAttribute(decode_f32_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                     "cudaFuncSetAttribute(decode_f32)");
     if (st) return st;
     int occ = 0;
-    st = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_f32_kernel<MODE>,
+    st = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_f32_kernel,
                                                                   THREADS, smem),
                     "occupancy(decode_f32)");
     if (st) return st;
@@ -647,7 +605,7 @@ int32_t launch(const Params& base, const CUtensorMap& mk, const CUtensorMap& mv,
     p.ml = reinterpret_cast<float2*>(static_cast<uint8_t*>(ws) + w.ml);
     p.po = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + w.po);
     p.err = dev->err_word;
-    decode_f32_kernel<MODE><<<grid, THREADS, smem, stream>>>(p, mk, mv);
+    decode_f32_kernel<<<grid, THREADS, smem, stream>>>(p, map);
     st = check_cuda(cudaGetLastError(), "decode_f32 launch");
     if (st) return st;
   }
@@ -661,15 +619,6 @@ int32_t pool_map(CUtensorMap* m, const float* pool, int64_t n_blocks) {
   const uint64_t strides[4] = {HD * 4, 128, PAGE * HD * 4, 2 * PAGE * HD * 4};
   const uint32_t box[5] = {32, (uint32_t)PAGE, 2, 2, 1};
   return encode_tmap(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, pool, dims, strides, box,
-                     CU_TENSOR_MAP_SWIZZLE_128B);
-}
-
-// Row arena: (x: 32 floats, row: 256 B, half: 128 B); box = 16 rows x both halves.
-int32_t rows_map(CUtensorMap* m, const float* base, uint64_t rows) {
-  const uint64_t dims[3] = {32, rows, 2};
-  const uint64_t strides[2] = {HD * 4, 128};
-  const uint32_t box[3] = {32, (uint32_t)PAGE, 2};
-  return encode_tmap(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box,
                      CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
@@ -853,7 +802,7 @@ extern "C" int32_t nyion_attn_decode_paged_f32(const float* q, const float* kv_p
   p.max_pages = max_pages;
   p.n_pool_pages = n_pool_pages;
   p.qscale = qscale;
-  return launch<kPool>(p, map, map, batch, seq_lens, q, out, page_table, workspace,
+  return launch(p, map, batch, seq_lens, q, out, page_table, workspace,
                        static_cast<cudaStream_t>(stream));
 }
 
@@ -895,30 +844,9 @@ extern "C" int32_t nyion_attn_decode_zoned_f32(float* out, const float* q, const
   if (valid_end + 1 <= zoned_small_max())
     return zoned_small(out, q, k_arena, v_arena, n_arena_pages, n_layers, layer_idx, valid_end + 1, n_kv_heads,
                        head_dim, nullptr, stream);
-  // rows in the arena: zone pages [0, n_arena_pages) of 32 / 128 / 1024 slots
-  const int64_t lp = (int64_t)n_layers * n_kv_heads;
-  int64_t z0 = n_arena_pages < 128 ? n_arena_pages : 128;
-  int64_t z1 = n_arena_pages - z0 < 992 ? n_arena_pages - z0 : 992;
-  int64_t z2 = n_arena_pages - z0 - z1;
-  uint64_t rows = (uint64_t)(z0 * 32 + z1 * 128 + z2 * 1024) * lp;
-  if (rows > (1ull << 31)) return fail(NYION_ERR_INVALID, "decode_zoned_f32: arena exceeds 2^31 rows");
-  CUtensorMap mk, mv;
-  st = rows_map(&mk, k_arena, rows);
-  if (st) return st;
-  st = rows_map(&mv, v_arena, rows);
-  if (st) return st;
-  void* ws = nullptr;
-  st = internal_workspace(ws_layout(1, n_kv_heads).total, &ws, kWsCounters, ws_layout(1, n_kv_heads).ml,
-                          static_cast<cudaStream_t>(stream));
-  if (st) return st;
-  Params p{};
-  p.n_kv = n_kv_heads;
-  p.n_layers = n_layers;
-  p.layer = layer_idx;
-  p.n_pool_pages = n_arena_pages;
-  p.uniform_len = (int32_t)(valid_end + 1);
-  p.qscale = (1.0f / sqrtf((float)head_dim)) * 1.4426950408889634f;
-  return launch<kZoned>(p, mk, mv, 1, nullptr, q, out, nullptr, ws, static_cast<cudaStream_t>(stream));
+  const float sl2 = (1.0f / sqrtf((float)head_dim)) * 1.4426950408889634f;
+  return contig_zoned_f32(q, k_arena, v_arena, out, n_kv_heads, n_layers, layer_idx, n_arena_pages,
+                          (int)(valid_end + 1), sl2, nullptr, 0, static_cast<cudaStream_t>(stream));
 }
 
 // ---- reference CUDA C ABI (swamp-gpu/kernels/fused_attention.cu) -------------
@@ -931,23 +859,9 @@ static int32_t contig_decode(const float* d_q, const float* d_k, const float* d_
   if (!d_q || !d_k || !d_v || !d_out) return fail(NYION_ERR_INVALID, "null pointer argument");
   if (seq_len <= 0 || kv_stride < seq_len)
     return fail(NYION_ERR_INVALID, "seq_len %d must be in [1, kv_stride=%d]", seq_len, kv_stride);
-  uint64_t rows = (uint64_t)n_kv_heads * kv_stride;
-  CUtensorMap mk, mv;
-  st = rows_map(&mk, d_k, rows);
-  if (st) return st;
-  st = rows_map(&mv, d_v, rows);
-  if (st) return st;
-  if (!ws) {
-    st = internal_workspace(ws_layout(1, n_kv_heads).total, &ws, kWsCounters, ws_layout(1, n_kv_heads).ml,
-                            stream);
-    if (st) return st;
-  }
-  Params p{};
-  p.n_kv = n_kv_heads;
-  p.kv_stride = kv_stride;
-  p.uniform_len = seq_len;
-  p.qscale = (1.0f / sqrtf((float)head_dim)) * 1.4426950408889634f;
-  return launch<kContig>(p, mk, mv, 1, nullptr, d_q, d_out, nullptr, ws, stream);
+  const float sl2 = (1.0f / sqrtf((float)head_dim)) * 1.4426950408889634f;
+  return contig_rows_f32(d_q, d_k, d_v, d_out, n_kv_heads, kv_stride, seq_len, sl2, ws,
+                         ws ? contig_workspace_bytes(n_kv_heads, seq_len) : 0, stream);
 }
 
 extern "C" int gpu_attention_streamed(const float* d_q, const float* d_k_cache,
@@ -1003,7 +917,7 @@ extern "C" void* gpu_graph_create_attention(const float* d_q, const float* d_k_c
   (void)d_scores;
   DeviceInfo* dev = nullptr;
   if (device_info(&dev)) return nullptr;
-  size_t wsb = ws_layout(1, n_kv_heads > 0 ? n_kv_heads : 1).total;
+  const size_t wsb = contig_workspace_bytes(n_kv_heads > 0 ? n_kv_heads : 1, seq_len);
   void* ws = nullptr;
   if (check_cuda(cudaMalloc(&ws, wsb), "cudaMalloc(graph workspace)")) return nullptr;
   if (check_cuda(cudaMemset(ws, 0, wsb), "cudaMemset(graph workspace)")) { cudaFree(ws); return nullptr; }
@@ -1113,12 +1027,12 @@ static int32_t noalloc_setup(NoAllocDevice** out) {
     cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
     if (major != 10) return fail(NYION_ERR_UNSUPPORTED, "device %d is not sm_100a", dev);
     const size_t smem = smem_bytes();
-    st = check_cuda(cudaFuncSetAttribute(decode_f32_kernel<kPool>,
+    st = check_cuda(cudaFuncSetAttribute(decode_f32_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                     "cudaFuncSetAttribute(decode_f32)");
     if (st) return st;
     int occ = 0;
-    st = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_f32_kernel<kPool>,
+    st = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_f32_kernel,
                                                                   THREADS, smem),
                     "occupancy(decode_f32)");
     if (st) return st;
@@ -1197,6 +1111,6 @@ extern "C" int32_t nyion_attn_decode_paged_f32_noalloc(
   p.ml = reinterpret_cast<float2*>(d->scratch + off_ml);
   p.po = reinterpret_cast<float*>(d->scratch + off_po);
   p.err = d->err;
-  decode_f32_kernel<kPool><<<d->grid, THREADS, smem_bytes(), s>>>(p, map, map);
+  decode_f32_kernel<<<d->grid, THREADS, smem_bytes(), s>>>(p, map);
   return check_cuda(cudaGetLastError(), "decode_f32_noalloc launch");
 }

@@ -200,12 +200,6 @@ __device__ __forceinline__ void rows_finish(Smem& s, const Params& p, const RowJ
   s.rows[slot][lane][4] = j.b;
 }
 
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-               ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
-}
-
 // fp16x2 {1 + n_a/16, 1 + n_b/16} from the nibbles at bits [s+0..3] and [s+16..19] of w
 template <int SHIFT>
 __device__ __forceinline__ uint32_t nib2h(uint32_t w) {

@@ -87,6 +87,20 @@ int32_t launch_pages(const float* q, const float* kv_pool, int64_t n_pool_pages,
 // Leading bytes of the page kernel's workspace that hold its merge counters.
 size_t pages_counter_bytes();
 
+// Single-sequence decode over row caches (decode_contig.cu), head_dim 64 and
+// GQA group 8: contiguous f32 / f16 caches [n_kv][stride][64] (f16 optionally
+// with a device length clamped to `window`) and the zone-page arena.  `sl2` is
+// scale * log2(e).  Workspace: contig_workspace_bytes(n_kv, max tokens), its
+// leading counters zeroed once (null = the library's, zeroed on allocation).
+size_t contig_workspace_bytes(int n_kv, int max_tokens);
+int32_t contig_rows_f32(const float* q, const float* k, const float* v, float* out, int n_kv, int64_t stride, int n,
+                        float sl2, void* ws, size_t ws_bytes, cudaStream_t stream);
+int32_t contig_rows_f16(const float* q, const void* k, const void* v, float* out, int n_kv, int64_t stride, int n,
+                        const int32_t* d_len, int window, float sl2, void* ws, size_t ws_bytes, cudaStream_t stream);
+int32_t contig_zoned_f32(const float* q, const float* k_arena, const float* v_arena, float* out, int n_kv,
+                         int n_layers, int layer, int64_t n_pages, int n, float sl2, void* ws, size_t ws_bytes,
+                         cudaStream_t stream);
+
 // Handle behind gpu_graph_create_attention[_half]: the instantiated graph
 // and the workspace it owns (freed by gpu_graph_destroy).
 struct AttnGraph {
