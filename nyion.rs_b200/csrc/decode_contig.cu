@@ -15,27 +15,32 @@
 //     tokens: zone pages of 32 / 128 / 1024 slots hold each KV head's slots
 //     as consecutive rows, so every 32-token tile is one run of rows there too.
 //
-// One call is a few MB to a few tens of MB read once, so the design is about
-// keeping HBM busy from the first cycle and keeping the merge short:
+// One call reads a few MB to a few hundred MB once:
 //
-//   * grid = (KV head, split): each CTA owns a contiguous range of 32-token
-//     tiles; splits are sized so ~2 CTAs run per SM (TARGET_CTAS);
-//   * thread 0 streams the tiles with 1-D bulk copies (K rows, V rows) into a
-//     96 KB ring of stages, all stages in flight from the start; a stage is
-//     refilled one barrier after its last reader is done;
-//   * scores: thread = (token, 1/8 of the dims) holds the pre-scaled query of
-//     all 8 heads of the GQA group for its dims (64 registers), reads its K
-//     slice from shared memory once (conflict-free 16-byte loads) and folds
-//     the 8 head partials across its 8 lanes by a reduce-scatter (7 shuffles)
-//     — every K byte is read from shared memory once for all 8 heads;
-//   * softmax: warp = head, lane = token; online log2-domain max and sum;
-//   * P.V: warp = 4 tokens of the tile, lane = (4 dims, 4 heads), 16 fp32
-//     accumulators; the 8 warps' accumulators are summed once at the end;
-//   * every CTA leaves one (m, l, o[8][64]) partial per KV head; a counter per
-//     KV head tells the last CTA to merge them: warp = head, the weights
-//     computed once per split, then every lane sums its two dims over the
-//     splits with 8 loads in flight.  A single split writes the output
-//     directly.  All arithmetic is fp32 FMA (no operand rounding).
+//   * grid = (KV head, split), one CTA per SM: each CTA owns a contiguous
+//     range of 32-token tiles of one KV head;
+//   * a producer warp streams the tiles with tensor copies (128-byte swizzle)
+//     into a 128 KB ring of stages, 8 consumer warps take the tiles
+//     round-robin, each tile computed by ONE warp for all 8 query heads of the
+//     GQA group, so no barrier spans the consumer warps;
+//   * S = Q K^T and O += P V run on mma.sync m16n8k16 with fp32 accumulation.
+//     The A operand stacks the hi parts of the 8 heads (rows 0-7) over their
+//     lo parts (rows 8-15), so one mma covers both halves of a split operand:
+//       - f16 caches: K and V are exact f16 B operands, q and P are split into
+//         f16 hi + lo (q pre-scaled by 2^8, P by 2^7, so their lo halves
+//         stay clear of f16's subnormal range);
+//       - f32 caches: K and V are split into bf16 hi + lo as well and every
+//         product is issued twice (B hi, B lo), so all four cross products
+//         accumulate (~2^-17 relative residual per operand);
+//     K fragments come from ldmatrix on the tile, V fragments from
+//     ldmatrix.trans (f16) or 32-bit shared loads (f32);
+//   * online softmax per warp in the log2 domain, the reference maximum moved
+//     only when a tile's maximum passes it by 8 (most tiles skip the rescale);
+//   * the 8 warps fold their partials in shared memory; every CTA leaves one
+//     (m, l, o[8][64]) partial per KV head and a counter per KV head tells
+//     the last CTA to merge them (warp = head, the weights computed once per
+//     split, every lane summing its two dims over the splits).  A single
+//     split writes the output directly.
 #include <cuda_fp16.h>
 #include <math.h>
 
@@ -47,18 +52,19 @@ namespace contig {
 
 constexpr int HD = 64;
 constexpr int GROUP = 8;
-constexpr int TILE = 32;               // tokens per stage
-constexpr int THREADS = 256;
-constexpr int KV_BYTES = 96 * 1024;    // stage ring
-constexpr int TARGET_CTAS = 296;       // 2 CTAs per SM on 148 SMs
-constexpr int MAX_SPLITS = TARGET_CTAS;
+constexpr int SUB = 32;                // tokens one warp computes at a time
+constexpr int NCW = 8;                 // consumer warps
+constexpr int THREADS = (NCW + 1) * 32;
+constexpr int TARGET_CTAS = 148;       // one CTA per SM
+constexpr int MAX_SPLITS = 296;
+constexpr float Q_PRE = 256.0f;        // f16 path: q * 2^8 before the split
+constexpr float P_PRE = 128.0f;        // f16 path: P * 2^7 before the split (P < 2^8: below f16 max)
+constexpr float RESCALE_AT = 8.0f;     // log2 units
 
 enum Layout { kRows = 0, kZoned = 1 };
 
 struct Params {
   const float* q;            // [n_kv * 8][64]
-  const void* k;             // rows of 64 elements
-  const void* v;
   float* out;                // [n_kv * 8][64]
   int64_t stride;            // kRows: rows per KV head
   int32_t n_kv;
@@ -76,25 +82,41 @@ struct Params {
   int32_t* err;
 };
 
+// One stage = the K tile then the V tile.  Copies of 8 KB or more keep HBM
+// near its copy rate where 4 KB pieces reach about half of it, so an f16 tile
+// is 64 tokens (64 x 128 B swizzled rows, 8 KB), computed by a pair of warps
+// (32 tokens each); an f32 tile is 32 tokens (two 128-byte column halves of
+// 32 swizzled rows, 8 KB) computed by one warp.
 template <typename T>
 struct Geo {
-  static constexpr int RB = HD * (int)sizeof(T);            // row bytes
-  static constexpr int TILE_BYTES = TILE * RB;              // one of K, V
-  static constexpr int STAGES = KV_BYTES / (2 * TILE_BYTES);
+  static constexpr int WPT = sizeof(T) == 2 ? 2 : 1;         // warps per tile
+  static constexpr int GROUPS = NCW / WPT;                   // tiles in flight on the consumers
+  static constexpr int TILE = SUB * WPT;                     // tokens per tile
+  static constexpr int TILE_BYTES = TILE * HD * (int)sizeof(T);
+  static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
+  static constexpr int RING_BYTES = sizeof(T) == 2 ? 192 * 1024 : 128 * 1024;
+  static constexpr int STAGES = RING_BYTES / STAGE_BYTES;   // 12 (f16) or 8 (f32)
+  // tile k uses stage k % STAGES and warp group k % GROUPS: with STAGES a
+  // multiple of GROUPS a stage is always read by the same warps, which take
+  // their tiles in order, so none can wait on a barrier phase two
+  // completions ahead of the stage's last copy
+  static_assert(STAGES % GROUPS == 0, "a stage must always belong to one group of consumer warps");
+  static_assert(STAGES <= 16, "Tail holds 16 stages");
 };
 
 struct Tail {                       // after the stage ring
   uint64_t full[16];
-  int32_t rows[16];                 // valid rows copied into the stage (0: none)
-  float sp[2][TILE][9];             // scores, then probabilities: [token][head], padded
-  float alpha[2][GROUP];
+  uint64_t empty[16];               // WPT arrivals: the group's warps are done with the stage
+  int32_t rows[16];                 // valid rows of the tile in the stage (0: none)
+  int32_t abort_;
   int32_t last;
 };
 
-size_t smem_bytes() { return KV_BYTES + sizeof(Tail) + 128; }
+template <typename T>
+size_t smem_bytes() { return Geo<T>::RING_BYTES + sizeof(Tail) + 1024; }
 
-// first row of the 32-token tile starting at t0 for KV head kvh, or -1 when
-// its zone page is not in the arena
+// first row of the tile starting at t0 for KV head kvh, or -1 when its zone
+// page is not in the arena (zone-arena tiles are 32 tokens: page-aligned)
 template <int LAYOUT>
 __device__ __forceinline__ int64_t tile_row(const Params& p, int kvh, int t0) {
   if (LAYOUT == kRows) return (int64_t)kvh * p.stride + t0;
@@ -111,233 +133,347 @@ __device__ __forceinline__ int64_t tile_row(const Params& p, int kvh, int t0) {
   return zrow + local * lp * bs + ((int64_t)p.layer * p.n_kv + kvh) * bs + slot;
 }
 
-template <typename T, int LAYOUT>
-__device__ __forceinline__ void issue_tile(const Params& p, uint8_t* kv, Tail& t, int kvh, int tile, int n,
-                                           int stage) {
+// tensor copies of one tile (K then V): f16 maps are (x 64 halves, row),
+// f32 maps (x 32 floats, row, 128-byte half)
+template <typename T>
+__device__ __forceinline__ void copy_tile(uint8_t* dst, const CUtensorMap* mk, const CUtensorMap* mv, int32_t row,
+                                          uint64_t* bar) {
   using G = Geo<T>;
-  const int t0 = tile * TILE;
-  int rows = min(TILE, n - t0);
-  const int64_t r0 = tile_row<LAYOUT>(p, kvh, t0);
-  if (r0 < 0) {
-    record_error(p.err, kErrPageRange);
-    rows = 0;
-  }
-  t.rows[stage] = rows;
-  if (rows > 0) {
-    uint8_t* dst = kv + stage * 2 * G::TILE_BYTES;
-    const uint32_t bytes = (uint32_t)rows * G::RB;
-    fence_proxy_async_smem();
-    mbar_arrive_expect_tx(&t.full[stage], 2 * bytes);
-    bulk_load(dst, static_cast<const uint8_t*>(p.k) + r0 * G::RB, bytes, &t.full[stage]);
-    bulk_load(dst + G::TILE_BYTES, static_cast<const uint8_t*>(p.v) + r0 * G::RB, bytes, &t.full[stage]);
+  if (sizeof(T) == 2) {
+    tma_load_2d(dst, mk, 0, row, bar);
+    tma_load_2d(dst + G::TILE_BYTES, mv, 0, row, bar);
   } else {
-    mbar_arrive(&t.full[stage]);
+    tma_load_3d(dst, mk, 0, row, 0, bar);
+    tma_load_3d(dst + G::TILE_BYTES, mv, 0, row, 0, bar);
   }
 }
 
-// the 8 dims of row slice c: f32 rows take float4 chunks c and c + 8,
-// f16 rows take the 16-byte chunk c
+// bounded wait that also gives up as soon as another warp has aborted
+__device__ __forceinline__ bool wait_stage(uint64_t* bar, uint32_t parity, const volatile int32_t* abort_) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_) return false;
+    if (i > 64) __nanosleep(64);
+  }
+  return false;
+}
+
+// Q as the A operand of S = Q K^T for k-step ks (dims 16ks..16ks+15): rows
+// 0-7 = hi parts of heads 0-7, rows 8-15 = lo parts.  The k index kappa maps
+// to dims identically for f16; for f32 it follows the ldmatrix word order of
+// the fp32 tile: kappa 2t, 2t+1, 2t+8, 2t+9 -> dims t, 4+t, 8+t, 12+t.
 template <typename T>
-__device__ __forceinline__ void load_slice(uint32_t row_addr, int c, float (&x)[8]) {
-  if (sizeof(T) == 4) {
-    const float4 a = lds128(row_addr + 16 * c), b = lds128(row_addr + 128 + 16 * c);
-    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
-    x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
-  } else {
-    uint32_t u0, u1, u2, u3;
-    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(u0), "=r"(u1), "=r"(u2), "=r"(u3)
-                 : "r"(row_addr + 16 * c));
-    const uint32_t u[4] = {u0, u1, u2, u3};
+__device__ __forceinline__ void load_q(const float* qh, float pre, int t, uint32_t (&qa)[4][4]) {
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[e]));
-      x[2 * e] = f.x;
-      x[2 * e + 1] = f.y;
+  for (int ks = 0; ks < 4; ++ks) {
+    const float* b = qh + 16 * ks;
+    float x0, x1, x2, x3;
+    if (sizeof(T) == 2) {
+      x0 = b[2 * t]; x1 = b[2 * t + 1]; x2 = b[2 * t + 8]; x3 = b[2 * t + 9];
+    } else {
+      x0 = b[t]; x1 = b[4 + t]; x2 = b[8 + t]; x3 = b[12 + t];
+    }
+    if (sizeof(T) == 2) {
+      split_f16x2(x0 * pre, x1 * pre, qa[ks][0], qa[ks][1]);
+      split_f16x2(x2 * pre, x3 * pre, qa[ks][2], qa[ks][3]);
+    } else {
+      split_bf16x2(x0 * pre, x1 * pre, qa[ks][0], qa[ks][1]);
+      split_bf16x2(x2 * pre, x3 * pre, qa[ks][2], qa[ks][3]);
     }
   }
 }
 
-template <typename T>
-__device__ __forceinline__ int slice_dim(int c, int e) {
-  return sizeof(T) == 4 ? (e < 4 ? 4 * c + e : 32 + 4 * c + (e - 4)) : 8 * c + e;
-}
-
-// 4 consecutive dims of a V row, starting at dim 4 * dq
-template <typename T>
-__device__ __forceinline__ float4 load_v4(uint32_t row_addr, int dq) {
-  if (sizeof(T) == 4) return lds128(row_addr + 16 * dq);
-  uint32_t u0, u1;
-  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(u0), "=r"(u1) : "r"(row_addr + 8 * dq));
-  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u0));
-  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u1));
-  return make_float4(a.x, a.y, b.x, b.y);
-}
-
 template <typename T, int LAYOUT>
-__global__ void __launch_bounds__(THREADS, 2) contig_kernel(const Params p) {
+__global__ void __launch_bounds__(THREADS, 1)
+contig_kernel(const Params p, const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v) {
   using G = Geo<T>;
+  constexpr bool F16 = sizeof(T) == 2;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* kv = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-  Tail& t = *reinterpret_cast<Tail*>(kv + KV_BYTES);
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Tail& t = *reinterpret_cast<Tail*>(ring + G::RING_BYTES);
+  static_assert(LAYOUT == kRows || G::TILE == 32, "zone-arena tiles must be page-aligned (32 tokens)");
   const int kvh = blockIdx.x, split = blockIdx.y;
-  const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   int n = p.n;
   if (p.d_len) {
     n = __ldg(p.d_len);
     n = n < 0 ? 0 : (n > p.window ? p.window : n);
   }
-  const int n_tiles = (n + TILE - 1) / TILE;
+  const int n_tiles = (n + G::TILE - 1) / G::TILE;
   const int tb = split * p.tiles_per_split;
   const int my_tiles = max(0, min(n_tiles, tb + p.tiles_per_split) - tb);
 
   if (tid == 0) {
-    for (int s = 0; s < G::STAGES; ++s) mbar_init(&t.full[s], 1);
+    prefetch_tensormap(&map_k);
+    prefetch_tensormap(&map_v);
+    for (int s = 0; s < G::STAGES; ++s) {
+      mbar_init(&t.full[s], 1);
+      mbar_init(&t.empty[s], G::WPT);
+    }
+    t.abort_ = 0;
     fence_barrier_init();
-    for (int k = 0; k < my_tiles && k < G::STAGES; ++k) issue_tile<T, LAYOUT>(p, kv, t, kvh, tb + k, n, k);
   }
-
-  // query slice: thread (token j, slice c) holds q[h][dims of c] * scale * log2(e)
-  const int j = tid >> 3, c = tid & 7;
-  float qr[GROUP][8];
-  {
-    const float* qb = p.q + (int64_t)kvh * GROUP * HD;
-#pragma unroll
-    for (int h = 0; h < GROUP; ++h)
-#pragma unroll
-      for (int e = 0; e < 8; ++e) qr[h][e] = __ldg(qb + h * HD + slice_dim<T>(c, e)) * p.sl2;
-  }
-  __syncthreads();   // barriers initialised
-
-  const int dq = lane & 15, hh = lane >> 4;
-  float o[4][4];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) o[e][0] = o[e][1] = o[e][2] = o[e][3] = 0.f;
-  float M = -INFINITY, l = 0.f;   // softmax state of head w (warp-uniform)
-  int issued = my_tiles < G::STAGES ? my_tiles : G::STAGES;
-  int i = 0;
-  bool aborted = false;
-  for (; i < my_tiles; ++i) {
-    const int st = i % G::STAGES, buf = i & 1;
-    const uint32_t ph = (uint32_t)(i / G::STAGES) & 1u;
-    const bool ok = mbar_wait_bounded(&t.full[st], ph);
-    const int rows = t.rows[st];
-    const uint32_t kbase = smem_u32(kv + st * 2 * G::TILE_BYTES);
-    const uint32_t vbase = kbase + G::TILE_BYTES;
-    // ---- scores: 8 head partials over this thread's 8 dims ----
-    float part[GROUP];
-    {
-      float x[8];
-      load_slice<T>(kbase + j * G::RB, c, x);
-#pragma unroll
-      for (int h = 0; h < GROUP; ++h) {
-        float a = 0.f;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) a = fmaf(qr[h][e], x[e], a);
-        part[h] = a;
-      }
-    }
-    // reduce-scatter over the 8 lanes of the token: lane c ends with head c
-    float r4[4], r2[2];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float send = (c & 4) ? part[e] : part[e + 4];
-      const float keep = (c & 4) ? part[e + 4] : part[e];
-      r4[e] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-    }
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const float send = (c & 2) ? r4[e] : r4[e + 2];
-      const float keep = (c & 2) ? r4[e + 2] : r4[e];
-      r2[e] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
-    }
-    {
-      const float send = (c & 1) ? r2[0] : r2[1];
-      const float keep = (c & 1) ? r2[1] : r2[0];
-      const float s = keep + __shfl_xor_sync(0xffffffffu, send, 1);
-      t.sp[buf][j][c] = j < rows ? s : -INFINITY;
-    }
-    if (__syncthreads_or(!ok)) {   // every reader of stage (i-1) is done here
-      aborted = true;
-      break;
-    }
-    if (tid == 0 && i >= 1 && i - 1 + G::STAGES < my_tiles) {
-      issue_tile<T, LAYOUT>(p, kv, t, kvh, tb + i - 1 + G::STAGES, n, (i - 1) % G::STAGES);
-      ++issued;
-    }
-    // ---- softmax: warp = head, lane = token ----
-    {
-      const float s = t.sp[buf][lane][w];
-      const float mn = fmaxf(M, warp_max(s));
-      float alpha = 1.f, pr = 0.f;
-      if (mn > -INFINITY) {
-        alpha = exp2f(M - mn);
-        pr = exp2f(s - mn);
-      }
-      l = fmaf(l, alpha, warp_sum(pr));
-      M = mn;
-      t.sp[buf][lane][w] = pr;
-      if (lane == 0) t.alpha[buf][w] = alpha;
-    }
-    __syncthreads();
-    // ---- P.V: warp = tokens 4w..4w+3, lane = (dims 4dq.., heads 4hh..) ----
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float a = t.alpha[buf][4 * hh + e];
-      o[e][0] *= a; o[e][1] *= a; o[e][2] *= a; o[e][3] *= a;
-    }
-#pragma unroll
-    for (int jj = 0; jj < 4; ++jj) {
-      const int tok = 4 * w + jj;
-      if (tok >= rows) break;
-      const float4 v = load_v4<T>(vbase + tok * G::RB, dq);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float pe = t.sp[buf][tok][4 * hh + e];
-        o[e][0] = fmaf(pe, v.x, o[e][0]);
-        o[e][1] = fmaf(pe, v.y, o[e][1]);
-        o[e][2] = fmaf(pe, v.z, o[e][2]);
-        o[e][3] = fmaf(pe, v.w, o[e][3]);
-      }
-    }
-  }
-  if (aborted) {
-    // a copy never landed: wait (bounded) for the copies this CTA issued, then
-    // publish an empty partial so the merge counters stay consistent
-    record_error(p.err, kErrWaitTimeout);
-    if (tid == 0)
-      for (int k = i; k < issued; ++k) mbar_wait_bounded(&t.full[k % G::STAGES], (uint32_t)(k / G::STAGES) & 1u);
-    M = -INFINITY;
-    l = 0.f;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) o[e][0] = o[e][1] = o[e][2] = o[e][3] = 0.f;
-  }
-  __syncthreads();   // the stage ring is free: sum the 8 warps' accumulators there
-  float* red = reinterpret_cast<float*>(kv);   // [warp][head][64]
-#pragma unroll
-  for (int e = 0; e < 4; ++e)
-    *reinterpret_cast<float4*>(red + (w * GROUP + 4 * hh + e) * HD + 4 * dq) =
-        make_float4(o[e][0], o[e][1], o[e][2], o[e][3]);
   __syncthreads();
-  float2 acc = make_float2(0.f, 0.f);
+
+  const int g = lane >> 2, tg = lane & 3;
+  float o[8][4];
 #pragma unroll
-  for (int ww = 0; ww < 8; ++ww) {
-    const float2 x = *reinterpret_cast<const float2*>(red + (ww * GROUP + w) * HD + 2 * lane);
-    acc.x += x.x;
-    acc.y += x.y;
+  for (int nt = 0; nt < 8; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+  float m = -INFINITY, l = 0.f;   // head g: reference max (log2 units), this lane's share of the sum
+
+  if (warp == NCW) {
+    // ================= producer =================
+    if (lane == 0) {
+      int issued = 0;
+      for (int k = 0; k < my_tiles; ++k) {
+        const int st = k % G::STAGES;
+        if (k >= G::STAGES && !wait_stage(&t.empty[st], (uint32_t)((k / G::STAGES) - 1) & 1u, &t.abort_)) {
+          record_error(p.err, kErrWaitTimeout);
+          atomicExch(&t.abort_, 1);
+          break;
+        }
+        const int t0 = (tb + k) * G::TILE;
+        int rows = min(G::TILE, n - t0);
+        const int64_t r0 = tile_row<LAYOUT>(p, kvh, t0);
+        if (r0 < 0) {
+          record_error(p.err, kErrPageRange);
+          rows = 0;
+        }
+        t.rows[st] = rows;
+        if (rows > 0) {
+          fence_proxy_async_smem();
+          mbar_arrive_expect_tx(&t.full[st], (uint32_t)G::STAGE_BYTES);
+          copy_tile<T>(ring + st * G::STAGE_BYTES, &map_k, &map_v, (int32_t)r0, &t.full[st]);
+        } else {
+          mbar_arrive(&t.full[st]);
+        }
+        issued = k + 1;
+      }
+      if (t.abort_) {   // the copies in flight must land before the CTA leaves
+        for (int k = max(0, issued - G::STAGES); k < issued; ++k)
+          mbar_wait_bounded(&t.full[k % G::STAGES], (uint32_t)(k / G::STAGES) & 1u);
+      }
+    }
+  } else {
+    // ====== consumers: tile k -> warp group k % GROUPS, warp sub of the group takes
+    // ====== tokens [32 sub, 32 sub + 32) of the tile
+    uint32_t qa[4][4];
+    load_q<T>(p.q + ((int64_t)kvh * GROUP + g) * HD, p.sl2 * (F16 ? Q_PRE : 1.0f), tg, qa);
+    const float s_post = F16 ? 1.0f / Q_PRE : 1.0f;
+    const float p_pre = F16 ? P_PRE : 1.0f;
+    const int r8 = lane & 7, j4 = lane >> 3;
+    const int grp = warp / G::WPT, sub = warp % G::WPT;
+    for (int k = grp; k < my_tiles; k += G::GROUPS) {
+      const int st = k % G::STAGES;
+      const bool ok = wait_stage(&t.full[st], (uint32_t)(k / G::STAGES) & 1u, &t.abort_);
+      if (!__all_sync(0xffffffffu, ok)) {
+        record_error(p.err, kErrWaitTimeout);
+        if (lane == 0) atomicExch(&t.abort_, 1);
+        break;
+      }
+      const int nv = min(SUB, max(0, t.rows[st] - SUB * sub));   // valid rows of this warp's 32
+      // this warp's 32 rows start 4 KB (f16) into the tile: a multiple of the
+      // 1024-byte swizzle period, so the in-tile row index keeps its phase
+      const uint32_t kb = smem_u32(ring + st * G::STAGE_BYTES) + sub * SUB * 128, vb = kb + G::TILE_BYTES;
+      if (nv == 0) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&t.empty[st]);
+        continue;
+      }
+      // ---- K fragments ----
+      uint32_t kf[4][4][2];   // [nt][ks] f16: B fragments of K
+      float kx[4][4][4];      // [nt][ks] f32: K[8nt+g][16ks + 4j + tg], j = 0..3
+      if (F16) {
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+          for (int kp = 0; kp < 2; ++kp) {
+            const int tok = 8 * nt + r8, chunk = 4 * kp + j4;
+            ldsm_x4(kb + tok * 128 + ((chunk ^ r8) << 4), kf[nt][2 * kp][0], kf[nt][2 * kp][1],
+                    kf[nt][2 * kp + 1][0], kf[nt][2 * kp + 1][1]);
+          }
+      } else {
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            const int tok = 8 * nt + r8, chunk = 4 * (ks & 1) + j4;
+            uint32_t a, b, c, d;
+            ldsm_x4(kb + (ks >> 1) * (SUB * 128) + tok * 128 + ((chunk ^ r8) << 4), a, b, c, d);
+            kx[nt][ks][0] = __uint_as_float(a);
+            kx[nt][ks][1] = __uint_as_float(b);
+            kx[nt][ks][2] = __uint_as_float(c);
+            kx[nt][ks][3] = __uint_as_float(d);
+          }
+      }
+      // ---- S = Q K^T: head g, tokens 8nt + 2tg + {0, 1} ----
+      float sc[4][4];
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+          if (F16) {
+            mma_f16(sc[nt], qa[ks], kf[nt][ks][0], kf[nt][ks][1]);
+          } else {
+            uint32_t bh0, bl0, bh1, bl1;
+            split_bf16x2(kx[nt][ks][0], kx[nt][ks][1], bh0, bl0);
+            split_bf16x2(kx[nt][ks][2], kx[nt][ks][3], bh1, bl1);
+            mma_bf16(sc[nt], qa[ks], bh0, bh1);
+            mma_bf16(sc[nt], qa[ks], bl0, bl1);
+          }
+        }
+      // ---- V fragments, then hand the stage back ----
+      uint32_t vf16[2][8][2]; // [kk][nt] f16: B fragments of V
+      float vx[2][8][4];      // [kk][nt] f32: V[16kk + 2tg + {0,1,8,9}][8nt + g]
+      if (F16) {
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk)
+#pragma unroll
+          for (int np = 0; np < 4; ++np) {
+            const int tok = 16 * kk + 8 * (j4 & 1) + r8, chunk = 2 * np + (j4 >> 1);
+            ldsm_x4_t(vb + tok * 128 + ((chunk ^ r8) << 4), vf16[kk][2 * np][0], vf16[kk][2 * np][1],
+                      vf16[kk][2 * np + 1][0], vf16[kk][2 * np + 1][1]);
+          }
+      } else {
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk)
+#pragma unroll
+          for (int nt = 0; nt < 8; ++nt) {
+            const int f = 8 * nt + g, chunk = (f & 31) >> 2;
+            const uint32_t col = vb + (f >> 5) * (SUB * 128) + 4 * (f & 3);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int tok = 16 * kk + 2 * tg + (e & 1) + 8 * (e >> 1);
+              vx[kk][nt][e] = lds32(col + tok * 128 + ((chunk ^ (tok & 7)) << 4));
+            }
+          }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&t.empty[st]);
+      float sv[4][2];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float v = (sc[nt][e] + sc[nt][e + 2]) * s_post;
+          sv[nt][e] = (8 * nt + 2 * tg + e < nv) ? v : -INFINITY;
+          mx = fmaxf(mx, sv[nt][e]);
+        }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      // ---- online softmax: the reference max moves only when passed by RESCALE_AT ----
+      if (mx > m + RESCALE_AT) {
+        const float al = exp2f(m - mx);   // 0 on the first tile (m = -inf)
+        l *= al;
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+          o[nt][0] *= al; o[nt][1] *= al; o[nt][2] *= al; o[nt][3] *= al;
+        }
+        m = mx;
+      }
+      const bool live = m > -INFINITY;   // false only while every score of head g is -inf
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        sv[nt][0] = live ? exp2f(sv[nt][0] - m) : 0.f;
+        sv[nt][1] = live ? exp2f(sv[nt][1] - m) : 0.f;
+        l += sv[nt][0] + sv[nt][1];
+      }
+      // ---- O += P V: k = tokens (2 steps of 16), n = dims (8 tiles of 8) ----
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk) {
+        if (16 * kk >= nv) break;
+        uint32_t pa[4];
+        if (F16) {
+          split_f16x2(sv[2 * kk][0] * p_pre, sv[2 * kk][1] * p_pre, pa[0], pa[1]);
+          split_f16x2(sv[2 * kk + 1][0] * p_pre, sv[2 * kk + 1][1] * p_pre, pa[2], pa[3]);
+        } else {
+          split_bf16x2(sv[2 * kk][0], sv[2 * kk][1], pa[0], pa[1]);
+          split_bf16x2(sv[2 * kk + 1][0], sv[2 * kk + 1][1], pa[2], pa[3]);
+        }
+        // rows past the sequence end may hold anything: P is 0 there, V must be finite
+        const int r = 16 * kk + 2 * tg;
+        const bool ragged = nv < 16 * kk + 16;
+        if (F16) {
+          const uint32_t m0 = (r < nv ? 0x0000ffffu : 0u) | (r + 1 < nv ? 0xffff0000u : 0u);
+          const uint32_t m1 = (r + 8 < nv ? 0x0000ffffu : 0u) | (r + 9 < nv ? 0xffff0000u : 0u);
+#pragma unroll
+          for (int nt = 0; nt < 8; ++nt) {
+            uint32_t b0 = vf16[kk][nt][0], b1 = vf16[kk][nt][1];
+            if (ragged) {
+              b0 &= m0;
+              b1 &= m1;
+            }
+            mma_f16(o[nt], pa, b0, b1);
+          }
+        } else {
+#pragma unroll
+          for (int nt = 0; nt < 8; ++nt) {
+            float v0 = vx[kk][nt][0], v1 = vx[kk][nt][1], v2 = vx[kk][nt][2], v3 = vx[kk][nt][3];
+            if (ragged) {
+              if (r >= nv) v0 = 0.f;
+              if (r + 1 >= nv) v1 = 0.f;
+              if (r + 8 >= nv) v2 = 0.f;
+              if (r + 9 >= nv) v3 = 0.f;
+            }
+            uint32_t bh0, bl0, bh1, bl1;
+            split_bf16x2(v0, v1, bh0, bl0);
+            split_bf16x2(v2, v3, bh1, bl1);
+            mma_bf16(o[nt], pa, bh0, bh1);
+            mma_bf16(o[nt], pa, bl0, bl1);
+          }
+        }
+      }
+    }
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
   }
-  // thread (head w, dims 2*lane, 2*lane+1); (M, l) of head w are this warp's
-  const int h = w;
+  __syncthreads();   // every copy has landed and been read: the ring is free
+
+  // ---- fold the 8 warps: [warp][head][64] partials and (m, l) in the ring ----
+  float* wo = reinterpret_cast<float*>(ring);                              // 16 KB
+  float2* wml = reinterpret_cast<float2*>(ring + NCW * GROUP * HD * 4);    // 512 B
+  if (warp < NCW) {
+    const float post = F16 ? 1.0f / P_PRE : 1.0f;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+      *reinterpret_cast<float2*>(wo + (warp * GROUP + g) * HD + 8 * nt + 2 * tg) =
+          make_float2((o[nt][0] + o[nt][2]) * post, (o[nt][1] + o[nt][3]) * post);
+    if (tg == 0) wml[warp * GROUP + g] = make_float2(m, l);
+  }
+  __syncthreads();
+  const int h = warp;   // fold, publish and merge: warp = head (consumer warps only)
+  float M = -INFINITY, L = 0.f;
+  float2 acc = make_float2(0.f, 0.f);
+  if (warp < NCW) {
+#pragma unroll
+    for (int w = 0; w < NCW; ++w) M = fmaxf(M, wml[w * GROUP + h].x);
+#pragma unroll
+    for (int w = 0; w < NCW; ++w) {
+      const float2 x = wml[w * GROUP + h];
+      const float sw = (M > -INFINITY && x.x > -INFINITY) ? exp2f(x.x - M) : 0.f;
+      const float2 ov = *reinterpret_cast<const float2*>(wo + (w * GROUP + h) * HD + 2 * lane);
+      L = fmaf(sw, x.y, L);
+      acc.x = fmaf(sw, ov.x, acc.x);
+      acc.y = fmaf(sw, ov.y, acc.y);
+    }
+  }
   float* dst = p.out + ((int64_t)kvh * GROUP + h) * HD + 2 * lane;
   if (p.n_splits == 1) {
-    const float inv = l > 0.f ? 1.0f / l : 0.f;
-    *reinterpret_cast<float2*>(dst) = make_float2(acc.x * inv, acc.y * inv);
+    if (warp < NCW) {
+      const float inv = L > 0.f ? 1.0f / L : 0.f;
+      *reinterpret_cast<float2*>(dst) = make_float2(acc.x * inv, acc.y * inv);
+    }
     return;
   }
   const int64_t slot = (int64_t)kvh * p.n_splits + split;
-  __stcg(reinterpret_cast<float2*>(p.part_o + (slot * GROUP + h) * HD + 2 * lane), acc);
-  if (lane == 0) __stcg(&p.part_ml[slot * GROUP + h], make_float2(M, l));
+  if (warp < NCW) {
+    __stcg(reinterpret_cast<float2*>(p.part_o + (slot * GROUP + h) * HD + 2 * lane), acc);
+    if (lane == 0) __stcg(&p.part_ml[slot * GROUP + h], make_float2(M, L));
+  }
   __threadfence();
   __syncthreads();
   if (tid == 0) {
@@ -347,10 +483,10 @@ __global__ void __launch_bounds__(THREADS, 2) contig_kernel(const Params p) {
     t.last = last;
   }
   __syncthreads();
-  if (!t.last) return;
+  if (!t.last || warp >= NCW) return;
   __threadfence();
-  // ---- merge the splits of this KV head: warp = head ----
-  float* wgt = reinterpret_cast<float*>(kv + GROUP * GROUP * HD * sizeof(float)) + h * MAX_SPLITS;
+  // ---- last CTA of this KV head: merge the splits, warp = head ----
+  float* wgt = reinterpret_cast<float*>(ring + 32 * 1024) + h * MAX_SPLITS;
   const int S = p.n_splits;
   const float2* ml = p.part_ml + (int64_t)kvh * S * GROUP + h;
   float mx = -INFINITY;
@@ -368,6 +504,17 @@ __global__ void __launch_bounds__(THREADS, 2) contig_kernel(const Params p) {
   const float* po = p.part_o + ((int64_t)kvh * S * GROUP + h) * HD + 2 * lane;
   float2 r = make_float2(0.f, 0.f);
   int s = 0;
+  for (; s + 32 <= S; s += 32) {   // all loads of a round in flight together
+    float2 x[32];
+#pragma unroll
+    for (int u = 0; u < 32; ++u) x[u] = __ldcg(reinterpret_cast<const float2*>(po + (int64_t)(s + u) * GROUP * HD));
+#pragma unroll
+    for (int u = 0; u < 32; ++u) {
+      const float wv = wgt[s + u];
+      r.x = fmaf(wv, x[u].x, r.x);
+      r.y = fmaf(wv, x[u].y, r.y);
+    }
+  }
   for (; s + 8 <= S; s += 8) {
     float2 x[8];
 #pragma unroll
@@ -393,8 +540,12 @@ struct Plan {
   int n_splits, tiles_per_split;
 };
 
-Plan plan(int n_kv, int max_tokens) {
-  const int tiles = max_tokens > 0 ? (max_tokens + TILE - 1) / TILE : 1;
+// Splits per KV head: one CTA per SM over all heads, as long as every split
+// has a tile.  Short contexts gain from the widest spread (a single SM pulls
+// a few hundred KB at well under its share of HBM bandwidth) more than they
+// lose to the longer merge.
+Plan plan(int n_kv, int max_tokens, int tile) {
+  const int tiles = max_tokens > 0 ? (max_tokens + tile - 1) / tile : 1;
   int per_head = TARGET_CTAS / n_kv;
   if (per_head < 1) per_head = 1;
   int s = tiles < per_head ? tiles : per_head;
@@ -407,22 +558,44 @@ size_t al(size_t x) { return (x + 255) & ~size_t(255); }
 
 size_t counters_bytes(int n_kv) { return al((size_t)n_kv * sizeof(int32_t)); }
 
+// sized for the most splits any element type plans, so one size serves f16 and f32
 size_t workspace_bytes(int n_kv, int max_tokens) {
-  const Plan pl = plan(n_kv, max_tokens);
+  const Plan pl = plan(n_kv, max_tokens, SUB);
   const size_t slots = (size_t)n_kv * pl.n_splits * GROUP;
   return counters_bytes(n_kv) + al(slots * sizeof(float2)) + al(slots * HD * sizeof(float));
 }
 
+// Tensor maps over `rows` rows of 64 elements: f16 (x 64, row), box 64 x 64;
+// f32 (x 32, row, 128-byte half), box 32 x 32 x 2; 128-byte swizzle.
+template <typename T>
+int32_t row_map(CUtensorMap* m, const void* base, uint64_t rows) {
+  if (sizeof(T) == 2)
+    return encode_rows_tmap(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, HD, rows, HD, Geo<T>::TILE,
+                            CU_TENSOR_MAP_SWIZZLE_128B);
+  const uint64_t dims[3] = {32, rows, 2};
+  const uint64_t strides[2] = {HD * 4, 128};
+  const uint32_t box[3] = {32, (uint32_t)Geo<T>::TILE, 2};
+  return encode_tmap(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 template <typename T, int LAYOUT>
-int32_t launch(Params p, int max_tokens, void* ws, size_t ws_bytes, cudaStream_t stream) {
+int32_t launch(Params p, const void* k, const void* v, uint64_t rows, int max_tokens, void* ws, size_t ws_bytes,
+               cudaStream_t stream) {
   if (p.n_kv <= 0 || p.n_kv > 65535) return fail(NYION_ERR_INVALID, "row decode: bad n_kv_heads %d", p.n_kv);
-  if ((reinterpret_cast<uintptr_t>(p.k) | reinterpret_cast<uintptr_t>(p.v)) & 15)
+  if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15)
     return fail(NYION_ERR_INVALID, "row decode: K/V must be 16-byte aligned");
   if (reinterpret_cast<uintptr_t>(p.out) & 7) return fail(NYION_ERR_INVALID, "row decode: out must be 8-byte aligned");
+  if (rows == 0 || rows >= (1ull << 31)) return fail(NYION_ERR_INVALID, "row decode: %llu rows (limit 2^31)",
+                                                     (unsigned long long)rows);
   DeviceInfo* dev = nullptr;
   int32_t st = device_info(&dev);
   if (st) return st;
-  const Plan pl = plan(p.n_kv, max_tokens);
+  CUtensorMap mk, mv;
+  st = row_map<T>(&mk, k, rows);
+  if (st) return st;
+  st = row_map<T>(&mv, v, rows);
+  if (st) return st;
+  const Plan pl = plan(p.n_kv, max_tokens, Geo<T>::TILE);
   const size_t need = workspace_bytes(p.n_kv, max_tokens);
   if (!ws) {
     st = internal_workspace(need, &ws, kWsCounters, counters_bytes(p.n_kv), stream);
@@ -434,7 +607,7 @@ int32_t launch(Params p, int max_tokens, void* ws, size_t ws_bytes, cudaStream_t
   const int di = dev->device < 64 ? dev->device : 0;
   if (!attr_set[di]) {
     st = check_cuda(cudaFuncSetAttribute(contig_kernel<T, LAYOUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem_bytes()),
+                                         (int)smem_bytes<T>()),
                     "cudaFuncSetAttribute(row decode)");
     if (st) return st;
     attr_set[di] = true;
@@ -447,7 +620,8 @@ int32_t launch(Params p, int max_tokens, void* ws, size_t ws_bytes, cudaStream_t
   p.part_ml = reinterpret_cast<float2*>(base + counters_bytes(p.n_kv));
   p.part_o = reinterpret_cast<float*>(base + counters_bytes(p.n_kv) + al(slots * sizeof(float2)));
   p.err = dev->err_word;
-  contig_kernel<T, LAYOUT><<<dim3((unsigned)p.n_kv, (unsigned)pl.n_splits), THREADS, smem_bytes(), stream>>>(p);
+  contig_kernel<T, LAYOUT>
+      <<<dim3((unsigned)p.n_kv, (unsigned)pl.n_splits), THREADS, smem_bytes<T>(), stream>>>(p, mk, mv);
   return check_cuda(cudaGetLastError(), "row decode launch");
 }
 
@@ -459,14 +633,12 @@ int32_t contig_rows_f32(const float* q, const float* k, const float* v, float* o
                         float sl2, void* ws, size_t ws_bytes, cudaStream_t stream) {
   contig::Params p{};
   p.q = q;
-  p.k = k;
-  p.v = v;
   p.out = out;
   p.stride = stride;
   p.n_kv = n_kv;
   p.n = n;
   p.sl2 = sl2;
-  return contig::launch<float, contig::kRows>(p, n, ws, ws_bytes, stream);
+  return contig::launch<float, contig::kRows>(p, k, v, (uint64_t)n_kv * (uint64_t)stride, n, ws, ws_bytes, stream);
 }
 
 int32_t contig_rows_f16(const float* q, const void* k, const void* v, float* out, int n_kv, int64_t stride, int n,
@@ -474,8 +646,6 @@ int32_t contig_rows_f16(const float* q, const void* k, const void* v, float* out
                         cudaStream_t stream) {
   contig::Params p{};
   p.q = q;
-  p.k = k;
-  p.v = v;
   p.out = out;
   p.stride = stride;
   p.n_kv = n_kv;
@@ -483,7 +653,8 @@ int32_t contig_rows_f16(const float* q, const void* k, const void* v, float* out
   p.d_len = d_len;
   p.window = window;
   p.sl2 = sl2;
-  return contig::launch<__half, contig::kRows>(p, d_len ? window : n, ws, ws_bytes, stream);
+  return contig::launch<__half, contig::kRows>(p, k, v, (uint64_t)n_kv * (uint64_t)stride, d_len ? window : n, ws,
+                                               ws_bytes, stream);
 }
 
 int32_t contig_zoned_f32(const float* q, const float* k_arena, const float* v_arena, float* out, int n_kv,
@@ -491,8 +662,6 @@ int32_t contig_zoned_f32(const float* q, const float* k_arena, const float* v_ar
                          cudaStream_t stream) {
   contig::Params p{};
   p.q = q;
-  p.k = k_arena;
-  p.v = v_arena;
   p.out = out;
   p.n_kv = n_kv;
   p.n = n;
@@ -500,7 +669,13 @@ int32_t contig_zoned_f32(const float* q, const float* k_arena, const float* v_ar
   p.layer = layer;
   p.n_pages = n_pages;
   p.sl2 = sl2;
-  return contig::launch<float, contig::kZoned>(p, n, ws, ws_bytes, stream);
+  // rows in the arena: zone pages [0, n_pages) of 32 / 128 / 1024 slots
+  const int64_t lp = (int64_t)n_layers * n_kv;
+  const int64_t z0 = n_pages < 128 ? n_pages : 128;
+  const int64_t z1 = n_pages - z0 < 992 ? n_pages - z0 : 992;
+  const int64_t z2 = n_pages - z0 - z1;
+  const uint64_t rows = (uint64_t)(z0 * 32 + z1 * 128 + z2 * 1024) * (uint64_t)lp;
+  return contig::launch<float, contig::kZoned>(p, k_arena, v_arena, rows, n, ws, ws_bytes, stream);
 }
 
 }  // namespace nyion

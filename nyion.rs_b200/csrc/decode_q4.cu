@@ -207,31 +207,9 @@ __device__ __forceinline__ uint32_t nib2h(uint32_t w) {
   return (x & 0x03C003C0u) | 0x3C003C00u;
 }
 
-__device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, "
-      "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ void split_f16x2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
-  const __half2 h = __floats2half2_rn(x0, x1);
-  hi = *reinterpret_cast<const uint32_t*>(&h);
-  const float2 hf = __half22float2(h);
-  const __half2 r = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
-  lo = *reinterpret_cast<const uint32_t*>(&r);
-}
-
 __device__ __forceinline__ float2 hdr2f(uint32_t w) {   // (d, dmin) of a block header word
   return make_float2(__half2float(__ushort_as_half((unsigned short)(w & 0xffffu))),
                      __half2float(__ushort_as_half((unsigned short)(w >> 16))));
-}
-
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                          uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
 }
 
 __device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
