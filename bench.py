@@ -380,6 +380,61 @@ def run_config4(A, torch, dev, stream, args):
             "launches_per_step": T // CH, "device_error": A.device_error(stream)}
 
 
+def run_row_caches(A, torch, dev, stream, args):
+    """The reference's own GPU decode path on B200: the layer-graph attention
+    node over 22 layers' f16 rings of window 4096 (length read on the device),
+    and the contiguous f32 cache of gpu_attention_streamed at ctx 12000; CUDA
+    graph of 22 calls, 256 MB L2 flush before every timed replay."""
+    W, T32 = 4096, 12000
+    gen = torch.Generator(device=dev).manual_seed(606)
+    q = torch.randn(H, D, device=dev, generator=gen)
+    out = torch.empty(H, D, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    rings = [(torch.randn(N_KV, W, D, device=dev, generator=gen).half(),
+              torch.randn(N_KV, W, D, device=dev, generator=gen).half()) for _ in range(LAYERS)]
+    d_len = torch.full((1,), W, dtype=torch.int32, device=dev)
+    ws = A.F16Workspace(H, W, device=dev)
+    caches = [(torch.randn(N_KV, T32, D, device=dev, generator=gen),
+               torch.randn(N_KV, T32, D, device=dev, generator=gen)) for _ in range(4)]
+    L = A.lib()
+    res = {}
+    legs = {
+        "ring_f16_window_4096": (lambda i: A.decode_ring_f16(q, rings[i][0], rings[i][1], d_len, out=out,
+                                                             workspace=ws, stream=stream),
+                                 2 * N_KV * W * D * 2),
+        "contig_f32_ctx_12000": (lambda i: L.gpu_attention_streamed(
+            q.data_ptr(), caches[i % 4][0].data_ptr(), caches[i % 4][1].data_ptr(), out.data_ptr(), H, N_KV, T32, D,
+            T32, stream.cuda_stream), 2 * N_KV * T32 * D * 4),
+    }
+    peak = float(peaks_all().get("hbm_gbs") or 6650.0)
+    for name, (call, nbytes) in legs.items():
+        with torch.cuda.stream(stream):
+            for _ in range(max(3, args.warmup)):
+                for i in range(LAYERS):
+                    call(i)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for i in range(LAYERS):
+                    call(i)
+            torch.cuda.synchronize()
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(args.steps)]
+            for e0, e1 in evs:
+                flush.fill_(1)
+                e0.record(stream)
+                g.replay()
+                e1.record(stream)
+            torch.cuda.synchronize()
+        us = sum(e0.elapsed_time(e1) for e0, e1 in evs) / len(evs) * 1e3 / LAYERS
+        gbs = nbytes / (us * 1e-6) / 1e9
+        res[name] = {"us_per_call": us, "gbs": gbs, "bytes_per_call": nbytes,
+                     "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak},
+                     "timing": f"graph of {LAYERS} calls, 256 MB L2 flush before each replay", "launches_per_call": 1}
+        del g
+    res["device_error"] = A.device_error(stream)
+    return res
+
+
 def run_config5(A, S, torch, dev, stream, args, barrier, dist, world, rank):
     """Config 5: B=1, 1M-token Q4 context split evenly over the ranks (strong
     scaling).  Timed path: the fused exchange (the reduce kernel writes each
@@ -434,6 +489,8 @@ def run_gpu(args, rank, world):
             r = run_config3(A, torch, dev, st, args, bar, dist_, world)
         elif args.only == "config4":
             r = run_config4(A, torch, dev, st, args)
+        elif args.only == "rows":
+            r = run_row_caches(A, torch, dev, st, args)
         else:
             r = run_config5(A, S, torch, dev, st, args, bar, dist_, world, rank)
         if rank == 0:
@@ -572,6 +629,7 @@ def run_gpu(args, rank, world):
                                                         not args.no_cpu)
             extra["q4_window_ring"] = run_config3(A, torch, dev, stream, args, barrier, dist, world)
             extra["prefill_2048"] = run_config4(A, torch, dev, stream, args)
+            extra["reference_gpu_path"] = run_row_caches(A, torch, dev, stream, args)
         extra["split_kv_1m"] = run_config5(A, S, torch, dev, stream, args, barrier, dist, world, rank)
 
     step_bytes = layer_step_bytes() * LAYERS
@@ -622,7 +680,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the config 3 / config 5 legs")
-    ap.add_argument("--only", choices=["config3", "config4", "config5"], default=None,
+    ap.add_argument("--only", choices=["config3", "config4", "config5", "rows"], default=None,
                     help="profiling runs: time only this leg (prints its JSON object)")
     ap.add_argument("--cpu-seconds", type=float, default=6.0)
     ap.add_argument("--layers", type=int, default=LAYERS,

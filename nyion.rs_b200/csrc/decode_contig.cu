@@ -194,16 +194,6 @@ contig_kernel(const Params p, const __grid_constant__ CUtensorMap map_k, const _
   static_assert(LAYOUT == kRows || G::TILE == 32, "zone-arena tiles must be page-aligned (32 tokens)");
   const int kvh = blockIdx.x, split = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-
-  int n = p.n;
-  if (p.d_len) {
-    n = __ldg(p.d_len);
-    n = n < 0 ? 0 : (n > p.window ? p.window : n);
-  }
-  const int n_tiles = (n + G::TILE - 1) / G::TILE;
-  const int tb = split * p.tiles_per_split;
-  const int my_tiles = max(0, min(n_tiles, tb + p.tiles_per_split) - tb);
-
   if (tid == 0) {
     prefetch_tensormap(&map_k);
     prefetch_tensormap(&map_v);
@@ -214,6 +204,22 @@ contig_kernel(const Params p, const __grid_constant__ CUtensorMap map_k, const _
     t.abort_ = 0;
     fence_barrier_init();
   }
+  // programmatic dependent launch: the set-up above overlaps the previous
+  // grid; nothing global is read before that grid has completed and flushed
+  // (the K/V rows, q and the device length may be its outputs), and the next
+  // grid may start its own set-up now (our kernels wait the same way before
+  // reading anything)
+  pdl_wait();
+
+  int n = p.n;
+  if (p.d_len) {
+    n = __ldg(p.d_len);
+    n = n < 0 ? 0 : (n > p.window ? p.window : n);
+  }
+  const int n_tiles = (n + G::TILE - 1) / G::TILE;
+  const int tb = split * p.tiles_per_split;
+  const int my_tiles = max(0, min(n_tiles, tb + p.tiles_per_split) - tb);
+
   __syncthreads();
 
   const int g = lane >> 2, tg = lane & 3;
@@ -486,9 +492,16 @@ contig_kernel(const Params p, const __grid_constant__ CUtensorMap map_k, const _
   if (!t.last || warp >= NCW) return;
   __threadfence();
   // ---- last CTA of this KV head: merge the splits, warp = head ----
+  // The first 32 splits' o rows are loaded before the weights are known, so
+  // their loads and the (m, l) loads share one L2 round trip.
   float* wgt = reinterpret_cast<float*>(ring + 32 * 1024) + h * MAX_SPLITS;
   const int S = p.n_splits;
   const float2* ml = p.part_ml + (int64_t)kvh * S * GROUP + h;
+  const float* po = p.part_o + ((int64_t)kvh * S * GROUP + h) * HD + 2 * lane;
+  float2 x[32];
+#pragma unroll
+  for (int u = 0; u < 32; ++u)
+    x[u] = u < S ? __ldcg(reinterpret_cast<const float2*>(po + (int64_t)u * GROUP * HD)) : make_float2(0.f, 0.f);
   float mx = -INFINITY;
   for (int s = lane; s < S; s += 32) mx = fmaxf(mx, __ldcg(ml + (int64_t)s * GROUP).x);
   mx = warp_max(mx);
@@ -501,36 +514,32 @@ contig_kernel(const Params p, const __grid_constant__ CUtensorMap map_k, const _
   }
   den = warp_sum(den);
   __syncwarp();
-  const float* po = p.part_o + ((int64_t)kvh * S * GROUP + h) * HD + 2 * lane;
   float2 r = make_float2(0.f, 0.f);
-  int s = 0;
-  for (; s + 32 <= S; s += 32) {   // all loads of a round in flight together
-    float2 x[32];
 #pragma unroll
-    for (int u = 0; u < 32; ++u) x[u] = __ldcg(reinterpret_cast<const float2*>(po + (int64_t)(s + u) * GROUP * HD));
-#pragma unroll
-    for (int u = 0; u < 32; ++u) {
-      const float wv = wgt[s + u];
+  for (int u = 0; u < 32; ++u) {
+    if (u < S) {
+      const float wv = wgt[u];
       r.x = fmaf(wv, x[u].x, r.x);
       r.y = fmaf(wv, x[u].y, r.y);
     }
   }
+  int s = 32;
   for (; s + 8 <= S; s += 8) {
-    float2 x[8];
+    float2 y[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) x[u] = __ldcg(reinterpret_cast<const float2*>(po + (int64_t)(s + u) * GROUP * HD));
+    for (int u = 0; u < 8; ++u) y[u] = __ldcg(reinterpret_cast<const float2*>(po + (int64_t)(s + u) * GROUP * HD));
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const float wv = wgt[s + u];
-      r.x = fmaf(wv, x[u].x, r.x);
-      r.y = fmaf(wv, x[u].y, r.y);
+      r.x = fmaf(wv, y[u].x, r.x);
+      r.y = fmaf(wv, y[u].y, r.y);
     }
   }
   for (; s < S; ++s) {
-    const float2 x = __ldcg(reinterpret_cast<const float2*>(po + (int64_t)s * GROUP * HD));
+    const float2 y = __ldcg(reinterpret_cast<const float2*>(po + (int64_t)s * GROUP * HD));
     const float wv = wgt[s];
-    r.x = fmaf(wv, x.x, r.x);
-    r.y = fmaf(wv, x.y, r.y);
+    r.x = fmaf(wv, y.x, r.x);
+    r.y = fmaf(wv, y.y, r.y);
   }
   const float inv = den > 0.f ? 1.0f / den : 0.f;
   *reinterpret_cast<float2*>(dst) = make_float2(r.x * inv, r.y * inv);
@@ -620,9 +629,9 @@ int32_t launch(Params p, const void* k, const void* v, uint64_t rows, int max_to
   p.part_ml = reinterpret_cast<float2*>(base + counters_bytes(p.n_kv));
   p.part_o = reinterpret_cast<float*>(base + counters_bytes(p.n_kv) + al(slots * sizeof(float2)));
   p.err = dev->err_word;
-  contig_kernel<T, LAYOUT>
-      <<<dim3((unsigned)p.n_kv, (unsigned)pl.n_splits), THREADS, smem_bytes<T>(), stream>>>(p, mk, mv);
-  return check_cuda(cudaGetLastError(), "row decode launch");
+  return check_cuda(launch_pdl(contig_kernel<T, LAYOUT>, dim3((unsigned)p.n_kv, (unsigned)pl.n_splits),
+                              dim3(THREADS), smem_bytes<T>(), stream, p, mk, mv),
+                    "row decode launch");
 }
 
 }  // namespace contig
