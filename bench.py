@@ -326,7 +326,7 @@ def run_config3(A, torch, dev, stream, args, barrier, dist, world):
     total = q4_bytes + ring_bytes + qo
     return {"workload": "config3: B=16, Q4 window 4096 of 65536 + fp32 ring 128", "us_per_layer_step": ms * 1e3,
             "gbs": total / (ms * 1e-3) / 1e9, "bytes_per_layer_step": total, "timing": mode,
-            "launches_per_step": 3}
+            "launches_per_step": 2}
 
 
 def prefill_flops(total=2048, heads=H, hd=D) -> int:

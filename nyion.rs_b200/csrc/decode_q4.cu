@@ -625,36 +625,34 @@ struct RingArgs {
   const int32_t* seq_lens; // [batch]
   int32_t ring_tokens, window;
   float qscale;            // scale * log2(e)
-  float* ring_part;        // [batch][H][HD + 2]: o (relative to m), m (log2), l of the ring tokens
 };
 
 constexpr int RING_MAX = 128;   // ring tokens of one sequence (larger rings: error)
 
 // fp32 ring tokens [max(max(0, L - window), L - ring), L) of config 3 (slot pos %
-// ring): CTA = (sequence, KV head, 128-token part), all 8 query heads of the group.
+// ring), one (sequence, KV head) per CTA, all 8 query heads of the group.
 // Scores: thread = (token, half row): one batch of eight 16-byte K loads, dots for
 // the 8 heads against q in shared memory, halves joined by a shuffle.  Softmax:
 // warp = head.  P.V: thread = (dim pair, 16-token group): one batch of sixteen
-// 8-byte V loads, 8 heads accumulated, the 8 groups summed through shared memory.
-// Launched after the 4-bit decode with programmatic dependent launch: its CTAs
-// start as decode CTAs leave the SMs (its inputs are complete: the decode
-// releases it only after its own wait on the grid before it), and it waits for
-// the decode to complete before it exits, so the reduce that waits on it sees
-// both.  The reduce folds its partial in.
-__global__ void __launch_bounds__(256) ring_partial_kernel(const RingArgs ra) {
-  constexpr int TOK = 128;
-  __shared__ float qs[GROUP][HD];
-  __shared__ float ps[GROUP][TOK];
-  __shared__ float red[8][GROUP][HD];
-  __shared__ float mls[GROUP][2];
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  const int b = blockIdx.x / NKV, kvh = blockIdx.x % NKV;
+// 8-byte V loads, 8 heads accumulated, the 8 groups summed at the merge.
+struct RingSmem {
+  float qs[GROUP][HD];
+  float ps[GROUP][RING_MAX];
+  float red[8][GROUP][HD];   // [16-token group][head][dim] partial P.V sums
+  float mls[GROUP][2];       // (m log2, l) per head
+};
+
+// The ring tokens' partial of (sequence b, KV head kvh), all 8 query heads,
+// left in shared memory: o[h][d] = sum_g red[g][h][d] (relative to mls[h][0]),
+// l = mls[h][1].  Returns the number of ring tokens attended.
+__device__ int ring_partial_cta(const RingArgs& ra, int b, int kvh, RingSmem& sm) {
+  constexpr int TOK = RING_MAX;
   const int t = threadIdx.x, w = t >> 5, lane = t & 31;
   const int Ls = ra.seq_lens[b];
   const int lo = max(max(0, Ls - ra.window), Ls - ra.ring_tokens);
   const int n = min(max(0, Ls - lo), TOK);
   const float* qb = ra.q + ((int64_t)b * NKV * GROUP + kvh * GROUP) * HD;
-  for (int i = t; i < GROUP * HD; i += 256) qs[i / HD][i % HD] = qb[i] * ra.qscale;
+  for (int i = t; i < GROUP * HD; i += 256) sm.qs[i / HD][i % HD] = qb[i] * ra.qscale;
   __syncthreads();
   const float* kb = ra.ring + ((int64_t)(b * NKV + kvh) * 2 + 0) * ra.ring_tokens * HD;
   const float* vb = ra.ring + ((int64_t)(b * NKV + kvh) * 2 + 1) * ra.ring_tokens * HD;
@@ -672,31 +670,31 @@ __global__ void __launch_bounds__(256) ring_partial_kernel(const RingArgs ra) {
       for (int c = 0; c < 8; ++c)
 #pragma unroll
         for (int h = 0; h < GROUP; ++h) {
-          const float* qq = &qs[h][32 * half + 4 * c];
+          const float* qq = &sm.qs[h][32 * half + 4 * c];
           acc[h] = fmaf(qq[0], k[c].x, fmaf(qq[1], k[c].y, fmaf(qq[2], k[c].z, fmaf(qq[3], k[c].w, acc[h]))));
         }
     }
 #pragma unroll
     for (int h = 0; h < GROUP; ++h) {
-      const float s = acc[h] + __shfl_xor_sync(0xffffffffu, acc[h], 1);
-      if (half == 0 && j < TOK) ps[h][j] = j < n ? s : -INFINITY;
+      const float sc = acc[h] + __shfl_xor_sync(0xffffffffu, acc[h], 1);
+      if (half == 0 && j < TOK) sm.ps[h][j] = j < n ? sc : -INFINITY;
     }
   }
   __syncthreads();
   {  // softmax of head w over the tokens
     float mx = -INFINITY;
-    for (int j = lane; j < TOK; j += 32) mx = fmaxf(mx, ps[w][j]);
+    for (int j = lane; j < TOK; j += 32) mx = fmaxf(mx, sm.ps[w][j]);
     mx = warp_max(mx);
     float l = 0.f;
     for (int j = lane; j < TOK; j += 32) {
-      const float pe = mx > -INFINITY ? exp2f(ps[w][j] - mx) : 0.f;
-      ps[w][j] = pe;
+      const float pe = mx > -INFINITY ? exp2f(sm.ps[w][j] - mx) : 0.f;
+      sm.ps[w][j] = pe;
       l += pe;
     }
     l = warp_sum(l);
     if (lane == 0) {
-      mls[w][0] = mx;
-      mls[w][1] = l;
+      sm.mls[w][0] = mx;
+      sm.mls[w][1] = l;
     }
   }
   __syncthreads();
@@ -716,30 +714,18 @@ __global__ void __launch_bounds__(256) ring_partial_kernel(const RingArgs ra) {
     for (int u = 0; u < 16; ++u)
 #pragma unroll
       for (int h = 0; h < GROUP; ++h) {
-        const float pe = ps[h][16 * tg + u];
+        const float pe = sm.ps[h][16 * tg + u];
         acc[h].x = fmaf(pe, v[u].x, acc[h].x);
         acc[h].y = fmaf(pe, v[u].y, acc[h].y);
       }
 #pragma unroll
     for (int h = 0; h < GROUP; ++h) {
-      red[tg][h][2 * dp] = acc[h].x;
-      red[tg][h][2 * dp + 1] = acc[h].y;
+      sm.red[tg][h][2 * dp] = acc[h].x;
+      sm.red[tg][h][2 * dp + 1] = acc[h].y;
     }
   }
   __syncthreads();
-  for (int i = t; i < GROUP * HD; i += 256) {
-    const int h = i / HD, d = i % HD;
-    float o = 0.f;
-#pragma unroll
-    for (int g = 0; g < 8; ++g) o += red[g][h][d];
-    ra.ring_part[((int64_t)b * NKV * GROUP + kvh * GROUP + h) * (HD + 2) + d] = o;
-  }
-  if (t < GROUP) {
-    float* dst = ra.ring_part + ((int64_t)b * NKV * GROUP + kvh * GROUP + t) * (HD + 2);
-    dst[HD] = n > 0 ? mls[t][0] : -INFINITY;
-    dst[HD + 1] = n > 0 ? mls[t][1] : 0.f;
-  }
-  asm volatile("griddepcontrol.wait;" ::: "memory");   // the decode before it has completed
+  return n;
 }
 
 // ---- split-KV exchange over peer memory ----------------------------------
@@ -783,8 +769,7 @@ __device__ __forceinline__ unsigned long long global_ns() {
 
 // One CTA per (sequence, query head) row.  The covering CTAs' partials are
 // taken by the 8 warps round-robin with up to RU of them loaded before any is
-// folded (one L2 round trip for up to 8 RU CTAs); the fp32 ring of config 3
-// is folded in; warp 0 combines.  Without an exchange the row is written as
+// folded (one L2 round trip for up to 8 RU CTAs); warp 0 combines.  Without an exchange the row is written as
 // the partial format (o/l, m natural, l) or, with `final_out`, o/l alone;
 // with an exchange it is sent to every rank and the ranks' partials of the
 // row are combined into `final_out`.
@@ -793,9 +778,8 @@ __global__ void __launch_bounds__(256) q4_reduce_kernel(const float* __restrict_
                                                        const int32_t* __restrict__ meta, int batch,
                                                        float* __restrict__ part,
                                                        float* __restrict__ final_out,
-                                                       const RingArgs ra, const __grid_constant__ Exchange ex,
-                                                       int32_t* err) {
-  __shared__ float red[9][HD + 2];
+                                                       const __grid_constant__ Exchange ex, int32_t* err) {
+  __shared__ float red[8][HD + 2];
   pdl_wait();
   const int row = blockIdx.x;                 // b * 32 + h
   const int b = row / (NKV * GROUP), h = row % (NKV * GROUP);
@@ -834,13 +818,7 @@ __global__ void __launch_bounds__(256) q4_reduce_kernel(const float* __restrict_
     red[warp][HD] = M;
     red[warp][HD + 1] = L;
   }
-  int nparts = 8;
-  if (ra.ring) {
-    // the ring tokens' partial (ring_partial_kernel) as a ninth part
-    const float* src = ra.ring_part + (int64_t)row * (HD + 2);
-    if (threadIdx.x < HD + 2) red[8][threadIdx.x] = src[threadIdx.x];
-    nparts = 9;
-  }
+  constexpr int nparts = 8;
   __syncthreads();
   if (warp != 0) return;
   float Mt = -INFINITY;
@@ -940,6 +918,63 @@ __global__ void __launch_bounds__(256) q4_reduce_kernel(const float* __restrict_
   if (lane == 0) *reinterpret_cast<volatile int*>(epochs + row) = (int)epoch;
 }
 
+// Config 3: the fp32 ring tokens' partial and the reduce in one launch.  CTA =
+// (sequence, KV head), warp = query head.  Launched with programmatic dependent
+// launch after the 4-bit decode, whose CTAs release it only after their own
+// wait on the grid before them, so the ring inputs are complete: the ring part
+// runs while decode CTAs drain, then the CTA waits for the decode to complete
+// and folds the covering CTAs' partials (up to RU loaded per round trip) into
+// the ring's.  Writes o / l.
+__global__ void __launch_bounds__(256) q4_reduce_ring_kernel(const float* __restrict__ cta_part,
+                                                            const int32_t* __restrict__ meta,
+                                                            float* __restrict__ final_out, const RingArgs ra) {
+  __shared__ RingSmem sm;
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int b = blockIdx.x / NKV, kvh = blockIdx.x % NKV;
+  const int hh = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = ring_partial_cta(ra, b, kvh, sm);
+  asm volatile("griddepcontrol.wait;" ::: "memory");   // the decode's partials and meta are complete
+  float M = -INFINITY, L = 0.f, o0 = 0.f, o1 = 0.f;
+  if (n > 0 && sm.mls[hh][1] > 0.f) {
+    M = sm.mls[hh][0];
+    L = sm.mls[hh][1];
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      o0 += sm.red[g][hh][2 * lane];
+      o1 += sm.red[g][hh][2 * lane + 1];
+    }
+  }
+  const int cf = meta[2 * b], cl = meta[2 * b + 1];
+  for (int cbase = cf; cbase <= cl; cbase += RU) {
+    float2 ml[RU], ov[RU];
+#pragma unroll
+    for (int u = 0; u < RU; ++u) {
+      const int c = cbase + u;
+      if (c <= cl) {
+        const float* src = cta_part + ((((int64_t)c + b) * NKV + kvh) * GROUP + hh) * (HD + 2);
+        ml[u] = __ldcg(reinterpret_cast<const float2*>(src + HD));
+        ov[u] = __ldcg(reinterpret_cast<const float2*>(src) + lane);
+      } else {
+        ml[u] = make_float2(-INFINITY, 0.f);
+        ov[u] = make_float2(0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < RU; ++u) {
+      if (!(ml[u].y > 0.f)) continue;
+      const float Mn = fmaxf(M, ml[u].x);
+      const float sa = exp2f(M - Mn), sb = exp2f(ml[u].x - Mn);
+      L = L * sa + ml[u].y * sb;
+      o0 = o0 * sa + ov[u].x * sb;
+      o1 = o1 * sa + ov[u].y * sb;
+      M = Mn;
+    }
+  }
+  const float inv = L > 0.f ? 1.0f / L : 0.f;
+  float* dst = final_out + ((int64_t)b * NKV * GROUP + kvh * GROUP + hh) * HD;
+  *reinterpret_cast<float2*>(dst + 2 * lane) = make_float2(o0 * inv, o1 * inv);
+}
+
 // ============================================================================
 // log-sum-exp combine: parts [G][rows][HD+2] -> out [rows][HD]
 // ============================================================================
@@ -1037,22 +1072,21 @@ int32_t launch_partial(Params base, int batch, const int32_t* tok_begin, const i
     st = check_cuda(launch_pdl(decode_q4_kernel, dim3(grid_cache[di]), dim3(THREADS), smem, stream, p),
                     "decode_q4 launch");
     if (st) return st;
-    RingArgs r = ra;
-    if (r.ring) {
-      r.q = q + (int64_t)b0 * NKV * GROUP * HD;
-      r.ring = ra.ring + (int64_t)b0 * NKV * 2 * ra.ring_tokens * HD;
-      r.seq_lens = ra.seq_lens + b0;
-      r.ring_part = ra.ring_part + (int64_t)b0 * NKV * GROUP * (HD + 2);
-      st = check_cuda(launch_pdl(ring_partial_kernel, dim3(nb * NKV), dim3(256), 0, stream, r), "ring_partial launch");
-      if (st) return st;
-    }
-    p.seq_lens = base.seq_lens ? base.seq_lens + b0 : nullptr;
     float* fo = final_out ? final_out + (int64_t)b0 * NKV * GROUP * HD : nullptr;
     const float* cp = p.cta_part;
     const int32_t* mt = p.meta;
-    st = check_cuda(launch_pdl(q4_reduce_kernel, dim3(nb * NKV * GROUP), dim3(256), 0, stream, cp, mt, nb, p.part,
-                               fo, r, ex, dev->err_word),
-                    "q4_reduce launch");
+    if (ra.ring) {   // config 3: ring partial + reduce in one launch (final output only)
+      RingArgs r = ra;
+      r.q = q + (int64_t)b0 * NKV * GROUP * HD;
+      r.ring = ra.ring + (int64_t)b0 * NKV * 2 * ra.ring_tokens * HD;
+      r.seq_lens = ra.seq_lens + b0;
+      st = check_cuda(launch_pdl(q4_reduce_ring_kernel, dim3(nb * NKV), dim3(256), 0, stream, cp, mt, fo, r),
+                      "q4_reduce_ring launch");
+    } else {
+      st = check_cuda(launch_pdl(q4_reduce_kernel, dim3(nb * NKV * GROUP), dim3(256), 0, stream, cp, mt, nb, p.part,
+                                 fo, ex, dev->err_word),
+                      "q4_reduce launch");
+    }
     if (st) return st;
   }
   return NYION_OK;
@@ -1150,6 +1184,8 @@ extern "C" int32_t nyion_attn_decode_q4_window_ring(
   if (ring_tokens <= 0 || window <= 0 || batch <= 0)
     return fail(NYION_ERR_INVALID, "decode_q4_window_ring: ring_tokens, window, batch must be > 0");
   // workspace: [q4 partial workspace][2 partial arrays of batch*H*(HD+2) floats][tok ranges]
+  // (the documented size; the fused ring reduce writes `out` directly and leaves the
+  // partial arrays unused)
   const size_t q4ws = ws_layout(batch).total;
   const size_t rows = (size_t)batch * n_heads;
   const size_t parts_bytes = 2 * rows * (HD + 2) * sizeof(float);
@@ -1182,7 +1218,6 @@ extern "C" int32_t nyion_attn_decode_q4_window_ring(
   ra.ring_tokens = ring_tokens;
   ra.window = window;
   ra.qscale = p.qscale;
-  ra.ring_part = parts + rows * (HD + 2);
   return launch_partial(p, batch, nullptr, nullptr, q, parts, page_table, w, s, out, ra);
 }
 
