@@ -630,13 +630,16 @@ struct RingArgs {
 constexpr int RING_MAX = 128;   // ring tokens of one sequence (larger rings: error)
 
 // fp32 ring tokens [max(max(0, L - window), L - ring), L) of config 3 (slot pos %
-// ring), one (sequence, KV head) per CTA, all 8 query heads of the group.
-// Scores: thread = (token, half row): one batch of eight 16-byte K loads, dots for
-// the 8 heads against q in shared memory, halves joined by a shuffle.  Softmax:
-// warp = head.  P.V: thread = (dim pair, 16-token group): one batch of sixteen
-// 8-byte V loads, 8 heads accumulated, the 8 groups summed at the merge.
+// ring), one (sequence, KV head) per CTA, all 8 query heads of the group.  Every
+// global load of the CTA goes out in one batch: q, each thread's half K row
+// (eight 16-byte loads) and its sixteen 8-byte V pairs (V does not depend on the
+// scores).  Scores: thread = (token, half row), dots for the 8 heads against q in
+// shared memory (each half padded by 16 bytes, so the two halves a warp reads
+// fall in different banks), halves joined by a shuffle.  Softmax: warp = head.
+// P.V: thread = (dim pair, 16-token group), 8 heads accumulated, the 8 groups
+// summed at the merge.
 struct RingSmem {
-  float qs[GROUP][HD];
+  float qs[GROUP][2][36];    // [head][half][32 dims + 4 pad]
   float ps[GROUP][RING_MAX];
   float red[8][GROUP][HD];   // [16-token group][head][dim] partial P.V sums
   float mls[GROUP][2];       // (m log2, l) per head
@@ -648,30 +651,49 @@ struct RingSmem {
 __device__ int ring_partial_cta(const RingArgs& ra, int b, int kvh, RingSmem& sm) {
   constexpr int TOK = RING_MAX;
   const int t = threadIdx.x, w = t >> 5, lane = t & 31;
+  const int R = ra.ring_tokens;
   const int Ls = ra.seq_lens[b];
-  const int lo = max(max(0, Ls - ra.window), Ls - ra.ring_tokens);
+  const int lo = max(max(0, Ls - ra.window), Ls - R);
   const int n = min(max(0, Ls - lo), TOK);
+  const int lo_slot = lo % R;
+  auto slot_of = [&](int j) { const int sl = lo_slot + j; return sl >= R ? sl - R : sl; };   // j < R
   const float* qb = ra.q + ((int64_t)b * NKV * GROUP + kvh * GROUP) * HD;
-  for (int i = t; i < GROUP * HD; i += 256) sm.qs[i / HD][i % HD] = qb[i] * ra.qscale;
+  const float* kb = ra.ring + ((int64_t)(b * NKV + kvh) * 2 + 0) * R * HD;
+  const float* vb = ra.ring + ((int64_t)(b * NKV + kvh) * 2 + 1) * R * HD;
+  // ---- all global loads in flight together ----
+  const int j = t >> 1, half = t & 1;          // scores: token j, dims 32 half .. +31
+  const int dp = lane, tg = w;                 // P.V: dims 2dp, 2dp+1; tokens 16tg .. 16tg+15
+  const float q0 = qb[t], q1 = qb[t + 256];
+  float4 k[8];
+  if (j < n) {
+    const float4* kr = reinterpret_cast<const float4*>(kb + (int64_t)slot_of(j) * HD + 32 * half);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) k[c] = __ldg(kr + c);
+  } else {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) k[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float2 v[16];
+#pragma unroll
+  for (int u = 0; u < 16; ++u) {
+    const int jj = 16 * tg + u;
+    v[u] = jj < n ? __ldg(reinterpret_cast<const float2*>(vb + (int64_t)slot_of(jj) * HD) + dp)
+                  : make_float2(0.f, 0.f);
+  }
+  sm.qs[t / HD][(t % HD) / 32][t % 32] = q0 * ra.qscale;
+  sm.qs[(t + 256) / HD][((t + 256) % HD) / 32][(t + 256) % 32] = q1 * ra.qscale;
   __syncthreads();
-  const float* kb = ra.ring + ((int64_t)(b * NKV + kvh) * 2 + 0) * ra.ring_tokens * HD;
-  const float* vb = ra.ring + ((int64_t)(b * NKV + kvh) * 2 + 1) * ra.ring_tokens * HD;
   {
-    const int j = t >> 1, half = t & 1;
     float acc[GROUP];
 #pragma unroll
     for (int h = 0; h < GROUP; ++h) acc[h] = 0.f;
     if (j < n) {
-      const float4* kr = reinterpret_cast<const float4*>(kb + (int64_t)((lo + j) % ra.ring_tokens) * HD + 32 * half);
-      float4 k[8];
-#pragma unroll
-      for (int c = 0; c < 8; ++c) k[c] = __ldg(kr + c);
 #pragma unroll
       for (int c = 0; c < 8; ++c)
 #pragma unroll
         for (int h = 0; h < GROUP; ++h) {
-          const float* qq = &sm.qs[h][32 * half + 4 * c];
-          acc[h] = fmaf(qq[0], k[c].x, fmaf(qq[1], k[c].y, fmaf(qq[2], k[c].z, fmaf(qq[3], k[c].w, acc[h]))));
+          const float4 qq = *reinterpret_cast<const float4*>(&sm.qs[h][half][4 * c]);
+          acc[h] = fmaf(qq.x, k[c].x, fmaf(qq.y, k[c].y, fmaf(qq.z, k[c].z, fmaf(qq.w, k[c].w, acc[h]))));
         }
     }
 #pragma unroll
@@ -699,17 +721,9 @@ __device__ int ring_partial_cta(const RingArgs& ra, int b, int kvh, RingSmem& sm
   }
   __syncthreads();
   {
-    const int dp = lane, tg = w;                 // dims 2dp, 2dp+1; tokens 16tg .. 16tg+15
     float2 acc[GROUP];
 #pragma unroll
     for (int h = 0; h < GROUP; ++h) acc[h] = make_float2(0.f, 0.f);
-    float2 v[16];
-#pragma unroll
-    for (int u = 0; u < 16; ++u) {
-      const int j = 16 * tg + u;
-      v[u] = j < n ? __ldg(reinterpret_cast<const float2*>(vb + (int64_t)((lo + j) % ra.ring_tokens) * HD) + dp)
-                   : make_float2(0.f, 0.f);
-    }
 #pragma unroll
     for (int u = 0; u < 16; ++u)
 #pragma unroll
