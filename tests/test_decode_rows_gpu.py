@@ -7,8 +7,6 @@ the f16 values), with the reference's masking (tokens [0, valid_end]); the
 zone arena is filled through the oracle's restatement of the reference page
 geometry (cache.rs page_id / slot_in_page).  Tolerance: max-abs 1e-3.
 """
-import ctypes as C
-
 import numpy as np
 import pytest
 import torch
@@ -120,4 +118,28 @@ def test_zoned_long_contexts_all_zones(cuda_device, ctx, qpos):
                              qpos)
     torch.cuda.synchronize()
     assert (out.cpu() - want).abs().max().item() < TOL
+    assert A.device_error() == 0
+
+
+def test_ring_f16_empty_and_single_token(cuda_device):
+    """Device length 0 attends nothing (zeros, no NaN); length 1 returns V of
+    slot 0 for every head of the group."""
+    H, n_kv, W = 32, 4, 256
+    g = torch.Generator().manual_seed(9)
+    q = torch.randn(H, D, generator=g)
+    k = torch.randn(n_kv, W, D, generator=g).half()
+    v = torch.randn(n_kv, W, D, generator=g).half()
+    dq, dk, dv = q.to(cuda_device), k.to(cuda_device), v.to(cuda_device)
+    ws = A.F16Workspace(H, W, device=cuda_device)
+    for n in (0, 1):
+        d_len = torch.full((1,), n, dtype=torch.int32, device=cuda_device)
+        out = A.decode_ring_f16(dq, dk, dv, d_len, workspace=ws)
+        torch.cuda.synchronize()
+        o = out.cpu()
+        assert torch.isfinite(o).all()
+        if n == 0:
+            assert (o == 0).all()
+        else:
+            want = v[:, 0].float().repeat_interleave(H // n_kv, dim=0)
+            assert (o - want).abs().max().item() < TOL
     assert A.device_error() == 0
