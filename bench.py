@@ -153,10 +153,11 @@ def cpu_sample_inputs(seed=1234, n_seq=8):
     return q, pool, table, lens
 
 
-def time_cpu_oracle(budget_s: float = 4.0, n_seq=8):
+def time_cpu_oracle(budget_s: float = 4.0, n_seq=8, threads: int = 0):
+    """The oracle's paged decode timed on the host cores (`threads` 0 = all)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
-    threads = os.cpu_count() or 1
+    threads = threads or os.cpu_count() or 1
     q, pool, table, lens = cpu_sample_inputs(n_seq=n_seq)
     O.decode_paged_f32(q[:1], pool, table[:1], lens[:1], N_KV, D, PT, threads=threads)  # warm
     reps, t0 = 0, time.perf_counter()
@@ -645,6 +646,9 @@ def run_gpu(args, rank, world):
         c = time_cpu_oracle(budget_s=args.cpu_seconds)
         cpu = {"value": c["value"], "unit": "GB/s", "cores": c["cores"], "kind": c["kind"],
                "sample": c["sample"] + f"; {c['isa']}"}
+        # the reference executor's own pool size (executor.rs:28-38): 6 threads
+        c6 = time_cpu_oracle(budget_s=max(1.0, args.cpu_seconds / 2), threads=6)
+        cpu["at_reference_threads"] = {"value": c6["value"], "unit": "GB/s", "cores": 6, "sample": c6["sample"]}
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
