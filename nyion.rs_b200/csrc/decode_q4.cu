@@ -440,6 +440,7 @@ __global__ void __launch_bounds__(THREADS, 2) decode_q4_kernel(const Params p) {
         }
       }
       const bool any = (pos0 < se) && (pos0 + 32 > sb);
+      const bool inner = (pos0 >= sb) && (pos0 + 32 <= se);   // no token of this warp is masked
       if (any) {
         const uint32_t kb = smem_u32(s.kv[stage]) + 2 * th * PAGE_BYTES + kvh * PAGE_KV;
         // token t of this warp: page 2th + t/16 (offset (t/16)*PAGE_BYTES), row t%16
@@ -460,7 +461,7 @@ __global__ void __launch_bounds__(THREADS, 2) decode_q4_kernel(const Params p) {
           const uint32_t kr = vr - PAGE * ROWB;
           const float2 k0 = hdr2f(lds_u32(kr)), k1 = hdr2f(lds_u32(kr + BLK));
           const float2 v0 = hdr2f(lds_u32(vr)), v1 = hdr2f(lds_u32(vr + BLK));
-          const bool live = (pos0 + lane >= sb) && (pos0 + lane < se);
+          const bool live = inner || ((pos0 + lane >= sb) && (pos0 + lane < se));
           const float a0 = 16.0f * k0.x, a1 = 16.0f * k1.x, b0 = 16.0f * v0.x, b1 = 16.0f * v1.x;
           const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
           const uint32_t sw = ((lane >> 2) & 1) << 4;
@@ -492,10 +493,17 @@ __global__ void __launch_bounds__(THREADS, 2) decode_q4_kernel(const Params p) {
             const float4 h = lds_f4(hd + tt * 32 + (((tt >> 2) & 1) << 4));   // a0, c0, a1, c1
             const float t0 = sc[nt][0][e] + sc[nt][0][2 + e];            // sum q (1 + n/16), hi + lo rows
             const float t1 = sc[nt][1][e] + sc[nt][1][2 + e];
-            const float acc = fmaf(h.x, t0, fmaf(h.z, t1, fmaf(h.y, qs[0], h.w * qs[1])));
-            const int pos = pos0 + tt;
-            sv[nt][e] = (pos >= sb && pos < se) ? acc : -INFINITY;
+            sv[nt][e] = fmaf(h.x, t0, fmaf(h.z, t1, fmaf(h.y, qs[0], h.w * qs[1])));
           }
+        if (!inner) {   // the sequence range starts or ends inside this warp's 32 tokens
+#pragma unroll
+          for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int pos = pos0 + 8 * nt + 2 * tig + e;
+              if (pos < sb || pos >= se) sv[nt][e] = -INFINITY;
+            }
+        }
         // ---- online softmax ----
         float mx = sv[0][0];
 #pragma unroll
