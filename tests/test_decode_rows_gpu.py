@@ -143,3 +143,23 @@ def test_ring_f16_empty_and_single_token(cuda_device):
             want = v[:, 0].float().repeat_interleave(H // n_kv, dim=0)
             assert (o - want).abs().max().item() < TOL
     assert A.device_error() == 0
+
+
+def test_zoned_long_context_missing_pages_report_error(cuda_device):
+    """An arena that lacks zone pages the context needs: the missing tiles are
+    skipped, the device error word reports a page outside the arena, and the
+    call neither faults nor hangs."""
+    gen = torch.Generator().manual_seed(21)
+    n_layers, n_kv, H = 1, 4, 32
+    ctx = 6000                                  # zone 0 (128 pages) + zone 1 pages
+    ks, vs, k_ar, v_ar = _zone_arena(n_layers, n_kv, 4096, gen)   # only the 128 zone-0 pages exist
+    q = torch.randn(H, D, generator=gen)
+    A.device_error()                            # clear
+    out = A.decode_zoned_f32(q.to(cuda_device), k_ar.to(cuda_device), v_ar.to(cuda_device), n_layers, 0, ctx,
+                             ctx - 1)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.cpu()).all()
+    assert A.device_error() & 1                 # page outside the arena
+    # the attended tokens that do exist (zone 0) give the output
+    want = _attend(q, ks[:, 0].transpose(0, 1), vs[:, 0].transpose(0, 1), 4096)
+    assert (out.cpu() - want).abs().max().item() < TOL
