@@ -658,19 +658,45 @@ __global__ void __launch_bounds__(256) zoned_small_kernel(const float* __restric
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int kvh = blockIdx.x, t = threadIdx.x, w = t >> 5, lane = t & 31;
-  for (int i = t; i < GROUP * HD; i += 256) qs[i / HD][i % HD] = q[(int64_t)kvh * GROUP * HD + i] * sl2;
-  __syncthreads();
   const int64_t lp = (int64_t)n_layers * n_kv;
   auto row = [&](int tok) { return ((int64_t)(tok >> 5) * lp * 32 + ((int64_t)layer * n_kv + kvh) * 32 + (tok & 31)) * HD; };
+  // Up to 256 tokens every global load goes out at once: q, the K row of token
+  // t and the V pairs of tokens 32 w .. 32 w + 31 (V does not depend on the scores).
+  constexpr bool ONE_BATCH = MAXT <= 256;
+  float4 kk0[HD / 4];
+  float2 vv0[ONE_BATCH ? 32 : 1];
+  if (ONE_BATCH) {
+    const float q0 = q[(int64_t)kvh * GROUP * HD + t], q1 = q[(int64_t)kvh * GROUP * HD + t + 256];
+    if (t < n) {
+      const float4* kr = reinterpret_cast<const float4*>(k_arena + row(t));
+#pragma unroll
+      for (int c = 0; c < HD / 4; ++c) kk0[c] = __ldg(kr + c);
+    }
+#pragma unroll
+    for (int u = 0; u < (ONE_BATCH ? 32 : 1); ++u) {
+      const int j = 32 * w + u;
+      vv0[u] = j < n ? __ldg(reinterpret_cast<const float2*>(v_arena + row(j)) + lane) : make_float2(0.f, 0.f);
+    }
+    qs[t / HD][t % HD] = q0 * sl2;
+    qs[(t + 256) / HD][(t + 256) % HD] = q1 * sl2;
+  } else {
+    for (int i = t; i < GROUP * HD; i += 256) qs[i / HD][i % HD] = q[(int64_t)kvh * GROUP * HD + i] * sl2;
+  }
+  __syncthreads();
   for (int tok = t; tok < MAXT; tok += 256) {
     float acc[GROUP];
 #pragma unroll
     for (int h = 0; h < GROUP; ++h) acc[h] = 0.f;
     if (tok < n) {
-      const float4* kr = reinterpret_cast<const float4*>(k_arena + row(tok));
       float4 kk[HD / 4];
+      if (ONE_BATCH) {
 #pragma unroll
-      for (int c = 0; c < HD / 4; ++c) kk[c] = __ldg(kr + c);
+        for (int c = 0; c < HD / 4; ++c) kk[c] = kk0[c];
+      } else {
+        const float4* kr = reinterpret_cast<const float4*>(k_arena + row(tok));
+#pragma unroll
+        for (int c = 0; c < HD / 4; ++c) kk[c] = __ldg(kr + c);
+      }
 #pragma unroll
       for (int c = 0; c < HD / 4; ++c)
 #pragma unroll
@@ -716,8 +742,11 @@ __global__ void __launch_bounds__(256) zoned_small_kernel(const float* __restric
 #pragma unroll
       for (int u = 0; u < 32; ++u) {
         const int j = tg * n_per + u0 + u;
-        vv[u] = (u0 + u < n_per && j < n) ? __ldg(reinterpret_cast<const float2*>(v_arena + row(j)) + dp)
-                                          : make_float2(0.f, 0.f);
+        if (ONE_BATCH)
+          vv[u] = vv0[ONE_BATCH ? u : 0];   // n_per = 32: loaded at the start
+        else
+          vv[u] = (u0 + u < n_per && j < n) ? __ldg(reinterpret_cast<const float2*>(v_arena + row(j)) + dp)
+                                            : make_float2(0.f, 0.f);
       }
 #pragma unroll
       for (int u = 0; u < 32; ++u) {
