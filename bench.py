@@ -436,6 +436,60 @@ def run_row_caches(A, torch, dev, stream, args):
     return res
 
 
+def run_position_lists(A, torch, dev, stream, args):
+    """Position-list attention (ops::attention_sparse / attention_fugu over f32
+    pages; ops::attention_sparse_q4 over 4-bit pages): B=16, context 65536,
+    positions = the 4096-token window + 128 globals every 256 tokens.  CUDA
+    graph of 10 calls, 256 MB L2 flush before each timed replay."""
+    B, L, W, STR = 16, 65536, 4096, 256
+    gen = torch.Generator(device=dev).manual_seed(707)
+    mp = L // PT
+    table = torch.randperm(B * mp, device=dev, generator=gen).to(torch.int32).reshape(B, mp)
+    pos = torch.cat([torch.arange(0, 128 * STR, STR, device=dev), torch.arange(L - W, L, device=dev)])
+    pos = pos.to(torch.int32).repeat(B, 1).contiguous()
+    npos = torch.full((B,), pos.shape[1], dtype=torch.int32, device=dev)
+    lens = torch.full((B,), L, dtype=torch.int32, device=dev)
+    q = torch.randn(B, H, D, device=dev, generator=gen)
+    out = torch.empty_like(q)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    f32_pool = torch.randn(B * mp, N_KV, 2, PT, D, device=dev, generator=gen)
+    q4_pool, _ = build_q4_pages(A, torch, B * L, dev, gen, page_perm=False)
+    ws_p = A.positions_workspace(B, H, pos.shape[1], device=dev)
+    ws_s = A.sparse_q4_workspace(B, device=dev)
+    legs = {
+        "f32_positions_4224": (lambda: A.decode_positions(q, f32_pool, table, pos, npos, out=out, workspace=ws_p,
+                                                          stream=stream),
+                               B * N_KV * pos.shape[1] * 2 * D * 4),
+        "q4_sparse_window_4096_globals_128": (lambda: A.sparse_q4(q, q4_pool, table, lens, W, STR, out=out,
+                                                                  workspace=ws_s, stream=stream),
+                                              B * N_KV * (W + 128) * 2 * 40),
+    }
+    res = {}
+    for name, (call, nbytes) in legs.items():
+        with torch.cuda.stream(stream):
+            for _ in range(max(3, args.warmup)):
+                call()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for _ in range(10):
+                    call()
+            torch.cuda.synchronize()
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(args.steps)]
+            for e0, e1 in evs:
+                flush.fill_(1)
+                e0.record(stream)
+                g.replay()
+                e1.record(stream)
+            torch.cuda.synchronize()
+        us = sum(e0.elapsed_time(e1) for e0, e1 in evs) / len(evs) * 1e3 / 10
+        res[name] = {"us_per_call": us, "gbs": nbytes / (us * 1e-6) / 1e9, "bytes_per_call": nbytes,
+                     "timing": "graph of 10 calls, 256 MB L2 flush before each replay"}
+        del g
+    res["device_error"] = A.device_error(stream)
+    return res
+
+
 def run_config5(A, S, torch, dev, stream, args, barrier, dist, world, rank):
     """Config 5: B=1, 1M-token Q4 context split evenly over the ranks (strong
     scaling).  Timed path: the fused exchange (the reduce kernel writes each
@@ -492,6 +546,8 @@ def run_gpu(args, rank, world):
             r = run_config4(A, torch, dev, st, args)
         elif args.only == "rows":
             r = run_row_caches(A, torch, dev, st, args)
+        elif args.only == "positions":
+            r = run_position_lists(A, torch, dev, st, args)
         else:
             r = run_config5(A, S, torch, dev, st, args, bar, dist_, world, rank)
         if rank == 0:
@@ -631,6 +687,7 @@ def run_gpu(args, rank, world):
             extra["q4_window_ring"] = run_config3(A, torch, dev, stream, args, barrier, dist, world)
             extra["prefill_2048"] = run_config4(A, torch, dev, stream, args)
             extra["reference_gpu_path"] = run_row_caches(A, torch, dev, stream, args)
+            extra["position_lists"] = run_position_lists(A, torch, dev, stream, args)
         extra["split_kv_1m"] = run_config5(A, S, torch, dev, stream, args, barrier, dist, world, rank)
 
     step_bytes = layer_step_bytes() * LAYERS
@@ -684,7 +741,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the config 3 / config 5 legs")
-    ap.add_argument("--only", choices=["config3", "config4", "config5", "rows"], default=None,
+    ap.add_argument("--only", choices=["config3", "config4", "config5", "rows", "positions"], default=None,
                     help="profiling runs: time only this leg (prints its JSON object)")
     ap.add_argument("--cpu-seconds", type=float, default=6.0)
     ap.add_argument("--layers", type=int, default=LAYERS,
