@@ -13,18 +13,19 @@
 //     merged.  Nibbles are read in the writer's order (element i in byte i/2,
 //     low nibble for even i, cache.rs:637-663).
 //
-// Scattered positions cannot use page-granular copies, so the CTA gathers rows:
-// CTA = (sequence, KV head, 128-position split).  Thread t < 128 resolves
-// position t of the split to its page row; then every thread brings one K or
-// V row (256 B, all sixteen 16-byte loads in flight; 4-bit rows are
-// dequantized on the way with the reference's separate multiply and add) into
-// shared memory, so each row crosses from memory once for all 8 query heads.
-// The split is then computed in 32-position tiles: scores with thread =
-// (position, 1/8 of the dims) holding the pre-scaled query of the 8 heads for
-// its dims and a reduce-scatter over its 8 lanes; softmax with warp = head
-// (online, log2 domain); P.V with warp = 4 positions, lane = (4 dims, 4
-// heads).  The 8 warps' P.V sums are folded in shared memory into one
-// (o/l, m, l) partial per head and split, merged by nyion_attn_lse_combine.
+// Scattered positions cannot use page-granular copies, so rows are gathered:
+// CTA = (sequence, KV head, 128-position split), warp = 32 positions.  Lane l
+// resolves position l of its warp's tile to a pool row and brings that row's
+// K and V into the warp's shared tiles (fp32 rows by sixteen 16-byte async
+// copies each, 4-bit rows dequantized on the way with the reference's
+// separate multiply and add), written in the 128-byte swizzled layout the
+// tensor copies of the row-cache kernel produce; each scattered row crosses
+// from memory once for all 8 query heads.  The warp then computes its tile
+// alone: S = Q K^T and O = P V on mma.sync with every fp32 operand split into
+// bf16 hi + lo (the A operand stacks the 8 heads' hi parts over their lo
+// parts), softmax over the tile in the log2 domain.  The 4 warps' partials
+// are folded in shared memory into one (o/l, m, l) partial per head and
+// split, merged by nyion_attn_lse_combine.
 #include <cuda_fp16.h>
 #include <math.h>
 
@@ -48,8 +49,10 @@ namespace posd {
 constexpr int HD = 64;
 constexpr int GROUP = 8;
 constexpr int PAGE = 16;
-constexpr int SPLIT = 128;            // positions per CTA
-constexpr int THREADS = 32 * GROUP;
+constexpr int WARPS = 4;               // one 32-position tile per warp
+constexpr int THREADS = 32 * WARPS;
+constexpr int SPLIT = 32 * WARPS;      // positions per CTA
+constexpr int TILE_BYTES = 32 * HD * 4;   // 32 fp32 rows as two 128-byte column halves, swizzled
 constexpr int PART = HD + 2;
 constexpr int MAX_GLOBAL = 128;        // attention_sparse*: at most 128 global tokens
 
@@ -116,38 +119,24 @@ __device__ __forceinline__ void load_row_q4(const Params& p, int64_t row, float 
 }
 
 struct GatherSmem {
-  float k[SPLIT][HD];
-  float v[SPLIT][HD];
-  float qs[GROUP][HD];
-  int64_t row[SPLIT];               // K row index in the pool (V: + PAGE), -1: none
-  float sp[2][32][9];               // scores, then probabilities: [position][head], padded
-  float alpha[2][GROUP];
+  uint8_t kv[WARPS][2][TILE_BYTES];   // per warp: K tile | V tile (1024-byte aligned)
+  float2 wml[WARPS][GROUP];           // per warp and head: (m log2, l)
 };
 
-// one K or V row of the pool into x[64]: f32 as is, 4-bit dequantized
-// (cache.rs:375-394: d * q + dmin with a separate multiply and add)
-template <bool Q4>
-__device__ __forceinline__ void gather_row(const Params& p, int64_t row, float* dst) {
-  if (!Q4) {
-    const float4* r = reinterpret_cast<const float4*>(static_cast<const float*>(p.pool) + row * HD);
-    float4 v[HD / 4];
-#pragma unroll
-    for (int c = 0; c < HD / 4; ++c) v[c] = __ldg(r + c);
-#pragma unroll
-    for (int c = 0; c < HD / 4; ++c) reinterpret_cast<float4*>(dst)[c] = v[c];
-  } else {
-    float x[HD];
-    load_row_q4(p, row, x);
-#pragma unroll
-    for (int c = 0; c < HD / 4; ++c)
-      reinterpret_cast<float4*>(dst)[c] = make_float4(x[4 * c], x[4 * c + 1], x[4 * c + 2], x[4 * c + 3]);
-  }
+// byte offset of 16-byte chunk c16 (0..15) of row rr (0..31) in a tile
+__device__ __forceinline__ uint32_t tile_off(int rr, int c16) {
+  return (uint32_t)((c16 >> 3) * 4096 + rr * 128 + (((c16 & 7) ^ (rr & 7)) << 4));
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
 
 template <bool Q4, bool RULE>
-__global__ void __launch_bounds__(THREADS) positions_kernel(const Params p) {
+__global__ void __launch_bounds__(THREADS, 3) positions_kernel(const Params p) {
   extern __shared__ uint8_t smem_raw[];
-  GatherSmem& sm = *reinterpret_cast<GatherSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 15) & ~uintptr_t(15));
+  GatherSmem& sm =
+      *reinterpret_cast<GatherSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int b = blockIdx.x / p.n_kv, kvh = blockIdx.x % p.n_kv, split = blockIdx.y;
   const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
   const int H = p.n_kv * GROUP;
@@ -162,144 +151,160 @@ __global__ void __launch_bounds__(THREADS) positions_kernel(const Params p) {
     return;
   }
   const int cnt = j1 - j0;
-  // ---- positions -> pool rows; q ----
-  const float q0 = p.q[((int64_t)b * H + kvh * GROUP) * HD + tid];
-  const float q1 = p.q[((int64_t)b * H + kvh * GROUP) * HD + tid + 256];
-  if (tid < SPLIT) {
-    int64_t r = -1;
-    if (tid < cnt) {
-      const int pos = position_of<RULE>(p, b, j0 + tid);
-      const int pidx = pos / PAGE;
-      int64_t page = -1;
-      if (pos >= 0 && pidx < p.max_pages) page = p.table[(int64_t)b * p.max_pages + pidx];
-      if (page < 0 || page >= p.n_pool_pages) record_error(p.err, kErrPageRange);
-      else r = ((page * p.n_kv + kvh) * 2) * PAGE + pos % PAGE;
-    }
-    sm.row[tid] = r;
+  // ---- lane -> position 32 w + lane of the split -> pool row ----
+  int64_t row = -1;
+  if (32 * w + lane < cnt) {
+    const int pos = position_of<RULE>(p, b, j0 + 32 * w + lane);
+    const int pidx = pos / PAGE;
+    int64_t page = -1;
+    if (pos >= 0 && pidx < p.max_pages) page = p.table[(int64_t)b * p.max_pages + pidx];
+    if (page < 0 || page >= p.n_pool_pages) record_error(p.err, kErrPageRange);
+    else row = ((page * p.n_kv + kvh) * 2) * PAGE + pos % PAGE;
   }
-  sm.qs[tid / HD][tid % HD] = q0 * p.sl2;
-  sm.qs[(tid + 256) / HD][(tid + 256) % HD] = q1 * p.sl2;
-  __syncthreads();
-  // ---- gather: thread -> (row tid / 2, K or V) ----
-  {
-    const int r = tid >> 1, kv = tid & 1;
-    float* dst = kv ? sm.v[r] : sm.k[r];
-    const int64_t row = r < cnt ? sm.row[r] : -1;
-    if (row >= 0) {
-      gather_row<Q4>(p, row + kv * PAGE, dst);
+  const uint32_t vmask = __ballot_sync(0xffffffffu, row >= 0);   // tokens of this tile that exist
+  // ---- gather this lane's K and V rows into the warp's tiles ----
+  const uint32_t kb = smem_u32(sm.kv[w][0]), vb = smem_u32(sm.kv[w][1]);
+  if (row >= 0) {
+    if (!Q4) {
+      const float* ks = static_cast<const float*>(p.pool) + row * HD;
+      const float* vs = ks + PAGE * HD;
+#pragma unroll
+      for (int c16 = 0; c16 < 16; ++c16) {
+        cp_async16(kb + tile_off(lane, c16), ks + 4 * c16);
+        cp_async16(vb + tile_off(lane, c16), vs + 4 * c16);
+      }
+      asm volatile("cp.async.commit_group;\ncp.async.wait_all;" ::: "memory");
     } else {
 #pragma unroll
-      for (int c = 0; c < HD / 4; ++c) reinterpret_cast<float4*>(dst)[c] = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-  }
-  // query slice: thread (position j, slice c) holds q[h][dims 4c..4c+3, 32+4c..32+4c+3]
-  const int j = tid >> 3, c = tid & 7;
-  __syncthreads();
-  float qr[GROUP][8];
+      for (int kv = 0; kv < 2; ++kv) {
+        float x[HD];
+        load_row_q4(p, row + kv * PAGE, x);
+        const uint32_t base = kv ? vb : kb;
 #pragma unroll
-  for (int h = 0; h < GROUP; ++h)
-#pragma unroll
-    for (int e = 0; e < 8; ++e) qr[h][e] = sm.qs[h][e < 4 ? 4 * c + e : 32 + 4 * c + (e - 4)];
-  const int dq = lane & 15, hh = lane >> 4;
-  float o[4][4];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) o[e][0] = o[e][1] = o[e][2] = o[e][3] = 0.f;
-  float M = -INFINITY, l = 0.f;   // softmax state of head w
-  const int n_tiles = (cnt + 31) / 32;
-  for (int i = 0; i < n_tiles; ++i) {
-    const int buf = i & 1, t0 = 32 * i;
-    // ---- scores: 8 head partials over this thread's 8 dims, reduce-scatter over 8 lanes ----
-    float part[GROUP];
-    {
-      const float4 a = *reinterpret_cast<const float4*>(&sm.k[t0 + j][4 * c]);
-      const float4 bb = *reinterpret_cast<const float4*>(&sm.k[t0 + j][32 + 4 * c]);
-      const float x[8] = {a.x, a.y, a.z, a.w, bb.x, bb.y, bb.z, bb.w};
-#pragma unroll
-      for (int h = 0; h < GROUP; ++h) {
-        float acc = 0.f;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc = fmaf(qr[h][e], x[e], acc);
-        part[h] = acc;
+        for (int c16 = 0; c16 < 16; ++c16)
+          asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(base + tile_off(lane, c16)),
+                       "f"(x[4 * c16]), "f"(x[4 * c16 + 1]), "f"(x[4 * c16 + 2]), "f"(x[4 * c16 + 3])
+                       : "memory");
       }
     }
-    float r4[4], r2[2];
+  } else {   // a missing row reads as zeros (its score is masked; V must be finite)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float send = (c & 4) ? part[e] : part[e + 4];
-      const float keep = (c & 4) ? part[e + 4] : part[e];
-      r4[e] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    for (int c16 = 0; c16 < 16; ++c16) {
+      asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(kb + tile_off(lane, c16)), "r"(0u) : "memory");
+      asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(vb + tile_off(lane, c16)), "r"(0u) : "memory");
     }
+  }
+  __syncwarp();
+  // ---- S = Q K^T for the tile: head g, tokens 8nt + 2tg + {0, 1} ----
+  const int g = lane >> 2, tg = lane & 3, r8 = lane & 7, j4 = lane >> 3;
+  uint32_t qa[4][4];   // k-step ks: kappa 2t, 2t+1, 2t+8, 2t+9 -> dims 16ks + t, +4, +8, +12
+  {
+    const float* qh = p.q + ((int64_t)b * H + kvh * GROUP + g) * HD;
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      const float* bq = qh + 16 * ks;
+      split_bf16x2(bq[tg] * p.sl2, bq[4 + tg] * p.sl2, qa[ks][0], qa[ks][1]);
+      split_bf16x2(bq[8 + tg] * p.sl2, bq[12 + tg] * p.sl2, qa[ks][2], qa[ks][3]);
+    }
+  }
+  float sc[4][4];
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      const int tok = 8 * nt + r8, chunk = 4 * (ks & 1) + j4;
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4(kb + (ks >> 1) * 4096 + tok * 128 + ((chunk ^ r8) << 4), a0, a1, a2, a3);
+      uint32_t bh0, bl0, bh1, bl1;
+      split_bf16x2(__uint_as_float(a0), __uint_as_float(a1), bh0, bl0);
+      split_bf16x2(__uint_as_float(a2), __uint_as_float(a3), bh1, bl1);
+      mma_bf16(sc[nt], qa[ks], bh0, bh1);
+      mma_bf16(sc[nt], qa[ks], bl0, bl1);
+    }
+  float sv[4][2];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
-      const float send = (c & 2) ? r4[e] : r4[e + 2];
-      const float keep = (c & 2) ? r4[e + 2] : r4[e];
-      r2[e] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+      const int tok = 8 * nt + 2 * tg + e;
+      sv[nt][e] = ((vmask >> tok) & 1u) ? sc[nt][e] + sc[nt][e + 2] : -INFINITY;
+      mx = fmaxf(mx, sv[nt][e]);
     }
-    {
-      const float send = (c & 1) ? r2[0] : r2[1];
-      const float keep = (c & 1) ? r2[1] : r2[0];
-      const float sc = keep + __shfl_xor_sync(0xffffffffu, send, 1);
-      const bool valid = t0 + j < cnt && sm.row[t0 + j] >= 0;
-      sm.sp[buf][j][c] = valid ? sc : -INFINITY;
-    }
-    __syncthreads();
-    // ---- softmax: warp = head, lane = position ----
-    {
-      const float sc = sm.sp[buf][lane][w];
-      const float mn = fmaxf(M, warp_max(sc));
-      float alpha = 1.f, pr = 0.f;
-      if (mn > -INFINITY) {
-        alpha = exp2f(M - mn);
-        pr = exp2f(sc - mn);
-      }
-      l = fmaf(l, alpha, warp_sum(pr));
-      M = mn;
-      sm.sp[buf][lane][w] = pr;
-      if (lane == 0) sm.alpha[buf][w] = alpha;
-    }
-    __syncthreads();
-    // ---- P.V: warp = positions 4w..4w+3 of the tile, lane = (dims 4dq.., heads 4hh..) ----
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+  float l = 0.f;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float a = sm.alpha[buf][4 * hh + e];
-      o[e][0] *= a; o[e][1] *= a; o[e][2] *= a; o[e][3] *= a;
-    }
+  for (int nt = 0; nt < 4; ++nt) {
+    sv[nt][0] = mx > -INFINITY ? exp2f(sv[nt][0] - mx) : 0.f;
+    sv[nt][1] = mx > -INFINITY ? exp2f(sv[nt][1] - mx) : 0.f;
+    l += sv[nt][0] + sv[nt][1];
+  }
+  l += __shfl_xor_sync(0xffffffffu, l, 1);
+  l += __shfl_xor_sync(0xffffffffu, l, 2);
+  // ---- O = P V: k = tokens (2 steps of 16), n = dims (8 tiles of 8) ----
+  float o[8][4];
 #pragma unroll
-    for (int jj = 0; jj < 4; ++jj) {
-      const int tok = 4 * w + jj;
-      const float4 v = *reinterpret_cast<const float4*>(&sm.v[t0 + tok][4 * dq]);   // zeros past the end
+  for (int nt = 0; nt < 8; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+#pragma unroll
+  for (int kk = 0; kk < 2; ++kk) {
+    uint32_t pa[4];
+    split_bf16x2(sv[2 * kk][0], sv[2 * kk][1], pa[0], pa[1]);
+    split_bf16x2(sv[2 * kk + 1][0], sv[2 * kk + 1][1], pa[2], pa[3]);
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      const int f = 8 * nt + g, chunk = (f & 31) >> 2;
+      const uint32_t col = vb + (f >> 5) * 4096 + 4 * (f & 3);
+      float v[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float pe = sm.sp[buf][tok][4 * hh + e];
-        o[e][0] = fmaf(pe, v.x, o[e][0]);
-        o[e][1] = fmaf(pe, v.y, o[e][1]);
-        o[e][2] = fmaf(pe, v.z, o[e][2]);
-        o[e][3] = fmaf(pe, v.w, o[e][3]);
+        const int tok = 16 * kk + 2 * tg + (e & 1) + 8 * (e >> 1);
+        v[e] = lds32(col + tok * 128 + ((chunk ^ (tok & 7)) << 4));
       }
+      uint32_t bh0, bl0, bh1, bl1;
+      split_bf16x2(v[0], v[1], bh0, bl0);
+      split_bf16x2(v[2], v[3], bh1, bl1);
+      mma_bf16(o[nt], pa, bh0, bh1);
+      mma_bf16(o[nt], pa, bl0, bl1);
     }
   }
-  __syncthreads();   // K rows are no longer read: fold the 8 warps' sums there
-  float* red = &sm.k[0][0];   // [warp][head][64]
+  // ---- fold the 4 warps: head h's (m, l) and o rows through shared memory ----
+  __syncthreads();   // every warp is done with its tiles
+  float* fo = reinterpret_cast<float*>(sm.kv);   // [warp][head][64]
 #pragma unroll
-  for (int e = 0; e < 4; ++e)
-    *reinterpret_cast<float4*>(red + (w * GROUP + 4 * hh + e) * HD + 4 * dq) =
-        make_float4(o[e][0], o[e][1], o[e][2], o[e][3]);
+  for (int nt = 0; nt < 8; ++nt)
+    *reinterpret_cast<float2*>(fo + (w * GROUP + g) * HD + 8 * nt + 2 * tg) =
+        make_float2(o[nt][0] + o[nt][2], o[nt][1] + o[nt][3]);
+  if (tg == 0) sm.wml[w][g] = make_float2(mx, l);
   __syncthreads();
-  float2 acc = make_float2(0.f, 0.f);
+  // thread -> head tid / 16, dims 4 (tid % 16) .. + 3
+  const int h = tid >> 4, d0 = 4 * (tid & 15);
+  float M = -INFINITY;
 #pragma unroll
-  for (int ww = 0; ww < 8; ++ww) {
-    const float2 x = *reinterpret_cast<const float2*>(red + (ww * GROUP + w) * HD + 2 * lane);
-    acc.x += x.x;
-    acc.y += x.y;
+  for (int ww = 0; ww < WARPS; ++ww) M = fmaxf(M, sm.wml[ww][h].x);
+  float L = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int ww = 0; ww < WARPS; ++ww) {
+    const float2 x = sm.wml[ww][h];
+    const float sw = (M > -INFINITY && x.x > -INFINITY) ? exp2f(x.x - M) : 0.f;
+    const float4 ov = *reinterpret_cast<const float4*>(fo + (ww * GROUP + h) * HD + d0);
+    L = fmaf(sw, x.y, L);
+    acc.x = fmaf(sw, ov.x, acc.x);
+    acc.y = fmaf(sw, ov.y, acc.y);
+    acc.z = fmaf(sw, ov.z, acc.z);
+    acc.w = fmaf(sw, ov.w, acc.w);
   }
-  const int h = kvh * GROUP + w;   // warp w holds head w's (M, l)
-  float* dst = p.part + ((int64_t)split * p.batch * H + (int64_t)b * H + h) * PART;
-  const float inv = l > 0.f ? 1.0f / l : 0.f;
-  dst[2 * lane] = acc.x * inv;
-  dst[2 * lane + 1] = acc.y * inv;
-  if (lane == 0) {
-    dst[HD] = l > 0.f ? M * 0.69314718055994531f : -INFINITY;
-    dst[HD + 1] = l;
+  float* dst = p.part + ((int64_t)split * p.batch * H + (int64_t)b * H + kvh * GROUP + h) * PART;
+  const float inv = L > 0.f ? 1.0f / L : 0.f;
+  // partial rows are 66 floats (264 bytes): 8-byte stores keep every address aligned
+  *reinterpret_cast<float2*>(dst + d0) = make_float2(acc.x * inv, acc.y * inv);
+  *reinterpret_cast<float2*>(dst + d0 + 2) = make_float2(acc.z * inv, acc.w * inv);
+  if ((tid & 15) == 0) {
+    dst[HD] = L > 0.f ? M * 0.69314718055994531f : -INFINITY;
+    dst[HD + 1] = L;
   }
 }
 
@@ -318,7 +323,7 @@ __global__ void window_ranges_kernel(const int32_t* __restrict__ seq_lens, int b
   te[b] = valid_end + 1;
 }
 
-constexpr size_t kSmem = sizeof(GatherSmem) + 16;
+constexpr size_t kSmem = sizeof(GatherSmem) + 1024;
 
 template <bool Q4, bool RULE>
 int32_t launch_positions(dim3 grid, const Params& p, cudaStream_t stream) {
