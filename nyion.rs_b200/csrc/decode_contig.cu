@@ -480,17 +480,19 @@ contig_kernel(const Params p, const __grid_constant__ CUtensorMap map_k, const _
     __stcg(reinterpret_cast<float2*>(p.part_o + (slot * GROUP + h) * HD + 2 * lane), acc);
     if (lane == 0) __stcg(&p.part_ml[slot * GROUP + h], make_float2(M, L));
   }
-  __threadfence();
+  // count in: the barrier makes the CTA's partial stores visible to thread 0,
+  // whose acq_rel atomic releases them at gpu scope (and, for the last CTA,
+  // acquires every other CTA's); the second barrier extends that to the CTA
   __syncthreads();
   if (tid == 0) {
-    const int old = atomicAdd(&p.cnt[kvh], 1);
+    int old;
+    asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(old) : "l"(p.cnt + kvh) : "memory");
     const int last = old == p.n_splits - 1;
     if (last) atomicExch(&p.cnt[kvh], 0);
     t.last = last;
   }
   __syncthreads();
   if (!t.last || warp >= NCW) return;
-  __threadfence();
   // ---- last CTA of this KV head: merge the splits, warp = head ----
   // The first 32 splits' o rows are loaded before the weights are known, so
   // their loads and the (m, l) loads share one L2 round trip.
