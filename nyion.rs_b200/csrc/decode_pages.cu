@@ -421,8 +421,10 @@ decode_pages_kernel(const Params p, const __grid_constant__ CUtensorMap map) {
   // ---- after the last unit: the parity-0 warp of each KV head counts the CTA
   // in for the (at most two) sequences it shares with other CTAs; where the
   // CTA is last, both warps of the head merge the CTA partials (heads 4 par ..
-  // 4 par + 3) with every partial's loads in flight together ----
-  __threadfence();
+  // 4 par + 3) with every partial's loads in flight together.  The named
+  // barrier just passed orders both warps' partial stores before lane 0's
+  // acq_rel atomic, which releases them at gpu scope and, in the last CTA,
+  // acquires the other CTAs' partials for both warps (next barrier) ----
   const int b_first = seq_of(s, p.batch, begin), b_last = seq_of(s, p.batch, end - 1);
 #pragma unroll 1
   for (int e = 0; e < 2; ++e) {
@@ -432,10 +434,10 @@ decode_pages_kernel(const Params p, const __grid_constant__ CUtensorMap map) {
     const int cfirst = pstart / W, clast = (pend - 1) / W;
     if (cfirst == clast) continue;                    // written above
     if (par == 0 && lane == 0) {
-      const int old = atomicAdd(&p.cnt[b * NKV + kvh], 1);
+      int old;
+      asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(old) : "l"(p.cnt + b * NKV + kvh) : "memory");
       const int last = (old == clast - cfirst);
       if (last) atomicExch(&p.cnt[b * NKV + kvh], 0);
-      __threadfence();
       s.xch[kvh].flag = last;
     }
     named_bar_sync(1 + kvh, 64);
