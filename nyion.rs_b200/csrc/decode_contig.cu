@@ -18,11 +18,15 @@
 // One call reads a few MB to a few hundred MB once:
 //
 //   * grid = (KV head, split), one CTA per SM: each CTA owns a contiguous
-//     range of 32-token tiles of one KV head;
+//     range of tiles of one KV head (f32: 32 tokens; f16: 64 tokens, so each
+//     copy is 8 KB: 4 KB pieces stream at about half the rate);
 //   * a producer warp streams the tiles with tensor copies (128-byte swizzle)
-//     into a 128 KB ring of stages, 8 consumer warps take the tiles
-//     round-robin, each tile computed by ONE warp for all 8 query heads of the
-//     GQA group, so no barrier spans the consumer warps;
+//     into a ring of stages (f32: 8 x 16 KB; f16: 12 x 16 KB); 8 consumer
+//     warps take them round-robin, every 32 tokens computed by ONE warp for
+//     all 8 query heads of the GQA group (an f16 tile by a pair of warps), so
+//     no barrier spans the consumer warps;
+//   * programmatic dependent launch: barrier set-up overlaps the previous grid,
+//     nothing global is read before it has completed;
 //   * S = Q K^T and O += P V run on mma.sync m16n8k16 with fp32 accumulation.
 //     The A operand stacks the hi parts of the 8 heads (rows 0-7) over their
 //     lo parts (rows 8-15), so one mma covers both halves of a split operand:
@@ -37,10 +41,10 @@
 //   * online softmax per warp in the log2 domain, the reference maximum moved
 //     only when a tile's maximum passes it by 8 (most tiles skip the rescale);
 //   * the 8 warps fold their partials in shared memory; every CTA leaves one
-//     (m, l, o[8][64]) partial per KV head and a counter per KV head tells
-//     the last CTA to merge them (warp = head, the weights computed once per
-//     split, every lane summing its two dims over the splits).  A single
-//     split writes the output directly.
+//     (m, l, o[8][64]) partial per KV head and counts in with one acq_rel
+//     atomic per KV head; the last CTA merges them (warp = head, the weights
+//     computed once per split, the first 32 splits' rows loaded together with
+//     the (m, l) pairs).  A single split writes the output directly.
 #include <cuda_fp16.h>
 #include <math.h>
 
