@@ -8,7 +8,7 @@ of ops::attention_sparse_q4 (ops.rs:597-723) against the CPU oracle.
 * attention_sparse_q4: oracle.attention_sparse_q4 on a ZonedPages store
   filled with the same tokens (writer-consistent nibble order), and the
   position kernel on oracle.sparse_positions' list;
-* edges: empty lists, lists longer than one 256-position split, ragged
+* edges: empty lists, lists spanning several 128-position splits, ragged
   batches, shuffled page tables, a page-table hole (skipped, page-range bit).
 Tolerance: max-abs 1e-3 (fp32 and 4-bit KV).
 """
