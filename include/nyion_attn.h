@@ -183,7 +183,10 @@ int32_t nyion_attn_decode_q4_window_ring(const float* q, const uint8_t* kv_pool,
  * A position whose page entry is outside [0, n_pool_pages) is skipped and
  * raises the page-range bit of the device error word.
  * workspace: nyion_attn_positions_workspace_size(batch, n_heads,
- * max_positions) bytes, or NULL.  This build: head_dim 64, GQA group 8. */
+ * max_positions) bytes (per-(sequence, KV head) merge counters first: reset
+ * once with nyion_attn_workspace_reset, every call leaves them at zero), or
+ * NULL.  One launch: the last CTA of each (sequence, KV head) merges the
+ * splits.  This build: head_dim 64, GQA group 8. */
 size_t nyion_attn_positions_workspace_size(int32_t batch, int32_t n_heads, int32_t max_positions);
 int32_t nyion_attn_decode_positions(const float* q, const void* kv_pool, int32_t kv_format,
                                     int64_t n_pool_pages, const int32_t* page_table,

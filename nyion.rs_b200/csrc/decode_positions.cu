@@ -69,6 +69,9 @@ struct Params {
   int64_t n_pool_pages;
   float sl2;                     // scale * log2(e)
   float* part;                   // [n_split][batch * H][66]
+  float* out;                    // [batch][H][64]: merged here (explicit mode), or null: partials only
+  int32_t* cnt;                  // [batch * n_kv] merge counters (start at 0, left at 0), with `out`
+  int32_t n_splits;              // with `out`
   int32_t* err;
 };
 
@@ -121,7 +124,85 @@ __device__ __forceinline__ void load_row_q4(const Params& p, int64_t row, float 
 struct GatherSmem {
   uint8_t kv[WARPS][2][TILE_BYTES];   // per warp: K tile | V tile (1024-byte aligned)
   float2 wml[WARPS][GROUP];           // per warp and head: (m log2, l)
+  int32_t last;
 };
+
+// With `out`: the CTA counts in for (b, kvh) after its partial is stored (one
+// acq_rel atomic after the CTA barrier), and the last of the n_splits CTAs
+// merges the partials of the 8 heads: w_s = l_s exp(m_s - M), o = sum w_s o_s /
+// sum w_s (the log-sum-exp identity of nyion_attn_lse_combine).
+__device__ __forceinline__ void count_in_and_merge(const Params& p, GatherSmem& sm, int b, int kvh) {
+  const int tid = threadIdx.x;
+  __syncthreads();   // this CTA's partial stores are ordered before thread 0's atomic
+  if (tid == 0) {
+    int old;
+    asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(old) : "l"(p.cnt + b * p.n_kv + kvh) : "memory");
+    const int last = old == p.n_splits - 1;
+    if (last) atomicExch(p.cnt + b * p.n_kv + kvh, 0);
+    sm.last = last;
+  }
+  __syncthreads();
+  if (!sm.last) return;
+  const int H = p.n_kv * GROUP;
+  const int h = tid >> 4, d0 = 4 * (tid & 15);   // head of the group, 4 dims
+  const int64_t row0 = (int64_t)b * H + kvh * GROUP;
+  const int64_t row = row0 + h;
+  const int64_t sstride = (int64_t)p.batch * H * PART;
+  // splits in chunks of MCH: their (m, l) pairs for the 8 heads go to shared
+  // memory in one parallel pass (the tiles are free), then every thread sums
+  // its 4 dims with 8 partial rows in flight; chunks fold online
+  constexpr int MCH = 256;
+  float2* mls = reinterpret_cast<float2*>(sm.kv);   // [MCH][8]
+  float M = -INFINITY, den = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int c0 = 0; c0 < p.n_splits; c0 += MCH) {
+    const int cn = min(MCH, p.n_splits - c0);
+    __syncthreads();   // the previous chunk's pairs have been read
+    for (int i = tid; i < cn * GROUP; i += THREADS) {
+      const float* pp = p.part + (int64_t)(c0 + i / GROUP) * sstride + (row0 + i % GROUP) * PART;
+      mls[i] = make_float2(__ldcg(pp + HD), __ldcg(pp + HD + 1));
+    }
+    __syncthreads();
+    float mc = -INFINITY;
+    for (int k = 0; k < cn; ++k) {
+      const float2 x = mls[k * GROUP + h];
+      if (x.y > 0.f) mc = fmaxf(mc, x.x);
+    }
+    const float Mn = fmaxf(M, mc);
+    if (Mn == -INFINITY) continue;                  // nothing attended so far
+    const float sc = M > -INFINITY ? expf(M - Mn) : 0.f;
+    den *= sc;
+    acc.x *= sc; acc.y *= sc; acc.z *= sc; acc.w *= sc;
+    M = Mn;
+    const float* src = p.part + (int64_t)c0 * sstride + row * PART + d0;
+    for (int k = 0; k < cn; k += 8) {
+      float4 ov[8];
+      float wv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int kk = k + u;
+        const float2 x = kk < cn ? mls[kk * GROUP + h] : make_float2(-INFINITY, 0.f);
+        wv[u] = x.y > 0.f ? x.y * expf(x.x - M) : 0.f;
+        ov[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (wv[u] > 0.f) {
+          const float2 a = __ldcg(reinterpret_cast<const float2*>(src + kk * sstride));
+          const float2 c = __ldcg(reinterpret_cast<const float2*>(src + kk * sstride + 2));
+          ov[u] = make_float4(a.x, a.y, c.x, c.y);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        den += wv[u];
+        acc.x = fmaf(wv[u], ov[u].x, acc.x);
+        acc.y = fmaf(wv[u], ov[u].y, acc.y);
+        acc.z = fmaf(wv[u], ov[u].z, acc.z);
+        acc.w = fmaf(wv[u], ov[u].w, acc.w);
+      }
+    }
+  }
+  const float inv = den > 0.f ? 1.0f / den : 0.f;
+  *reinterpret_cast<float4*>(p.out + row * HD + d0) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+}
 
 // byte offset of 16-byte chunk c16 (0..15) of row rr (0..31) in a tile
 __device__ __forceinline__ uint32_t tile_off(int rr, int c16) {
@@ -148,6 +229,7 @@ __global__ void __launch_bounds__(THREADS, 3) positions_kernel(const Params p) {
       p.part[((int64_t)split * p.batch * H + (int64_t)b * H + kvh * GROUP + h) * PART + e] =
           e == HD ? -INFINITY : 0.f;
     }
+    if (p.out) count_in_and_merge(p, sm, b, kvh);
     return;
   }
   const int cnt = j1 - j0;
@@ -306,6 +388,7 @@ __global__ void __launch_bounds__(THREADS, 3) positions_kernel(const Params p) {
     dst[HD] = L > 0.f ? M * 0.69314718055994531f : -INFINITY;
     dst[HD + 1] = L;
   }
+  if (p.out) count_in_and_merge(p, sm, b, kvh);
 }
 
 __global__ void window_ranges_kernel(const int32_t* __restrict__ seq_lens, int batch, int window,
@@ -362,9 +445,14 @@ int32_t check(const void* q, const void* pool, const int32_t* table, const float
 using namespace nyion;
 using namespace nyion::posd;
 
+// [merge counters: batch * n_kv ints, 256-byte aligned][split partials]
+static size_t positions_counter_bytes(int32_t batch, int32_t n_heads) {
+  return ((size_t)batch * (n_heads / GROUP > 0 ? n_heads / GROUP : 1) * sizeof(int32_t) + 255) & ~size_t(255);
+}
+
 extern "C" size_t nyion_attn_positions_workspace_size(int32_t batch, int32_t n_heads, int32_t max_positions) {
   const int ns = max_positions <= 0 ? 1 : (max_positions + SPLIT - 1) / SPLIT;
-  return part_bytes(ns, batch, n_heads);
+  return positions_counter_bytes(batch, n_heads) + part_bytes(ns, batch, n_heads);
 }
 
 extern "C" int32_t nyion_attn_decode_positions(const float* q, const void* kv_pool, int32_t kv_format,
@@ -384,9 +472,10 @@ extern "C" int32_t nyion_attn_decode_positions(const float* q, const void* kv_po
   st = device_info(&dev);
   if (st) return st;
   const int ns = (max_positions + SPLIT - 1) / SPLIT;
-  const size_t need = part_bytes(ns, batch, n_heads);
+  const size_t cb = positions_counter_bytes(batch, n_heads);
+  const size_t need = cb + part_bytes(ns, batch, n_heads);
   if (!workspace) {
-    st = internal_workspace(need, &workspace);
+    st = internal_workspace(need, &workspace, kWsCounters, cb, static_cast<cudaStream_t>(stream));
     if (st) return st;
   } else if (workspace_bytes < need) {
     return fail(NYION_ERR_WORKSPACE, "decode_positions: workspace %zu < %zu", workspace_bytes, need);
@@ -403,15 +492,15 @@ extern "C" int32_t nyion_attn_decode_positions(const float* q, const void* kv_po
   p.max_pages = max_pages;
   p.n_pool_pages = n_pool_pages;
   p.sl2 = (scale > 0.f ? scale : 1.0f / sqrtf((float)head_dim)) * 1.4426950408889634f;
-  p.part = static_cast<float*>(workspace);
+  p.cnt = static_cast<int32_t*>(workspace);
+  p.part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + cb);
+  p.out = out;
+  p.n_splits = ns;
   p.err = dev->err_word;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const dim3 grid((unsigned)(batch * n_kv_heads), (unsigned)ns);
-  st = kv_format == 0 ? launch_positions<false, false>(grid, p, s) : launch_positions<true, false>(grid, p, s);
-  if (st) return st;
-  st = check_cuda(cudaGetLastError(), "decode_positions launch");
-  if (st) return st;
-  return nyion_attn_lse_combine(p.part, ns, (int64_t)batch * n_heads, HD, out, stream);
+  // the last CTA of each (sequence, KV head) merges the splits: one launch
+  return kv_format == 0 ? launch_positions<false, false>(grid, p, s) : launch_positions<true, false>(grid, p, s);
 }
 
 extern "C" size_t nyion_attn_sparse_q4_workspace_size(int32_t batch, int32_t n_heads) {
