@@ -201,8 +201,9 @@ int32_t nyion_attn_decode_positions(const float* q, const void* kv_pool, int32_t
  * position set is { global_stride * gi : gi < min(window_start /
  * global_stride, 128) } followed by [window_start, valid_end].  The window
  * runs on the Q4 page kernel (nyion_attn_decode_q4_partial), the global
- * positions on the position kernel, and the two partials are merged by the
- * log-sum-exp combine.  Nibbles in the writer's order (cache.rs:637-663).
+ * positions on the position kernel, which folds the window's log-sum-exp
+ * partial into its own and writes `out` (two launches, plus one that turns
+ * seq_lens into window ranges).  Nibbles in the writer's order (cache.rs:637-663).
  * workspace: nyion_attn_sparse_q4_workspace_size(batch, n_heads) or NULL. */
 size_t nyion_attn_sparse_q4_workspace_size(int32_t batch, int32_t n_heads);
 int32_t nyion_attn_sparse_q4(const float* q, const uint8_t* kv_pool, int64_t n_pool_pages,

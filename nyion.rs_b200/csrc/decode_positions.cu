@@ -9,8 +9,8 @@
 //     positions = stride * gi for gi < min(window_start / stride, 128), then
 //     the window [window_start, valid_end] — nyion_attn_sparse_q4: the window
 //     is a token range of the Q4 page kernel (decode_q4.cu), the global
-//     positions go through this kernel, and the two log-sum-exp partials are
-//     merged.  Nibbles are read in the writer's order (element i in byte i/2,
+//     positions go through this kernel, whose CTA folds the window's
+//     log-sum-exp partial into its own and writes the output.  Nibbles are read in the writer's order (element i in byte i/2,
 //     low nibble for even i, cache.rs:637-663).
 //
 // Scattered positions cannot use page-granular copies, so rows are gathered:
@@ -25,15 +25,14 @@
 // bf16 hi + lo (the A operand stacks the 8 heads' hi parts over their lo
 // parts), softmax over the tile in the log2 domain.  The 4 warps' partials
 // are folded in shared memory into one (o/l, m, l) partial per head and
-// split, merged by nyion_attn_lse_combine.
+// split; the last CTA of each (sequence, KV head) to finish merges the
+// splits' partials and writes the output.
 #include <cuda_fp16.h>
 #include <math.h>
 
 #include "common.cuh"
 #include "host.h"
 
-extern "C" int32_t nyion_attn_lse_combine(const float* parts, int32_t n_parts, int64_t rows,
-                                          int32_t head_dim, float* out, void* stream);
 extern "C" int32_t nyion_attn_decode_q4_partial(const float* q, const uint8_t* kv_pool, int64_t n_pool_pages,
                                                 const int32_t* page_table, int32_t max_pages,
                                                 const int32_t* tok_begin, const int32_t* tok_end,
@@ -69,9 +68,10 @@ struct Params {
   int64_t n_pool_pages;
   float sl2;                     // scale * log2(e)
   float* part;                   // [n_split][batch * H][66]
-  float* out;                    // [batch][H][64]: merged here (explicit mode), or null: partials only
-  int32_t* cnt;                  // [batch * n_kv] merge counters (start at 0, left at 0), with `out`
+  float* out;                    // [batch][H][64]: merged here, or null: partials only
+  int32_t* cnt;                  // [batch * n_kv] merge counters (start at 0, left at 0), n_splits > 1
   int32_t n_splits;              // with `out`
+  const float* extra_part;       // with `out`: one more partial row set [batch * H][66] folded in, or null
   int32_t* err;
 };
 
@@ -128,26 +128,34 @@ struct GatherSmem {
 };
 
 // With `out`: the CTA counts in for (b, kvh) after its partial is stored (one
-// acq_rel atomic after the CTA barrier), and the last of the n_splits CTAs
-// merges the partials of the 8 heads: w_s = l_s exp(m_s - M), o = sum w_s o_s /
+// acq_rel atomic after the CTA barrier; a single split is its own last CTA),
+// and the last of the n_splits CTAs merges the partials of the 8 heads, plus
+// `extra_part`'s row when given: w_s = l_s exp(m_s - M), o = sum w_s o_s /
 // sum w_s (the log-sum-exp identity of nyion_attn_lse_combine).
 __device__ __forceinline__ void count_in_and_merge(const Params& p, GatherSmem& sm, int b, int kvh) {
   const int tid = threadIdx.x;
   __syncthreads();   // this CTA's partial stores are ordered before thread 0's atomic
-  if (tid == 0) {
-    int old;
-    asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(old) : "l"(p.cnt + b * p.n_kv + kvh) : "memory");
-    const int last = old == p.n_splits - 1;
-    if (last) atomicExch(p.cnt + b * p.n_kv + kvh, 0);
-    sm.last = last;
+  if (p.n_splits > 1) {
+    if (tid == 0) {
+      int old;
+      asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(old) : "l"(p.cnt + b * p.n_kv + kvh) : "memory");
+      const int last = old == p.n_splits - 1;
+      if (last) atomicExch(p.cnt + b * p.n_kv + kvh, 0);
+      sm.last = last;
+    }
+    __syncthreads();
+    if (!sm.last) return;
   }
-  __syncthreads();
-  if (!sm.last) return;
   const int H = p.n_kv * GROUP;
   const int h = tid >> 4, d0 = 4 * (tid & 15);   // head of the group, 4 dims
   const int64_t row0 = (int64_t)b * H + kvh * GROUP;
   const int64_t row = row0 + h;
   const int64_t sstride = (int64_t)p.batch * H * PART;
+  const int n_all = p.n_splits + (p.extra_part ? 1 : 0);
+  // partial row of split sp (the extra set last) for head row r
+  auto prow = [&](int sp, int64_t r) {
+    return sp < p.n_splits ? p.part + (int64_t)sp * sstride + r * PART : p.extra_part + r * PART;
+  };
   // splits in chunks of MCH: their (m, l) pairs for the 8 heads go to shared
   // memory in one parallel pass (the tiles are free), then every thread sums
   // its 4 dims with 8 partial rows in flight; chunks fold online
@@ -155,11 +163,11 @@ __device__ __forceinline__ void count_in_and_merge(const Params& p, GatherSmem& 
   float2* mls = reinterpret_cast<float2*>(sm.kv);   // [MCH][8]
   float M = -INFINITY, den = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int c0 = 0; c0 < p.n_splits; c0 += MCH) {
-    const int cn = min(MCH, p.n_splits - c0);
+  for (int c0 = 0; c0 < n_all; c0 += MCH) {
+    const int cn = min(MCH, n_all - c0);
     __syncthreads();   // the previous chunk's pairs have been read
     for (int i = tid; i < cn * GROUP; i += THREADS) {
-      const float* pp = p.part + (int64_t)(c0 + i / GROUP) * sstride + (row0 + i % GROUP) * PART;
+      const float* pp = prow(c0 + i / GROUP, row0 + i % GROUP);
       mls[i] = make_float2(__ldcg(pp + HD), __ldcg(pp + HD + 1));
     }
     __syncthreads();
@@ -174,7 +182,6 @@ __device__ __forceinline__ void count_in_and_merge(const Params& p, GatherSmem& 
     den *= sc;
     acc.x *= sc; acc.y *= sc; acc.z *= sc; acc.w *= sc;
     M = Mn;
-    const float* src = p.part + (int64_t)c0 * sstride + row * PART + d0;
     for (int k = 0; k < cn; k += 8) {
       float4 ov[8];
       float wv[8];
@@ -185,8 +192,9 @@ __device__ __forceinline__ void count_in_and_merge(const Params& p, GatherSmem& 
         wv[u] = x.y > 0.f ? x.y * expf(x.x - M) : 0.f;
         ov[u] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (wv[u] > 0.f) {
-          const float2 a = __ldcg(reinterpret_cast<const float2*>(src + kk * sstride));
-          const float2 c = __ldcg(reinterpret_cast<const float2*>(src + kk * sstride + 2));
+          const float* src = prow(c0 + kk, row) + d0;
+          const float2 a = __ldcg(reinterpret_cast<const float2*>(src));
+          const float2 c = __ldcg(reinterpret_cast<const float2*>(src + 2));
           ov[u] = make_float4(a.x, a.y, c.x, c.y);
         }
       }
@@ -560,8 +568,11 @@ extern "C" int32_t nyion_attn_sparse_q4(const float* q, const uint8_t* kv_pool, 
   p.n_pool_pages = n_pool_pages;
   p.sl2 = (scale > 0.f ? scale : 1.0f / sqrtf((float)head_dim)) * 1.4426950408889634f;
   p.part = parts + (size_t)batch * n_heads * PART;
+  // <= 128 globals: one split per (sequence, KV head), whose CTA folds the
+  // window's partial in and writes the output
+  p.out = out;
+  p.n_splits = 1;
+  p.extra_part = parts;
   p.err = dev->err_word;
-  st = launch_positions<true, true>(dim3((unsigned)(batch * n_kv_heads), 1), p, s);   // <= 128 globals: one split
-  if (st) return st;
-  return nyion_attn_lse_combine(parts, 2, (int64_t)batch * n_heads, HD, out, stream);
+  return launch_positions<true, true>(dim3((unsigned)(batch * n_kv_heads), 1), p, s);
 }
