@@ -60,6 +60,18 @@ size_t nyion_attn_decode_workspace_size(int32_t batch, int32_t n_kv_heads, int32
                                         int32_t head_dim);
 int32_t nyion_attn_workspace_reset(void* workspace, size_t bytes, void* stream);
 
+/* Host staging for callers with host buffers (the reference copies the query
+ * in and the output out with cudaMemcpy around its CUDA attention call,
+ * swamp-gpu/kernels/fused_attention.cu:313-330).
+ * nyion_attn_host_map: the device address of page-locked host memory
+ * (cudaHostAlloc / cudaHostRegister), NYION_ERR_CUDA for pageable memory.
+ * nyion_attn_copy_async: copies `bytes` from src to dst on `stream` with an SM
+ * kernel; either side may be a mapped host address from nyion_attn_host_map
+ * or device memory.  Ranges must not overlap.  In a CUDA graph the copy is a
+ * kernel node. */
+int32_t nyion_attn_host_map(const void* host, void** device_ptr);
+int32_t nyion_attn_copy_async(void* dst, const void* src, size_t bytes, void* stream);
+
 /* ---------------------------------------------------- paged fp32 decode ----
  * GQA decode attention with online softmax over an fp32 paged KV pool, one
  * query token per sequence.  Replaces the per-head score/softmax/AXPY loops

@@ -42,6 +42,8 @@ def lib() -> C.CDLL:
             "nyion_attn_device_error": (i32, [vp, C.POINTER(i32)]),
             "nyion_attn_decode_workspace_size": (sz, [i32, i32, i32, i32]),
             "nyion_attn_workspace_reset": (i32, [vp, sz, vp]),
+            "nyion_attn_host_map": (i32, [vp, C.POINTER(vp)]),
+            "nyion_attn_copy_async": (i32, [vp, vp, sz, vp]),
             "nyion_attn_decode_paged_f32": (i32, [vp, vp, i64, vp, i32, vp, vp, i32, i32, i32, i32,
                                                   i32, f32, vp, sz, vp]),
             "nyion_attn_decode_zoned_f32": (i32, [vp, vp, vp, vp, i64, i32, i32, i64, i64, i32, i32,
@@ -164,6 +166,31 @@ def _stream_ptr(stream=None) -> int:
     torch = _torch()
     s = stream if stream is not None else torch.cuda.current_stream()
     return int(s.cuda_stream)
+
+
+def device_address(t) -> int:
+    """Address of tensor `t` as the device sees it: data_ptr() for a CUDA
+    tensor, the mapped address (nyion_attn_host_map) for a pinned CPU tensor."""
+    if t.is_cuda:
+        return int(t.data_ptr())
+    if not t.is_pinned():
+        raise ValueError("device_address: a CPU tensor must be pinned (page-locked)")
+    base = int(t.untyped_storage().data_ptr())
+    d = C.c_void_p()
+    check(lib().nyion_attn_host_map(base, C.byref(d)))
+    return int(d.value) + (int(t.data_ptr()) - base)
+
+
+def copy_async(dst, src, stream=None, dst_addr: int | None = None, src_addr: int | None = None) -> None:
+    """dst <- src (same byte size, contiguous) by an SM kernel on `stream`;
+    either may be a pinned CPU tensor.  dst_addr / src_addr: addresses from
+    device_address() resolved beforehand (e.g. outside a CUDA graph capture)."""
+    n = dst.numel() * dst.element_size()
+    if n != src.numel() * src.element_size() or not (dst.is_contiguous() and src.is_contiguous()):
+        raise ValueError("copy_async: contiguous tensors of equal byte size required")
+    check(lib().nyion_attn_copy_async(dst_addr if dst_addr is not None else device_address(dst),
+                                      src_addr if src_addr is not None else device_address(src), n,
+                                      _stream_ptr(stream)))
 
 
 class Workspace:
