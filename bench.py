@@ -219,8 +219,22 @@ def build_q4_pages(A, torch, n_tokens, dev, gen, page_perm=True):
     return pool, order.to(torch.int32)
 
 
-def timed_graph(torch, fn, stream, steps, warmup, barrier, dist=None, world=1, dev=None, graph=True):
-    """CUDA-event time of fn() per call (graph replay when capture works), max over ranks."""
+_FLUSH = {}
+
+
+def l2_flush_buffer(torch, dev):
+    """256 MB device buffer (twice the 126 MB L2) written before each timed step
+    whose inputs would otherwise stay resident in L2 between steps."""
+    if dev not in _FLUSH:
+        _FLUSH[dev] = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    return _FLUSH[dev]
+
+
+def timed_graph(torch, fn, stream, steps, warmup, barrier, dist=None, world=1, dev=None, graph=True,
+                flush=None):
+    """CUDA-event time of fn() per call (graph replay when capture works), max over ranks.
+    With `flush` (a buffer larger than L2), every timed step is preceded by a
+    write of the whole buffer, outside its own event pair."""
     g = None
     with torch.cuda.stream(stream):
         for _ in range(max(3, warmup)):
@@ -244,15 +258,27 @@ def timed_graph(torch, fn, stream, steps, warmup, barrier, dist=None, world=1, d
             run()
         torch.cuda.synchronize()
         barrier()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(steps):
-            run()
-        e1.record(stream)
-        torch.cuda.synchronize()
+        if flush is None:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(steps):
+                run()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / steps
+        else:
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(steps)]
+            for e0, e1 in evs:
+                flush.fill_(1)
+                e0.record(stream)
+                run()
+                e1.record(stream)
+            torch.cuda.synchronize()
+            ms = sum(e0.elapsed_time(e1) for e0, e1 in evs) / steps
+            mode += ", 256 MB L2 flush before each timed step"
         barrier()
-    ms = e0.elapsed_time(e1) / steps
     if world > 1:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -272,15 +298,24 @@ def run_config1(A, torch, dev, stream, args, barrier, dist, world, with_cpu):
     v = torch.randn(pages * N_KV * slots * D, device=dev, generator=gen)
     q = torch.randn(H, D, device=dev, generator=gen)
     out = torch.empty_like(q)
-    calls = 22   # one call per layer of a 22-layer step, captured together like config 2
+    # timing: one call per layer of a 22-layer step, each layer its own K/V rows
+    # (a 22-layer zone arena), captured together like config 2; L2 flushed
+    # before every timed step
+    calls = 22
+    k22 = torch.randn(pages * calls * N_KV * slots * D, device=dev, generator=gen)
+    v22 = torch.randn(pages * calls * N_KV * slots * D, device=dev, generator=gen)
+    q22 = torch.randn(calls, H, D, device=dev, generator=gen)
+    out22 = torch.empty_like(q22)
 
     def fn():
-        for _ in range(calls):
-            A.decode_zoned_f32(q, k, v, 1, 0, ctx, ctx - 1, out=out, stream=stream)
+        for l in range(calls):
+            A.decode_zoned_f32(q22[l], k22, v22, calls, l, ctx, ctx - 1, out=out22[l], stream=stream)
 
-    ms, mode = timed_graph(torch, fn, stream, max(args.steps, 20), args.warmup, barrier, dist, world, dev)
+    ms, mode = timed_graph(torch, fn, stream, max(args.steps, 20), args.warmup, barrier, dist, world, dev,
+                           flush=l2_flush_buffer(torch, dev))
+    A.decode_zoned_f32(q, k, v, 1, 0, ctx, ctx - 1, out=out, stream=stream)   # the parity case
     r = {"workload": "config1: 1 layer, B=1, ctx 128, reference zone-page layout", "us_per_call": ms * 1e3 / calls,
-         "timing": f"{mode} of {calls} calls", "launches_per_step": 1}
+         "timing": f"{mode} of {calls} calls (22 layers of one zone arena)", "launches_per_step": 1}
     if with_cpu:
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         import oracle as O   # CPU baseline leg only
@@ -320,7 +355,9 @@ def run_config3(A, torch, dev, stream, args, barrier, dist, world):
     out = torch.empty_like(q)
     ws = A.window_ring_workspace(B, device=dev)
     fn = lambda: A.decode_q4_window_ring(q, pool, table, lens, ring, W, out=out, workspace=ws, stream=stream)
-    ms, mode = timed_graph(torch, fn, stream, args.steps, args.warmup, barrier, dist, world, dev)
+    # the window (21 MB) and ring fit in L2: flushed before every timed step
+    ms, mode = timed_graph(torch, fn, stream, args.steps, args.warmup, barrier, dist, world, dev,
+                           flush=l2_flush_buffer(torch, dev))
     q4_bytes = B * 2 * N_KV * (W - R) * 40
     ring_bytes = B * 2 * N_KV * R * D * 4
     qo = 2 * B * H * D * 4
@@ -509,7 +546,10 @@ def run_config5(A, S, torch, dev, stream, args, barrier, dist, world, rank):
     res = {}
     for m, d in decs.items():
         fn = lambda d=d: d.step(q, pool, table, stream=stream)
-        res[m] = timed_graph(torch, fn, stream, args.steps, args.warmup, barrier, dist, world, dev)
+        # each rank's shard is 335 MB / world: below L2 from 4 ranks on, so every
+        # timed step follows an L2 flush on every rank
+        res[m] = timed_graph(torch, fn, stream, args.steps, args.warmup, barrier, dist, world, dev,
+                             flush=l2_flush_buffer(torch, dev))
     diff = (decs["p2p"].step(q, pool, table, stream=stream) -
             decs["collective"].step(q, pool, table, stream=stream)).abs().max().item()
     err = A.device_error(stream)
