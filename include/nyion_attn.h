@@ -101,9 +101,9 @@ int32_t nyion_attn_decode_paged_f32(const float* q, const float* kv_pool, int64_
 /* ------------------------------------- paged fp32 decode, no allocation ----
  * No counterpart in the reference.  Same arguments and result as
  * nyion_attn_decode_paged_f32 without the workspace, for callers that must
- * not allocate device memory while decoding (a thread inside CUDA-graph
- * capture, a serving loop that cannot afford cudaFree's device-wide
- * synchronisation, a host whose HBM is fully owned by its own arena).  The
+ * not allocate device memory while decoding (a serving loop that cannot
+ * afford cudaFree's device-wide synchronisation, a host whose HBM is fully
+ * owned by its own arena, a plugin host that forbids library allocations).  The
  * split-KV scratch is a fixed 8 MiB device array inside the library, reserved
  * on every GPU that loads it; the call allocates nothing.  Limit: batch <= 512;
  * with 4 KV heads (the whole-page kernel of the main entry) every such batch

@@ -1002,20 +1002,19 @@ extern "C" void gpu_graph_destroy(void* graph_handle) {
 
 // ---- allocation-free variant of the paged fp32 decode -----------------------
 //
-// For callers that cannot allocate device memory at decode time: a thread in
-// the middle of capturing a CUDA graph (cudaMalloc is not allowed while a
-// capture is open), a latency-critical serving loop that must never hit
-// cudaFree's implicit device synchronisation, or a host whose HBM is entirely
-// handed out by its own arena so an extra cudaMalloc would fail or fragment
-// it.  The split-KV scratch (merge counters and log-sum-exp partials) lives
+// For callers that cannot allocate device memory at decode time: a
+// latency-critical serving loop that must never hit cudaFree's implicit device
+// synchronisation, a host whose HBM is entirely handed out by its own arena so
+// an extra cudaMalloc would fail or fragment it, or a plugin host whose rules
+// forbid a library from allocating behind its back.  The split-KV scratch (merge counters and log-sum-exp partials) lives
 // in one file-scope device array instead, sized kNoAllocScratchBytes; every
 // GPU that loads this library reserves it until the process exits.
 //
 // The first call on a device looks up the array's device address with
 // cudaGetSymbolAddress (and sets the kernel's shared-memory attribute); make
 // that first call before any stream capture.  All calls on a device share the
-// one array, so calls that overlap on the GPU (different streams, or graphs
-// replayed concurrently) race and corrupt each other's partials: serialise
+// one array, so calls that overlap on the GPU (for example on different
+// streams) race and corrupt each other's partials: serialise
 // them.  The merge counters are cleared at the start of every call.
 // Device-side page-id range errors of this variant go to a private error
 // word and are not reported by nyion_attn_device_error.

@@ -1,8 +1,8 @@
 """The allocation-free decode entry point (nyion_attn_decode_paged_f32_noalloc).
 
-Some callers cannot allocate device memory while they decode — a thread that
-is capturing a CUDA graph, a serving loop that must not stall on cudaFree's
-device synchronisation, a host whose HBM is fully owned by its own arena.
+Some callers cannot allocate device memory while they decode — a serving loop
+that must not stall on cudaFree's device synchronisation, a host whose HBM is
+fully owned by its own arena, a plugin host that forbids library allocations.
 This variant keeps its split-KV scratch in a fixed device array inside the
 library.  The test calls it through the C ABI twice in a row and checks both
 results against the workspace-taking entry point (same tolerance as the other
