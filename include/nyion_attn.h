@@ -43,7 +43,9 @@ enum {
 int32_t nyion_attn_version(void);
 const char* nyion_attn_last_error(void);
 /* Synchronises `stream`, returns the current device's error word in *bits and
- * clears it.  Returns NYION_ERR_DEVICE when any bit was set.  Replaces the
+ * clears it (the bits of every entry point that has run on the device,
+ * nyion_attn_decode_paged_f32_noalloc's own word included; no allocation).
+ * Returns NYION_ERR_DEVICE when any bit was set.  Replaces the
  * reference's per-call stderr + `return -1` (fused_attention.cu:218-240),
  * which cannot see asynchronous device faults. */
 int32_t nyion_attn_device_error(void* stream, int32_t* bits);
@@ -112,8 +114,11 @@ int32_t nyion_attn_decode_paged_f32(const float* q, const float* kv_pool, int64_
  * return NYION_ERR_WORKSPACE.  The first call on a device resolves the
  * array's address (cudaGetSymbolAddress): make it before any stream capture.
  * Calls share the array: calls that overlap on the GPU race, so serialise
- * them.  Page-id range errors of this variant are not reported by
- * nyion_attn_device_error. */
+ * them.  Page-id range errors of this variant set its own device error word,
+ * which nyion_attn_device_error reads and clears with the shared one (it
+ * allocates nothing when only this entry point has run on the device).  The
+ * resolved addresses belong to the current CUDA context: do not use the
+ * library again after cudaDeviceReset. */
 int32_t nyion_attn_decode_paged_f32_noalloc(const float* q, const float* kv_pool,
                                             int64_t n_pool_pages, const int32_t* page_table,
                                             int32_t max_pages, const int32_t* seq_lens,
@@ -346,6 +351,10 @@ int32_t nyion_attn_decode_ring_f16(const float* q, const void* k_ring, const voi
 int32_t nyion_attn_softmax_padic(const float* logits, float* probs, int32_t n, float temperature,
                                  void* stream);
 void mojo_softmax_padic(const float* logits, float* probs, int n, float temperature);
+/* exp_q16_16 (swamp-kernels/src/lib.rs:97-103) of the softmax above, over a
+ * device array: out[i] = 0 for x < -655360, 65536 for x >= 0, else
+ * round(exp(x / 65536) * 65536).  Device pointers, asynchronous on `stream`. */
+int32_t nyion_attn_exp_q16_16(const int32_t* x_fixed, int32_t* out, int64_t n, void* stream);
 
 /* Stokes KV store (lib.rs:27-85), same names and arguments: keys / values of
  * head_dim floats per appended token (host pointers), a score per token;

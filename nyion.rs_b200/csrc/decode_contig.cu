@@ -618,15 +618,8 @@ int32_t launch(Params p, const void* k, const void* v, uint64_t rows, int max_to
   } else if (ws_bytes < need) {
     return fail(NYION_ERR_WORKSPACE, "row decode: workspace %zu B < %zu B", ws_bytes, need);
   }
-  static bool attr_set[64] = {false};
-  const int di = dev->device < 64 ? dev->device : 0;
-  if (!attr_set[di]) {
-    st = check_cuda(cudaFuncSetAttribute(contig_kernel<T, LAYOUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem_bytes<T>()),
-                    "cudaFuncSetAttribute(row decode)");
-    if (st) return st;
-    attr_set[di] = true;
-  }
+  st = kernel_setup(reinterpret_cast<const void*>(contig_kernel<T, LAYOUT>), smem_bytes<T>(), THREADS, nullptr);
+  if (st) return st;
   p.n_splits = pl.n_splits;
   p.tiles_per_split = pl.tiles_per_split;
   uint8_t* base = static_cast<uint8_t*>(ws);

@@ -574,22 +574,11 @@ int32_t launch(const Params& base, const CUtensorMap& map, int batch,
   DeviceInfo* dev = nullptr;
   int32_t st = device_info(&dev);
   if (st) return st;
-  static int occ_cache[64] = {0};
-  int di = dev->device < 64 ? dev->device : 0;
-  size_t smem = smem_bytes();
-  if (!occ_cache[di]) {
-    st = check_cuda(cudaFuncSetAttribute(decode_f32_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                    "cudaFuncSetAttribute(decode_f32)");
-    if (st) return st;
-    int occ = 0;
-    st = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_f32_kernel,
-                                                                  THREADS, smem),
-                    "occupancy(decode_f32)");
-    if (st) return st;
-    occ_cache[di] = occ > 0 ? occ : 1;
-  }
-  int grid = dev->num_sms * occ_cache[di];
+  const size_t smem = smem_bytes();
+  int occ = 1;
+  st = kernel_setup(reinterpret_cast<const void*>(decode_f32_kernel), smem, THREADS, &occ);
+  if (st) return st;
+  int grid = dev->num_sms * occ;
   if (grid > MAX_GRID) grid = MAX_GRID;
   WsLayout w = ws_layout(batch, base.n_kv);
   for (int b0 = 0; b0 < batch; b0 += MAX_SEQS) {
@@ -1016,8 +1005,12 @@ extern "C" void gpu_graph_destroy(void* graph_handle) {
 // one array, so calls that overlap on the GPU (for example on different
 // streams) race and corrupt each other's partials: serialise
 // them.  The merge counters are cleared at the start of every call.
-// Device-side page-id range errors of this variant go to a private error
-// word and are not reported by nyion_attn_device_error.
+// Device-side page-id range errors of this variant go to its own error word,
+// a second file-scope device variable; nyion_attn_device_error reads and
+// clears it together with the shared word, and allocates nothing when only
+// this entry point has run on the device.  The cached addresses belong to the
+// CUDA context that resolved them: after cudaDeviceReset the library (this
+// entry point included) must not be used again in the process.
 namespace nyion {
 namespace f32dec {
 
@@ -1054,15 +1047,8 @@ static int32_t noalloc_setup(NoAllocDevice** out) {
     if (st) return st;
     cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
     if (major != 10) return fail(NYION_ERR_UNSUPPORTED, "device %d is not sm_100a", dev);
-    const size_t smem = smem_bytes();
-    st = check_cuda(cudaFuncSetAttribute(decode_f32_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                    "cudaFuncSetAttribute(decode_f32)");
-    if (st) return st;
-    int occ = 0;
-    st = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_f32_kernel,
-                                                                  THREADS, smem),
-                    "occupancy(decode_f32)");
+    int occ = 1;
+    st = kernel_setup(reinterpret_cast<const void*>(decode_f32_kernel), smem_bytes(), THREADS, &occ);
     if (st) return st;
     d.scratch = static_cast<uint8_t*>(sp);
     d.err = static_cast<int32_t*>(ep);
@@ -1076,6 +1062,14 @@ static int32_t noalloc_setup(NoAllocDevice** out) {
 }
 
 }  // namespace f32dec
+
+int32_t* noalloc_error_word_if_ready() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(f32dec::g_noalloc_mu);
+  return f32dec::g_noalloc_dev[dev].ready ? f32dec::g_noalloc_dev[dev].err : nullptr;
+}
+
 }  // namespace nyion
 
 extern "C" int32_t nyion_attn_decode_paged_f32_noalloc(

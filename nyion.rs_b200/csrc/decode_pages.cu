@@ -537,21 +537,11 @@ int32_t launch_pages(const float* q, const float* kv_pool, int64_t n_pool_pages,
                      CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
   }
-  static int occ_cache[64] = {0};
-  const int di = dev->device < 64 ? dev->device : 0;
   const size_t smem = smem_bytes();
-  if (!occ_cache[di]) {
-    st = check_cuda(cudaFuncSetAttribute(decode_pages_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem),
-                    "cudaFuncSetAttribute(decode_pages)");
-    if (st) return st;
-    int occ = 0;
-    st = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_pages_kernel, THREADS, smem),
-                    "occupancy(decode_pages)");
-    if (st) return st;
-    occ_cache[di] = occ > 0 ? occ : 1;
-  }
-  int grid = dev->num_sms * occ_cache[di];
+  int occ = 1;
+  st = kernel_setup(reinterpret_cast<const void*>(decode_pages_kernel), smem, THREADS, &occ);
+  if (st) return st;
+  int grid = dev->num_sms * occ;
   if (grid > MAX_GRID) grid = MAX_GRID;
   auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
   for (int b0 = 0; b0 < batch; b0 += MAX_SEQS) {

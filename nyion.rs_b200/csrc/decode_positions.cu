@@ -418,17 +418,8 @@ constexpr size_t kSmem = sizeof(GatherSmem) + 1024;
 
 template <bool Q4, bool RULE>
 int32_t launch_positions(dim3 grid, const Params& p, cudaStream_t stream) {
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const int di = dev < 64 ? dev : 0;
-  if (!attr_set[di]) {
-    const int32_t st = check_cuda(cudaFuncSetAttribute(positions_kernel<Q4, RULE>,
-                                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem),
-                                  "cudaFuncSetAttribute(positions)");
-    if (st) return st;
-    attr_set[di] = true;
-  }
+  const int32_t st = kernel_setup(reinterpret_cast<const void*>(positions_kernel<Q4, RULE>), kSmem, THREADS, nullptr);
+  if (st) return st;
   positions_kernel<Q4, RULE><<<grid, THREADS, kSmem, stream>>>(p);
   return check_cuda(cudaGetLastError(), "positions launch");
 }

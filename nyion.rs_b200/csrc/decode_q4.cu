@@ -1062,21 +1062,11 @@ int32_t launch_partial(Params base, int batch, const int32_t* tok_begin, const i
   DeviceInfo* dev = nullptr;
   int32_t st = device_info(&dev);
   if (st) return st;
-  static int grid_cache[64] = {0};
-  const int di = dev->device < 64 ? dev->device : 0;
   const size_t smem = smem_bytes();
-  if (!grid_cache[di]) {
-    st = check_cuda(cudaFuncSetAttribute(decode_q4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem),
-                    "cudaFuncSetAttribute(decode_q4)");
-    if (st) return st;
-    int occ = 0;
-    st = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_q4_kernel, THREADS, smem),
-                    "occupancy(decode_q4)");
-    if (st) return st;
-    grid_cache[di] = dev->num_sms * (occ > 0 ? occ : 1);
-    if (grid_cache[di] > MAX_GRID) grid_cache[di] = MAX_GRID;
-  }
+  int occ = 1;
+  st = kernel_setup(reinterpret_cast<const void*>(decode_q4_kernel), smem, THREADS, &occ);
+  if (st) return st;
+  const int grid = dev->num_sms * occ < MAX_GRID ? dev->num_sms * occ : MAX_GRID;
   const WsLayout w = ws_layout(batch);
   for (int b0 = 0; b0 < batch; b0 += MAX_SEQS) {
     Params p = base;
@@ -1091,7 +1081,7 @@ int32_t launch_partial(Params base, int batch, const int32_t* tok_begin, const i
     p.meta = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws) + w.meta);
     p.cta_part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + w.cta_part);
     p.err = dev->err_word;
-    st = check_cuda(launch_pdl(decode_q4_kernel, dim3(grid_cache[di]), dim3(THREADS), smem, stream, p),
+    st = check_cuda(launch_pdl(decode_q4_kernel, dim3(grid), dim3(THREADS), smem, stream, p),
                     "decode_q4 launch");
     if (st) return st;
     float* fo = final_out ? final_out + (int64_t)b0 * NKV * GROUP * HD : nullptr;

@@ -122,14 +122,9 @@ extern "C" int32_t nyion_attn_gemv_q4k(const uint8_t* w, const float* x, float* 
   if (reinterpret_cast<uintptr_t>(w) & 15) return fail(NYION_ERR_INVALID, "gemv_q4k: weights must be 16-byte aligned");
   const size_t sm = smem_bytes(n_blocks);
   if (sm > 227 * 1024) return fail(NYION_ERR_UNSUPPORTED, "gemv_q4k: n_blocks %d too large for one pass", n_blocks);
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (sm > 48 * 1024 && dev < 64 && !attr_set[dev]) {
-    int32_t st = check_cuda(cudaFuncSetAttribute(gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024),
-                            "gemv_q4k smem attribute");
+  if (sm > 48 * 1024) {   // the limit is raised once per device to the largest size any call may use
+    const int32_t st = kernel_setup(reinterpret_cast<const void*>(gemv_kernel), 227 * 1024, THREADS, nullptr);
     if (st) return st;
-    attr_set[dev] = true;
   }
   gemv_kernel<<<(n_rows + ROWS_CTA - 1) / ROWS_CTA, THREADS, sm, static_cast<cudaStream_t>(stream)>>>(
       w, x, out, n_rows, n_blocks, batch);

@@ -3,7 +3,9 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <map>
 #include <mutex>
+#include <utility>
 #include <vector>
 
 #include "host.h"
@@ -56,6 +58,39 @@ int32_t device_info(DeviceInfo** out) {
     d.err_word = w;
   }
   *out = &d;
+  return NYION_OK;
+}
+
+int32_t* device_error_word_if_ready() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (dev < 0 || (int)g_devs.size() <= dev || g_devs[dev].device < 0) return nullptr;
+  return g_devs[dev].err_word;
+}
+
+static std::mutex g_kernel_mu;
+static std::map<std::pair<const void*, int>, int> g_kernel_occ;   // (kernel, device) -> blocks per SM
+
+int32_t kernel_setup(const void* func, size_t smem, int threads, int* occ) {
+  int dev = -1;
+  int32_t st = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  if (st) return st;
+  std::lock_guard<std::mutex> lk(g_kernel_mu);
+  const auto key = std::make_pair(func, dev);
+  auto it = g_kernel_occ.find(key);
+  if (it == g_kernel_occ.end()) {
+    if (smem > 48 * 1024) {
+      st = check_cuda(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                      "cudaFuncSetAttribute(max dynamic shared memory)");
+      if (st) return st;
+    }
+    int n = 0;
+    st = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, func, threads, smem), "occupancy query");
+    if (st) return st;
+    it = g_kernel_occ.emplace(key, n > 0 ? n : 1).first;
+  }
+  if (occ) *occ = it->second;
   return NYION_OK;
 }
 
@@ -170,22 +205,30 @@ extern "C" int32_t nyion_attn_version(void) { return NYION_ATTN_VERSION; }
 
 extern "C" const char* nyion_attn_last_error(void) { return g_msg; }
 
+// Reads and clears the error words of the current device: the one the
+// workspace-taking entry points share and the allocation-free decode's own.
+// Only words that already exist are read, so a process that has used nothing
+// but the allocation-free entry point allocates nothing here either.
 extern "C" int32_t nyion_attn_device_error(void* stream, int32_t* bits) {
-  DeviceInfo* d = nullptr;
-  int32_t st = device_info(&d);
-  if (st) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  int32_t h = 0;
-  st = check_cuda(cudaMemcpyAsync(&h, d->err_word, sizeof(int32_t), cudaMemcpyDeviceToHost, s),
-                  "read error word");
-  if (st) return st;
+  int32_t* words[2] = {device_error_word_if_ready(), noalloc_error_word_if_ready()};
+  int32_t vals[2] = {0, 0};
+  int32_t st = NYION_OK;
+  for (int i = 0; i < 2; ++i) {
+    if (!words[i]) continue;
+    st = check_cuda(cudaMemcpyAsync(&vals[i], words[i], sizeof(int32_t), cudaMemcpyDeviceToHost, s),
+                    "read error word");
+    if (st) return st;
+  }
   st = check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize");
   if (st) return st;
-  if (h) {
-    st = check_cuda(cudaMemsetAsync(d->err_word, 0, sizeof(int32_t), s), "clear error word");
+  for (int i = 0; i < 2; ++i) {
+    if (!vals[i]) continue;
+    st = check_cuda(cudaMemsetAsync(words[i], 0, sizeof(int32_t), s), "clear error word");
     if (st) return st;
-    cudaStreamSynchronize(s);
   }
+  if (vals[0] || vals[1]) cudaStreamSynchronize(s);
+  const int32_t h = vals[0] | vals[1];
   if (bits) *bits = h;
   if (h)
     return fail(NYION_ERR_DEVICE, "device error word 0x%x (%s%s%s)", h,

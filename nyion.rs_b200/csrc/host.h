@@ -22,6 +22,18 @@ struct DeviceInfo {
 };
 // Info for the current device; allocates the error word on first use.
 int32_t device_info(DeviceInfo** out);
+// The current device's error word if device_info has already set it up on
+// this device, else null (never allocates).
+int32_t* device_error_word_if_ready();
+// The allocation-free decode's own error word on the current device once that
+// entry point has run there, else null (decode_f32.cu; never allocates).
+int32_t* noalloc_error_word_if_ready();
+
+// Sets `func`'s dynamic shared-memory limit to `smem` bytes on the current
+// device (once per kernel and device) and returns in *occ (when non-null) how
+// many blocks of `threads` threads are resident per SM.  Thread-safe: the
+// per-(kernel, device) results are kept under a mutex.
+int32_t kernel_setup(const void* func, size_t smem, int threads, int* occ);
 
 // 2-D row-major tensor map over `rows` rows of `row_elems` elements of
 // `dtype`, box = (box_x elements, box_y rows), 128-byte swizzle.

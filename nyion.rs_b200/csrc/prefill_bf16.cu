@@ -612,14 +612,9 @@ extern "C" int32_t nyion_attn_prefill_paged_bf16(const void* q, const void* kv_p
                      CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
   }
-  static bool attr_done[64] = {false};
   const size_t smem = smem_bytes();
-  if (!attr_done[dev->device < 64 ? dev->device : 0]) {
-    st = check_cuda(cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                    "cudaFuncSetAttribute(prefill)");
-    if (st) return st;
-    attr_done[dev->device < 64 ? dev->device : 0] = true;
-  }
+  st = kernel_setup(reinterpret_cast<const void*>(prefill_kernel), smem, THREADS, nullptr);
+  if (st) return st;
   Params p{};
   p.table = page_table;
   p.max_pages = max_pages;

@@ -12,8 +12,13 @@
 //   inv     = 2^32 / sum e  (u64 division, kept as i32)
 //   16-wide blocks: (u32)(e * inv) >> 16 (low 32 bits, logical shift);
 //   tail: (i64)e * inv >> 16;  probs = fixed / 65536.
-// exp is taken in double and rounded to float, which is the correctly
-// rounded expf value (the reference's glibc expf is within 0.502 ulp of it).
+// exp is taken in double and rounded to float (the correctly rounded expf
+// value).  glibc's expf, which Rust's f32::exp calls on Linux, is not always
+// correctly rounded (glibc 2.39: 437 of the 655,360 inputs of exp_q16_16 get
+// the other neighbour), but on none of those inputs does the difference
+// survive round(e * 65536): the Q16.16 results agree on the whole domain.
+// nyion_attn_exp_q16_16 exposes this function over an array so that a test
+// compares every input with the CPU oracle bit for bit.
 #include <math.h>
 #include <stdlib.h>
 #include <string.h>
@@ -89,6 +94,12 @@ __global__ void __launch_bounds__(THREADS) softmax_padic_kernel(const float* __r
   }
 }
 
+// exp_q16_16 over an array (the test of the whole domain).
+__global__ void exp_q16_16_kernel(const int32_t* __restrict__ x, int32_t* __restrict__ out, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = exp_q16_16(x[i]);
+}
+
 }  // namespace smx
 
 // ---- Stokes KV store: device rows, host scores ------------------------------
@@ -118,6 +129,15 @@ extern "C" int32_t nyion_attn_softmax_padic(const float* logits, float* probs, i
   smx::softmax_padic_kernel<<<1, smx::THREADS, 0, static_cast<cudaStream_t>(stream)>>>(logits, probs, n,
                                                                                       temperature);
   return check_cuda(cudaGetLastError(), "softmax_padic launch");
+}
+
+extern "C" int32_t nyion_attn_exp_q16_16(const int32_t* x_fixed, int32_t* out, int64_t n, void* stream) {
+  if (!x_fixed || !out || n < 0) return fail(NYION_ERR_INVALID, "exp_q16_16: bad arguments");
+  if (n == 0) return NYION_OK;
+  const int64_t blocks = (n + 255) / 256;
+  smx::exp_q16_16_kernel<<<(unsigned)(blocks < 4096 ? blocks : 4096), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x_fixed, out, n);
+  return check_cuda(cudaGetLastError(), "exp_q16_16 launch");
 }
 
 // Same name, arguments and silence on bad input as the reference
