@@ -96,6 +96,7 @@ def lib() -> C.CDLL:
                                            vp, sz, vp]),
             "nyion_attn_softmax_padic": (i32, [vp, vp, i32, f32, vp]),
             "mojo_softmax_padic": (None, [vp, vp, C.c_int, f32]),
+            "nyion_attn_exp_q16_16": (i32, [vp, vp, i64, vp]),
             "mojo_stokes_init": (vp, [C.c_int]),
             "mojo_stokes_append": (None, [vp, C.c_int, vp, vp, f32]),
             "mojo_stokes_free": (None, [vp]),
@@ -575,6 +576,16 @@ def decode_q4_splitkv(q, kv_pool, page_table, u_begin: int, u_end: int, mailboxe
         _ptr(q), _ptr(kv_pool), kv_pool.shape[0], _ptr(page_table), page_table.shape[1], u_begin, u_end, _ptr(out),
         B, H, kv_pool.shape[1], D, kv_pool.shape[3], float(scale), arr, world, rank, timeout_ms, ws_ptr, ws_bytes,
         _stream_ptr(stream)))
+    return out
+
+
+def exp_q16_16(x_fixed, out=None, stream=None):
+    """exp_q16_16 of a device int32 vector (nyion_attn_exp_q16_16)."""
+    import torch
+    assert x_fixed.is_cuda and x_fixed.dtype == torch.int32 and x_fixed.is_contiguous()
+    if out is None:
+        out = torch.empty_like(x_fixed)
+    check(lib().nyion_attn_exp_q16_16(_ptr(x_fixed), _ptr(out), x_fixed.numel(), _stream_ptr(stream)))
     return out
 
 

@@ -730,6 +730,10 @@ int32_t or_exp_q16_16(int32_t x_fixed) {         /* lib.rs:97-103 */
     return (int32_t)r;
 }
 
+void or_exp_q16_16_many(const int32_t* x_fixed, int32_t* out, int64_t n) {
+    for (int64_t i = 0; i < n; i++) out[i] = or_exp_q16_16(x_fixed[i]);
+}
+
 static int32_t sat_f32_to_i32(float x) {          /* Rust `as i32` */
     if (x != x) return 0;
     if (x >= 2147483648.0f) return 2147483647;
@@ -933,6 +937,38 @@ static void run_items(job_t* j) {
             if (j->kind == 2) { out_row[hd] = -INFINITY; out_row[hd + 1] = 0.0f; }
             continue;
         }
+        if (j->kind == 2) {
+            /* partial over Q4 rows: the same per-head algorithm as attend_head
+             * (scores, max, serial exp sum, normalised AXPY), keeping (max,
+             * sum); each row is dequantized when it is used, so memory does
+             * not grow with the range (the values are the same either way) */
+            float* scores = (float*)malloc(sizeof(float) * (size_t)n);
+            float row[hd];
+            float mx = -INFINITY;
+            for (int64_t i = 0; i < n; i++) {
+                const uint8_t* pk = paged_row_q4((const uint8_t*)j->pool, j->page_table, j->max_pages, b, t0 + i,
+                                                 j->n_kv, kv_h, 0, j->pt, nblk);
+                or_q4_dequant_rows(pk, 1, hd, row);
+                float sc = or_dot_product_raw(qh, row, hd) * j->scale;
+                scores[i] = sc;
+                if (sc > mx) mx = sc;
+            }
+            float l = 0.0f;
+            for (int64_t i = 0; i < n; i++) { float e = expf(scores[i] - mx); scores[i] = e; l += e; }
+            float inv = 1.0f / l;
+            for (int64_t i = 0; i < n; i++) scores[i] *= inv;
+            memset(out_row, 0, sizeof(float) * (size_t)hd);
+            for (int64_t i = 0; i < n; i++) {
+                const uint8_t* pv = paged_row_q4((const uint8_t*)j->pool, j->page_table, j->max_pages, b, t0 + i,
+                                                 j->n_kv, kv_h, 1, j->pt, nblk);
+                or_q4_dequant_rows(pv, 1, hd, row);
+                or_weighted_sum_raw(out_row, row, scores[i], hd);
+            }
+            out_row[hd] = mx;
+            out_row[hd + 1] = l;
+            free(scores);
+            continue;
+        }
         const float** kr = (const float**)malloc(sizeof(float*) * (size_t)n);
         const float** vr = (const float**)malloc(sizeof(float*) * (size_t)n);
         float* deq = NULL;
@@ -956,25 +992,7 @@ static void run_items(job_t* j) {
             }
         }
         float* scores = (float*)malloc(sizeof(float) * (size_t)n);
-        if (j->kind == 2) {
-            /* partial: same per-head algorithm, keeping (max, sum) */
-            float mx = -INFINITY;
-            for (int64_t i = 0; i < n; i++) {
-                float s = or_dot_product_raw(qh, kr[i], hd) * j->scale;
-                scores[i] = s;
-                if (s > mx) mx = s;
-            }
-            float l = 0.0f;
-            for (int64_t i = 0; i < n; i++) { float e = expf(scores[i] - mx); scores[i] = e; l += e; }
-            float inv = 1.0f / l;
-            for (int64_t i = 0; i < n; i++) scores[i] *= inv;
-            memset(out_row, 0, sizeof(float) * (size_t)hd);
-            for (int64_t i = 0; i < n; i++) or_weighted_sum_raw(out_row, vr[i], scores[i], hd);
-            out_row[hd] = mx;
-            out_row[hd + 1] = l;
-        } else {
-            attend_head(out_row, qh, kr, vr, n, hd, j->scale, scores, NULL, NULL);
-        }
+        attend_head(out_row, qh, kr, vr, n, hd, j->scale, scores, NULL, NULL);
         free(scores);
         free(deq);
         free(kr);

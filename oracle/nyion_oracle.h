@@ -107,6 +107,7 @@ void or_gemv_q4k(const uint8_t* w, const float* x, float* out, int n_rows, int n
 
 /* ---- Q16.16 softmax (swamp-kernels/src/lib.rs:97-223) ---- */
 int32_t or_exp_q16_16(int32_t x_fixed);
+void    or_exp_q16_16_many(const int32_t* x_fixed, int32_t* out, int64_t n);
 void    or_softmax_padic(const float* logits, float* probs, int n, float temperature);
 
 /* ---- Stokes KV store (swamp-kernels/src/lib.rs:27-85) ---- */

@@ -62,6 +62,7 @@ def lib():
             "or_attention_sparse_q4": (None, [f32p, f32p, C.c_void_p, C.c_void_p, i32, i32, i64, i64, i32, i32, i32, i64, i64, i32]),
             "or_sparse_positions": (i64, [i64, i64, i64, i64, i64p, i64]),
             "or_exp_q16_16": (C.c_int32, [C.c_int32]),
+            "or_exp_q16_16_many": (None, [i32p, i32p, i64]),
             "or_rope_lut": (None, [f32p, i32, i64]),
             "or_gemv_q4k": (None, [u8p, f32p, f32p, i32, i32]),
             "or_mojo_sparse_attention_q4": (None, [f32p, f32p, f32p, i32p, f32p, i32, i32, i32]),
@@ -314,6 +315,13 @@ def mojo_rows_from_q4(rows_u8: np.ndarray) -> np.ndarray:
 # ---------------------------------------------------------------- softmax / stokes
 def exp_q16_16(x: int) -> int:
     return int(lib().or_exp_q16_16(int(x)))
+
+
+def exp_q16_16_many(x: np.ndarray) -> np.ndarray:
+    x = _c(x, np.int32)
+    out = np.zeros_like(x)
+    lib().or_exp_q16_16_many(x, out, x.size)
+    return out
 
 
 def softmax_padic(logits: np.ndarray, temperature: float = 1.0) -> np.ndarray:

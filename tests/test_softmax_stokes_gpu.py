@@ -22,6 +22,31 @@ def test_softmax_padic_bit_exact(cuda_device, n, T, scale):
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
 
 
+def test_exp_q16_16_whole_domain_bit_exact(cuda_device):
+    """Every input of exp_q16_16 that is neither clamped to 0 (below -655360)
+    nor to 65536 (>= 0), plus both clamps and the i32 extremes: the device
+    function equals the oracle (glibc expf, as Rust's f32::exp) bit for bit."""
+    x = np.concatenate([np.arange(-655362, 3, dtype=np.int32),
+                        np.array([-(2 ** 31), 2 ** 31 - 1, -(2 ** 20), 1 << 20], np.int32)])
+    want = O.exp_q16_16_many(x)
+    got = A.exp_q16_16(torch.from_numpy(x).to(cuda_device)).cpu().numpy()
+    bad = np.nonzero(got != want)[0]
+    assert bad.size == 0, f"{bad.size} mismatches, first x = {x[bad[:5]]}"
+    assert want[x == 0][0] == 65536 and want[x == -655361][0] == 0
+
+
+@pytest.mark.parametrize("seed", [0, 1])
+def test_softmax_padic_normalisation_small_n(cuda_device, seed):
+    """Normalisation for every length 1..64 (both sides of the 16-wide block
+    boundary and the tail rule), bit-exact."""
+    rng = np.random.default_rng(100 + seed)
+    for n in range(1, 65):
+        x = (rng.standard_normal(n) * (1 + 4 * seed)).astype(np.float32)
+        want = O.softmax_padic(x, 1.0)
+        got = A.softmax_padic(torch.from_numpy(x).to(cuda_device), 1.0).cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), n
+
+
 def test_softmax_padic_extremes_and_host_abi(cuda_device):
     x = np.array([0.0, -1e30, 1e30, float("nan"), -5.0, 40000.0, -40000.0] * 5, np.float32)
     want = O.softmax_padic(x, 1.0)
