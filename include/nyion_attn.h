@@ -153,8 +153,12 @@ int32_t nyion_attn_dequant_q4(const uint8_t* src, float* dst, int64_t n_rows, in
  *              scaled score, natural log units), l = sum exp(s - m); an empty
  *              range gives (0, -inf, 0).
  * This build: 32 query heads, 4 KV heads, head_dim 64, page_tokens 16.
- * workspace: nyion_attn_q4_workspace_size(batch) bytes, reset once, or NULL
- * for the library-owned one. */
+ * One launch per 512 sequences: the CTAs that share a sequence merge their
+ * partials in the same launch (the last to finish merges).
+ * workspace: nyion_attn_q4_workspace_size(batch) bytes whose leading merge
+ * counters are zero before the first call (nyion_attn_workspace_reset once;
+ * every call leaves them at zero), or NULL for the library-owned one.  Calls
+ * that share a workspace must not overlap on the GPU. */
 size_t nyion_attn_q4_workspace_size(int32_t batch);
 int32_t nyion_attn_decode_q4_partial(const float* q, const uint8_t* kv_pool, int64_t n_pool_pages,
                                      const int32_t* page_table, int32_t max_pages,
@@ -175,7 +179,7 @@ int32_t nyion_attn_lse_combine(const float* parts, int32_t n_parts, int64_t rows
  * (ring_tokens <= 128), the
  * older ones from the Q4 pages.  out [batch][n_heads][head_dim].
  * workspace: nyion_attn_q4_workspace_size(batch) + 2 * batch * n_heads *
- * (head_dim + 2) * 4 + 8 * batch bytes, or NULL. */
+ * (head_dim + 2) * 4 + 8 * batch bytes (reset once, as above), or NULL. */
 int32_t nyion_attn_decode_q4_window_ring(const float* q, const uint8_t* kv_pool,
                                          int64_t n_pool_pages, const int32_t* page_table,
                                          int32_t max_pages, const int32_t* seq_lens,
@@ -221,7 +225,8 @@ int32_t nyion_attn_decode_positions(const float* q, const void* kv_pool, int32_t
  * positions on the position kernel, which folds the window's log-sum-exp
  * partial into its own and writes `out` (two launches, plus one that turns
  * seq_lens into window ranges).  Nibbles in the writer's order (cache.rs:637-663).
- * workspace: nyion_attn_sparse_q4_workspace_size(batch, n_heads) or NULL. */
+ * workspace: nyion_attn_sparse_q4_workspace_size(batch, n_heads) bytes (the
+ * Q4 decode's merge counters first: reset once, left at zero), or NULL. */
 size_t nyion_attn_sparse_q4_workspace_size(int32_t batch, int32_t n_heads);
 int32_t nyion_attn_sparse_q4(const float* q, const uint8_t* kv_pool, int64_t n_pool_pages,
                              const int32_t* page_table, int32_t max_pages, const int32_t* seq_lens,
@@ -265,11 +270,13 @@ int32_t nyion_attn_decode_zoned_f32_tracked(float* out, const float* q, const fl
  * zeroed by nyion_attn_mailbox_alloc) and opens every other rank's through
  * CUDA IPC (nyion_attn_ipc_handle gives 64 bytes to send, nyion_attn_ipc_open
  * maps a received one).  nyion_attn_decode_q4_splitkv then runs the rank's
- * partial and, in the same reduce kernel, writes each (sequence, head) row's
- * partial into every rank's mailbox over peer memory as 64-bit words tagged
- * with the step's epoch, waits (at most timeout_ms; 0 = 2000) until all
- * ranks' words of the row carry it, and writes the combined attention to
- * `out` [batch][n_heads][head_dim] on every rank.
+ * decode and, in the same launch (the CTAs that merge a sequence's partials),
+ * writes each (sequence, head) row's partial into every rank's mailbox over
+ * peer memory as 64-bit words tagged with the step's epoch, waits (at most
+ * timeout_ms; 0 = 2000) until all ranks' words of the row carry it, and writes
+ * the combined attention to `out` [batch][n_heads][head_dim] on every rank.
+ * With world 1 the merged rows are written directly (no mailbox traffic).
+ * workspace: nyion_attn_q4_workspace_size(batch) bytes (reset once) or NULL.
  * `mailboxes` is a host array of `world` device pointers ([rank] = own).
  * All ranks must call it the same number of times with the same batch;
  * steps alternate two mailbox halves, so it is graph-replayable.  A wait that

@@ -522,7 +522,8 @@ extern "C" int32_t nyion_attn_sparse_q4(const float* q, const uint8_t* kv_pool, 
   if (st) return st;
   const size_t need = nyion_attn_sparse_q4_workspace_size(batch, n_heads);
   if (!workspace) {
-    st = internal_workspace(need, &workspace);
+    // the Q4 decode keeps its merge counters at the start of this buffer
+    st = internal_workspace(need, &workspace, kWsCounters, q4_counter_bytes(), static_cast<cudaStream_t>(stream));
     if (st) return st;
   } else if (workspace_bytes < need) {
     return fail(NYION_ERR_WORKSPACE, "sparse_q4: workspace %zu < %zu", workspace_bytes, need);

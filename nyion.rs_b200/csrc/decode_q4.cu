@@ -1,6 +1,7 @@
-// decode_q4.cu — the 4-bit KV path: block quantizer / dequantizer, Q4 paged
-// decode producing log-sum-exp partials, the fp32 ring partial, and the
-// partial combine.
+// decode_q4.cu — the 4-bit KV path: block quantizer / dequantizer, the Q4
+// paged decode with its split-KV merge (and, across GPUs, the exchange of the
+// ranks' partials) inside the same launch, the fp32 ring partial of config 3,
+// and the log-sum-exp partial combine.
 //
 // Block format (swamp-engine/src/cache.rs:637-663, 375-394): 32 values ->
 // 20 bytes [f16 d][f16 dmin][16 bytes of nibbles], element i in byte i/2,
@@ -15,11 +16,33 @@
 // accumulate; q split into fp16 hi + lo rows) and the rest a per-score fix-up.
 // P.V uses the same identity: v = 16 d (1 + n/16) + (dmin - 16 d), so
 // o = sum_t (16 p_t d_t) v'_t  +  sum_t p_t (dmin_t - 16 d_t) per block.
-// Only the nibbles of V are staged again in shared memory, as a swizzled fp16
-// tile for ldmatrix.trans; K nibbles go straight from a 4-byte load into the
-// B fragments.  The dims inside a 32-value block are visited in a fixed
+// Only the nibbles of V are staged again in shared memory, as an fp16 tile for
+// ldmatrix.trans; K nibbles go straight from a 4-byte load into the B
+// fragments.  The dims inside a 32-value block are visited in a fixed
 // permutation (pairs (0,4), (1,5), (2,6), (3,7) of each 8-value group) that q
 // and the output share.
+//
+// Work split: the (sequence, 64-token chunk) units of a call are flattened
+// and cut into equal contiguous ranges, one persistent CTA per SM.  A CTA
+// has one producer warp (whole 5 KB pages by bulk copy into a 4-stage ring)
+// and 16 consumer warps in two groups that take alternate stages (stage s
+// always goes to group s % 2); within a group, warp = (KV head, 32-token
+// half of the chunk) computes its tokens for the 8 query heads of its KV
+// head.  Every shared-memory access of the chunk loop is a per-lane base plus
+// a constant: the V tile and the per-token factor table are padded (144- and
+// 48-byte rows) instead of swizzled, which keeps ldmatrix and the 16-byte
+// stores free of bank conflicts.
+//
+// Merge: at the end of a sequence's chunks the 4 warps of each KV head fold
+// their partials in shared memory and the CTA writes one partial per
+// (sequence, query head).  A sequence covered by several CTAs is merged in the
+// same launch by the last CTA to finish: CTAs count in per group of about
+// sqrt(n) CTAs (acq_rel atomic after a CTA barrier, no waiting), the last of
+// a group merges the group's partials, and the last group to finish merges
+// the group partials and writes the result — the (o/l, m, l) partial, the
+// output, or, across GPUs, this rank's rows sent to every rank's mailbox
+// over peer memory, the other ranks' rows awaited (bounded wait) and the
+// combined output written.  One launch per call.
 #include <cuda_fp16.h>
 #include <math.h>
 
@@ -42,12 +65,6 @@ constexpr int PAGE_KV = 2 * PAGE * ROWB;      // 1280 B: K rows then V rows of o
 constexpr int PAGE_BYTES = NKV * PAGE_KV;     // 5120 B: one whole page
 constexpr int CHUNK = 64;               // tokens per stage (4 pages)
 constexpr int STAGE_BYTES = 4 * PAGE_BYTES;   // 20 KB
-constexpr int STAGES = 3;                // x 2 CTAs per SM
-constexpr int NC = 8;                   // consumer warps: 4 KV heads x 2 token halves
-constexpr int THREADS = (NC + 1) * 32;
-constexpr int MAX_SEQS = 512;
-constexpr int MAX_GRID = 1024;
-constexpr int RING = 32;
 
 // ============================================================================
 // quantizer / dequantizer (bit-exact with cache.rs)
@@ -117,8 +134,65 @@ __global__ void dequant_kernel(const uint8_t* __restrict__ src, float* __restric
 }
 
 // ============================================================================
-// Q4 paged decode -> log-sum-exp partials
+// Q4 paged decode with the split-KV merge (and the rank exchange) in-launch
 // ============================================================================
+
+constexpr int STAGES = 4;               // 20 KB each
+constexpr int GROUPS = 2;               // consumer groups: stage s is consumed by group s % GROUPS
+constexpr int NCW = GROUPS * NKV * 2;   // 16 consumer warps: group x KV head x 32-token half
+constexpr int NCT = NCW * 32;           // 512 consumer threads
+constexpr int THREADS = NCT + 32;       // + the producer warp
+constexpr int MAX_SEQS = 512;
+constexpr int MAX_GRID = 1024;
+constexpr int RING = 32;                // chunks whose page ids the producer stages ahead
+constexpr int VT_STRIDE = 144;          // bytes per token row of a warp's fp16 V tile (128 + 16)
+constexpr int HT_STRIDE = 48;           // bytes per token of a warp's factor table (32 + 16)
+constexpr int ROWS = NKV * GROUP;       // query heads of a sequence
+constexpr int CP = HD + 4;              // floats per row of a CTA partial: o[64], m, l, 2 unused
+static_assert(STAGES % GROUPS == 0, "a stage must always be consumed by the same warps");
+static_assert(STAGES == 4, "the stage and phase arithmetic of the chunk loops assumes 4 stages");
+static_assert(NCT == ROWS * 16, "merge mapping: 16 threads per query head, 4 dims each");
+
+enum : int32_t { kModePart = 0, kModeFinal = 1, kModeExchange = 2, kModeRing = 3 };
+
+// ---- split-KV exchange over peer memory ----------------------------------
+// Every rank owns a mailbox with the same layout.  A rank writes its partial
+// of row r into slot [rank] of EVERY rank's mailbox (stores over NVLink) as
+// 64-bit words: value bits low, the step's epoch high.  An aligned 64-bit
+// store is single-copy atomic, so a reader that sees the epoch in a word sees
+// its value: no fence and no separate flag (the scheme of NCCL's LL
+// protocol).  A reader polls its row's words of every rank until all carry
+// the epoch, then combines.  Each row's epoch is a counter kept in this
+// rank's own mailbox header; buf = epoch & 1 double-buffers consecutive
+// steps: a rank writes step s+1 only after reading every rank's step-s words,
+// and every rank has read step s-1 before it writes step s.
+constexpr int MAX_RANKS = 8;
+struct Exchange {
+  uint8_t* mbox[MAX_RANKS];   // mailbox of rank r ([rank] = this rank's own)
+  int32_t world, rank, rows;  // world 0: no exchange
+  long long timeout_ns;       // bound on the wait for the other ranks
+};
+__host__ __device__ constexpr size_t mbox_data_off(int rows) {
+  return (size_t(rows) * 4 + 255) & ~size_t(255);          // after the per-row epochs
+}
+__host__ __device__ constexpr size_t mbox_bytes(int rows) {
+  return mbox_data_off(rows) + size_t(2) * MAX_RANKS * rows * (HD + 2) * 8;
+}
+
+__device__ __forceinline__ void st_word(uint64_t* p, float v, uint32_t epoch) {
+  const uint64_t w = ((uint64_t)epoch << 32) | __float_as_uint(v);
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_word(const uint64_t* p) {
+  uint64_t w;
+  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
 
 struct Params {
   const float* q;              // [batch][H][HD]
@@ -132,23 +206,29 @@ struct Params {
   int32_t batch, max_pages;
   int64_t n_pool_pages;
   float qscale;                // scale * log2(e)
-  float* part;                 // [batch][H][HD + 2] result of the reduce: o / l, m (natural log), l
-  float* cta_part;             // [MAX_GRID + batch][NKV][GROUP][HD + 2]: o (relative to m), m (log2), l
-  int32_t* meta;               // [batch][2]: first and last CTA covering sequence b
+  int32_t mode;                // kModePart / Final / Exchange / Ring
+  float* part;                 // kModePart: [batch][H][HD + 2] (o / l, m natural log, l)
+  float* out;                  // kModeFinal, kModeExchange: [batch][H][HD]
+  float* cta_part;             // [MAX_GRID + batch][ROWS][CP]: o (relative to m), m (log2), l
+  int32_t* gcnt;               // [MAX_GRID + MAX_SEQS] group counters (zero between calls)
+  int32_t* scnt;               // [MAX_SEQS] sequence counters (zero between calls)
+  int32_t* meta;               // kModeRing: [batch][2] first and last CTA covering sequence b
   int32_t* err;
+  Exchange ex;
 };
 
 struct Smem {
   uint8_t kv[STAGES][STAGE_BYTES];
-  uint8_t vt[NC][32 * 128];          // per warp: V chunk as fp16 [32 tokens][64], swizzled
-  float hdr[NC][32][8];              // per warp and token: K factors | V factors, halves swapped for
-                                     // tokens with bit 2 set (conflict-free 16-byte accesses)
+  uint8_t vt[NCW][32 * VT_STRIDE];   // per warp: V chunk as fp16 [32 tokens][64] (row padded)
+  uint8_t ht[NCW][32 * HT_STRIDE];   // per warp and token: K factors | V factors (row padded)
   uint64_t full[STAGES], empty[STAGES];
+  int32_t vmask[STAGES];             // bit pg: page pg of the stage was copied
   int32_t prefix[MAX_SEQS + 1];      // flat chunk index where sequence b starts
   int32_t c0[MAX_SEQS];              // first chunk (absolute, in 64-token units) of sequence b
   int32_t beg[MAX_SEQS], end[MAX_SEQS];
-  int32_t rows[2][RING][5];          // per chunk: 4 page ids (or -1) and the sequence index
+  int32_t rows[2][RING][5];          // per chunk: 4 page ids (or -1 / -2) and the sequence index
   int32_t warp_tot[THREADS / 32];
+  int32_t flag;
   int32_t abort_;
 };
 
@@ -188,12 +268,9 @@ __device__ __forceinline__ void rows_finish(Smem& s, const Params& p, const RowJ
 #pragma unroll
   for (int pg = 0; pg < 4; ++pg) {
     int32_t v = j.page[pg];
-    if (v == -1 || (v >= 0 && v >= p.n_pool_pages)) {
+    if (v == -1 || v < -2 || (v >= 0 && v >= p.n_pool_pages)) {
       record_error(p.err, kErrPageRange);
-      v = -2;    // skipped: the stage slot keeps stale bytes, all its tokens are masked out
-    } else if (v < -2) {
-      record_error(p.err, kErrPageRange);
-      v = -2;
+      v = -2;    // not copied: the page's tokens are masked out by the consumers
     }
     s.rows[slot][lane][pg] = v;
   }
@@ -212,56 +289,174 @@ __device__ __forceinline__ float2 hdr2f(uint32_t w) {   // (d, dmin) of a block 
                      __half2float(__ushort_as_half((unsigned short)(w >> 16))));
 }
 
-__device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
-  uint32_t v;
-  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
-  return v;
-}
-
-__device__ __forceinline__ float4 lds_f4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
-  return v;
-}
-
-__device__ __forceinline__ void sts_f4(uint32_t addr, float4 v) {
-  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
-               : "memory");
-}
-
-__device__ __forceinline__ void sts_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
-               : "memory");
-}
-
 // dim visited at position c (0..63) of a row: pairs (0,4),(1,5),(2,6),(3,7) per 8-group
 __device__ __forceinline__ int perm_dim(int c) {
   const int base = c & ~7, e = c & 7;
   return base + ((e & 1) ? 4 : 0) + (e >> 1);
 }
 
-__device__ __forceinline__ void named_sync() {
-  asm volatile("bar.sync 1, %0;" ::"n"(NC * 32) : "memory");
+__device__ __forceinline__ void consumer_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(NCT) : "memory");
 }
 
-__global__ void __launch_bounds__(THREADS, 2) decode_q4_kernel(const Params p) {
-  extern __shared__ uint8_t smem_raw[];
-  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
-                                     ~uintptr_t(127));
+__device__ __forceinline__ int atom_add_acq_rel(int32_t* p, int v) {
+  int old;
+  asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+// byte offset of n-tile nt's token (8 nt + g) row, relative to token g's row of
+// the warp's first page
+__device__ __forceinline__ constexpr int nt_off(int nt) { return (nt >> 1) * PAGE_BYTES + (nt & 1) * 8 * ROWB; }
+
+// Merge of n partials at slots first, first + stride, ... for this thread's
+// (query head r, dims d4 .. d4 + 3): o relative to M (log2), L.
+__device__ __forceinline__ void merge_slots(const Params& p, int first, int stride, int n, int r, int d4,
+                                            float4& O, float& M, float& L) {
+  M = -INFINITY;
+  L = 0.f;
+  O = make_float4(0.f, 0.f, 0.f, 0.f);
+  constexpr int U = 8;
+  for (int j0 = 0; j0 < n; j0 += U) {
+    float2 ml[U];
+    float4 ov[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (j0 + u < n) {
+        const float* src = p.cta_part + ((int64_t)(first + (j0 + u) * stride) * ROWS + r) * CP;
+        ml[u] = __ldcg(reinterpret_cast<const float2*>(src + HD));
+        ov[u] = __ldcg(reinterpret_cast<const float4*>(src + d4));
+      } else {
+        ml[u] = make_float2(-INFINITY, 0.f);
+        ov[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (!(ml[u].y > 0.f)) continue;
+      const float Mn = fmaxf(M, ml[u].x);
+      const float sa = exp2f(M - Mn), sb = exp2f(ml[u].x - Mn);
+      L = L * sa + ml[u].y * sb;
+      O.x = O.x * sa + ov[u].x * sb;
+      O.y = O.y * sa + ov[u].y * sb;
+      O.z = O.z * sa + ov[u].z * sb;
+      O.w = O.w * sa + ov[u].w * sb;
+      M = Mn;
+    }
+  }
+}
+
+__device__ __forceinline__ void store_slot(const Params& p, int slot, int r, int d4, float4 O, float M, float L) {
+  float* dst = p.cta_part + ((int64_t)slot * ROWS + r) * CP;
+  __stcg(reinterpret_cast<float4*>(dst + d4), O);
+  if (d4 == 0) __stcg(reinterpret_cast<float2*>(dst + HD), make_float2(M, L));
+}
+
+// The result of sequence b for this thread's (query head r, dims d4 .. d4+3)
+// from its merged (O relative to M in log2 units, L): the partial, the
+// output, or the exchange with the other ranks and the combined output.
+__device__ void finish_row(const Params& p, int b, int r, int d4, float4 O, float M, float L) {
+  const float inv = L > 0.f ? 1.0f / L : 0.f;
+  const float4 o = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
+  const float mnat = L > 0.f ? M * 0.6931471805599453f : -INFINITY;   // log2 -> natural units
+  const int64_t row = (int64_t)b * ROWS + r;
+  if (p.mode == kModePart) {
+    float* dst = p.part + row * (HD + 2);
+    dst[d4] = o.x;
+    dst[d4 + 1] = o.y;
+    dst[d4 + 2] = o.z;
+    dst[d4 + 3] = o.w;
+    if (d4 == 0) {
+      dst[HD] = mnat;
+      dst[HD + 1] = L;
+    }
+    return;
+  }
+  if (p.mode == kModeFinal) {
+    *reinterpret_cast<float4*>(p.out + row * HD + d4) = o;
+    return;
+  }
+  // ---- exchange: this rank's row to every rank, then the ranks' rows combined ----
+  const Exchange& ex = p.ex;
+  int* epochs = reinterpret_cast<int*>(ex.mbox[ex.rank]);     // [rows] steps done per row
+  const uint32_t epoch = (uint32_t)(*reinterpret_cast<volatile int*>(epochs + row)) + 1u;
+  __syncwarp();   // every lane has read the epoch before any lane can update it
+  const int buf = epoch & 1;
+  const size_t slot = ((size_t)(buf * MAX_RANKS + ex.rank) * ex.rows + row) * (HD + 2);
+  for (int rk = 0; rk < ex.world; ++rk) {
+    uint64_t* dst = reinterpret_cast<uint64_t*>(ex.mbox[rk] + mbox_data_off(ex.rows)) + slot;
+    st_word(dst + d4, o.x, epoch);
+    st_word(dst + d4 + 1, o.y, epoch);
+    st_word(dst + d4 + 2, o.z, epoch);
+    st_word(dst + d4 + 3, o.w, epoch);
+    if (d4 == 0) {
+      st_word(dst + HD, mnat, epoch);
+      st_word(dst + HD + 1, L, epoch);
+    }
+  }
+  const uint64_t* box = reinterpret_cast<const uint64_t*>(ex.mbox[ex.rank] + mbox_data_off(ex.rows));
+  bool ok = true;
+  const unsigned long long t0 = global_ns();
+  float Mr = -INFINITY, den = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int rk = 0; rk < ex.world && ok; ++rk) {
+    const uint64_t* src = box + ((size_t)(buf * MAX_RANKS + rk) * ex.rows + row) * (HD + 2);
+    uint32_t spins = 0;
+    uint64_t w[6];
+    while (true) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) w[i] = ld_word(src + d4 + i);
+      w[4] = ld_word(src + HD);
+      w[5] = ld_word(src + HD + 1);
+      bool here = true;
+#pragma unroll
+      for (int i = 0; i < 6; ++i) here &= (uint32_t)(w[i] >> 32) == epoch;
+      if (here) break;
+      if (++spins > 32) __nanosleep(64);
+      if ((long long)(global_ns() - t0) > ex.timeout_ns) {
+        ok = false;
+        break;
+      }
+    }
+    if (!ok) break;
+    const float mr = __uint_as_float((uint32_t)w[4]), lr = __uint_as_float((uint32_t)w[5]);
+    if (!(lr > 0.f)) continue;
+    const float Mn = fmaxf(Mr, mr);
+    const float sa = expf(Mr - Mn), sb = lr * expf(mr - Mn);
+    den = den * sa + sb;
+    acc.x = acc.x * sa + __uint_as_float((uint32_t)w[0]) * sb;
+    acc.y = acc.y * sa + __uint_as_float((uint32_t)w[1]) * sb;
+    acc.z = acc.z * sa + __uint_as_float((uint32_t)w[2]) * sb;
+    acc.w = acc.w * sa + __uint_as_float((uint32_t)w[3]) * sb;
+    Mr = Mn;
+  }
+  if (!ok) record_error(p.err, kErrWaitTimeout);
+  const float ir = den > 0.f ? 1.0f / den : 0.f;
+  *reinterpret_cast<float4*>(p.out + row * HD + d4) = make_float4(acc.x * ir, acc.y * ir, acc.z * ir, acc.w * ir);
+  __syncwarp();
+  if (d4 == 0) *reinterpret_cast<volatile int*>(epochs + row) = (int)epoch;
+}
+
+__global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_constant__ Params p) {
+  // every access needs 16-byte alignment at most (bulk copies, ldmatrix, 16-byte
+  // stores, mbarriers): the dynamic shared window provides it, and using the
+  // array directly keeps the shared state space visible to the compiler
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  Smem& s = *reinterpret_cast<Smem*>(smem_raw);
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  const int H = NKV * GROUP;
+  const int H = ROWS;
 
   if (t == 0) {
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&s.full[i], 1);
-      mbar_init(&s.empty[i], NC);
+      mbar_init(&s.empty[i], NKV * 2);
     }
     s.abort_ = 0;
     fence_barrier_init();
   }
   // programmatic dependent launch: nothing global is read before the previous grid
-  // in the stream completed, and the next grid (the ring partial or the reduce) is
-  // released only after that, so it may read this kernel's inputs without waiting
+  // in the stream completed; the next grid may be scheduled from here on and
+  // waits for this one the same way
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   for (int b = t; b < p.batch; b += THREADS) {
@@ -282,38 +477,29 @@ __global__ void __launch_bounds__(THREADS, 2) decode_q4_kernel(const Params p) {
     s.c0[b] = lo / CHUNK;
   }
   __syncthreads();
-  constexpr int PER = (MAX_SEQS + THREADS - 1) / THREADS;
-  int local[PER];
-  int run = 0;
-#pragma unroll
-  for (int j = 0; j < PER; ++j) {
-    const int b = t * PER + j;
+  {
+    // exclusive prefix of the chunk counts: thread t owns sequence t
+    static_assert(THREADS >= MAX_SEQS + 1, "one thread per sequence in the prefix scan");
+    const int b = t;
     int c = 0;
     if (b < p.batch && s.end[b] > s.beg[b]) c = (s.end[b] + CHUNK - 1) / CHUNK - s.c0[b];
-    local[j] = run;
-    run += c;
-  }
-  int incl = run;
+    int incl = c;
 #pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int v = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += v;
-  }
-  if (lane == 31) s.warp_tot[warp] = incl;
-  __syncthreads();
-  int woff = 0;
-  for (int w = 0; w < warp; ++w) woff += s.warp_tot[w];
-  const int excl = woff + incl - run;
-#pragma unroll
-  for (int j = 0; j < PER; ++j) {
-    const int b = t * PER + j;
-    if (b <= p.batch) s.prefix[b] = excl + local[j];
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) s.warp_tot[warp] = incl;
+    __syncthreads();
+    int woff = 0;
+    for (int w = 0; w < warp; ++w) woff += s.warp_tot[w];
+    if (b <= p.batch) s.prefix[b] = woff + incl - c;
   }
   __syncthreads();
 
   const int total = s.prefix[p.batch];
   const int W = (total + gridDim.x - 1) / gridDim.x;
-  if (blockIdx.x == 0) {
+  if (p.mode == kModeRing && blockIdx.x == 0) {
     for (int b = t; b < p.batch; b += THREADS) {
       const int lo = s.prefix[b], hi = s.prefix[b + 1];
       p.meta[2 * b] = hi > lo ? lo / W : 0;
@@ -322,40 +508,46 @@ __global__ void __launch_bounds__(THREADS, 2) decode_q4_kernel(const Params p) {
   }
   const int begin = blockIdx.x * W;
   const int end = min(total, begin + W);
-  if (begin >= end) return;
-  const int n = end - begin;
 
-  if (warp == NC) {
+  if (warp == NCW) {
     // ================= producer warp: whole pages by bulk copy =================
+    if (begin >= end) return;
+    const int n = end - begin;
     RowJob job;
     rows_start(job, s, p, begin + lane, end);
     rows_finish(s, p, job, 0, lane);
     rows_start(job, s, p, begin + RING + lane, end);
     __syncwarp();
+    int stage = 0;
     for (int k = 0; k < n; ++k) {
-      const int stage = k % STAGES;
-      if (k % RING == RING / 2) {
+      if ((k & (RING - 1)) == RING / 2) {
         rows_finish(s, p, job, ((k / RING) + 1) & 1, lane);
         __syncwarp();
-      } else if (k % RING == 0 && k > 0) {
+      } else if ((k & (RING - 1)) == 0 && k > 0) {
         rows_start(job, s, p, begin + k + RING + lane, end);
       }
       bool ok = true;
-      if (k >= STAGES) ok = mbar_wait_bounded(&s.empty[stage], (uint32_t)(((k / STAGES) - 1) & 1));
+      if (k >= STAGES) ok = mbar_wait_bounded(&s.empty[stage], (uint32_t)(((k >> 2) - 1) & 1));
       if (!__all_sync(0xffffffffu, ok)) {
         record_error(p.err, kErrWaitTimeout);
         if (lane == 0) {
           atomicExch(&s.abort_, 1);
           for (int c = k - 1; c >= 0 && c >= k - STAGES; --c)
-            mbar_wait_bounded(&s.full[c % STAGES], (uint32_t)((c / STAGES) & 1));
+            mbar_wait_bounded(&s.full[c & 3], (uint32_t)((c >> 2) & 1));
         }
         return;
       }
       if (lane == 0) {
-        const int32_t* e = s.rows[(k / RING) & 1][k % RING];
+        const int32_t* e = s.rows[(k / RING) & 1][k & (RING - 1)];
         uint32_t bytes = 0;
+        int mask = 0;
 #pragma unroll
-        for (int pg = 0; pg < 4; ++pg) bytes += (e[pg] >= 0) ? PAGE_BYTES : 0;
+        for (int pg = 0; pg < 4; ++pg)
+          if (e[pg] >= 0) {
+            bytes += PAGE_BYTES;
+            mask |= 1 << pg;
+          }
+        s.vmask[stage] = mask;
         // an all-skipped chunk still completes the phase through the arrive itself
         mbar_arrive_expect_tx(&s.full[stage], bytes);
 #pragma unroll
@@ -365,32 +557,30 @@ __global__ void __launch_bounds__(THREADS, 2) decode_q4_kernel(const Params p) {
                       PAGE_BYTES, &s.full[stage]);
       }
       __syncwarp();
+      stage = (stage + 1) & (STAGES - 1);
     }
     return;
   }
 
   // ================= consumer warps =================
-  const int kvh = warp & 3, th = warp >> 2;
+  const int grp = warp >> 3, kvh = warp & 3, th = (warp >> 2) & 1;
   const int g = lane >> 2, tig = lane & 3;
-  const uint32_t vt = smem_u32(s.vt[warp]);
-  const uint32_t hd = smem_u32(s.hdr[warp]);
-  // ldmatrix.trans row addresses of the V tile for k-step kt, n-tile pair np:
-  // matrix m = lane>>3: tokens 16kt + 8(m&1) + (lane&7), 16-B chunk 2np + (m>>1)
-  uint32_t voff[2][4];
-#pragma unroll
-  for (int kt = 0; kt < 2; ++kt)
-#pragma unroll
-    for (int np = 0; np < 4; ++np) {
-      const uint32_t tok = 16 * kt + 8 * ((lane >> 3) & 1) + (lane & 7);
-      const uint32_t ch = 2 * np + (lane >> 4);
-      voff[kt][np] = tok * 128 + (((ch ^ tok) & 7) << 4);
-    }
+  const int woff = th * 2 * PAGE_BYTES + kvh * PAGE_KV;                        // the warp's 2 pages, its KV head
+  const int loff_v = (lane >> 4) * PAGE_BYTES + PAGE * ROWB + (lane & 15) * ROWB;   // V row of token `lane`
+  const int loff_k = g * ROWB + 4 + 4 * tig;                                  // K word tig of token g, block 0
+  uint8_t* const vtw = s.vt[warp] + lane * VT_STRIDE;
+  const uint32_t vtr = smem_u32(s.vt[warp]) + (8 * ((lane >> 3) & 1) + (lane & 7)) * VT_STRIDE + (lane >> 4) * 16;
+  uint8_t* const htw = s.ht[warp] + lane * HT_STRIDE;
+  const uint8_t* const htr = s.ht[warp] + 2 * tig * HT_STRIDE;
+  // merge mapping: thread -> query head r of the sequence, dims d4 .. d4 + 3
+  const int mr = t >> 4, md4 = (t & 15) * 4;
 
   int i = begin;
   while (i < end) {
     const int b = seek_seq(s, p.batch, i);
+    const int pb = s.prefix[b];
     const int seg_hi = min(end, s.prefix[b + 1]);
-    const int sb = s.beg[b], se = s.end[b];
+    const int sb = s.beg[b], se = s.end[b], c0b = s.c0[b];
     // q fragments, dims permuted: k-step (blk, ks) pairs dims 32blk + 8tig + {ks*2 + (0,4)} in
     // a0/a1 and {ks*2 + (1,5)} in a2/a3, hi rows 0-7 and lo rows 8-15
     uint32_t qa[2][2][4];
@@ -429,79 +619,81 @@ __global__ void __launch_bounds__(THREADS, 2) decode_q4_kernel(const Params p) {
     float cb[2] = {0.f, 0.f};   // sum_t p_t (dmin - 16 d) per V block (this thread's tokens)
     float m = -INFINITY, l = 0.f;
 
-    for (int k = i - begin; k < seg_hi - begin; ++k) {
-      const int stage = k % STAGES;
-      const int chunk = s.c0[b] + (begin + k - s.prefix[b]);
-      const int pos0 = chunk * CHUNK + 32 * th;       // absolute position of this warp's token 0
+    int k = i - begin;
+    k += (k & 1) ^ grp;         // this group's chunks: k = grp (mod 2)
+    for (; k < seg_hi - begin; k += 2) {
+      const int stage = k & (STAGES - 1);
       if (!s.abort_) {
-        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&s.full[stage], (uint32_t)((k / STAGES) & 1)))) {
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&s.full[stage], (uint32_t)((k >> 2) & 1)))) {
           record_error(p.err, kErrWaitTimeout);
           if (lane == 0) atomicExch(&s.abort_, 1);
         }
       }
-      const bool any = (pos0 < se) && (pos0 + 32 > sb);
-      const bool inner = (pos0 >= sb) && (pos0 + 32 <= se);   // no token of this warp is masked
+      const int chunk = c0b + (begin + k - pb);
+      const int pos0 = chunk * CHUNK + 32 * th;       // absolute position of this warp's token 0
+      const int vm = (s.vmask[stage] >> (2 * th)) & 3;  // this warp's two pages were copied
+      const bool any = vm != 0 && (pos0 < se) && (pos0 + 32 > sb);
+      const bool inner = vm == 3 && (pos0 >= sb) && (pos0 + 32 <= se);   // no token of this warp is masked
       if (any) {
-        const uint32_t kb = smem_u32(s.kv[stage]) + 2 * th * PAGE_BYTES + kvh * PAGE_KV;
-        // token t of this warp: page 2th + t/16 (offset (t/16)*PAGE_BYTES), row t%16
-        // ---- V nibbles of token `lane` -> fp16 tile row `lane` ----
+        const uint8_t* const kb = s.kv[stage] + woff;
+        // ---- V nibbles of token `lane` -> fp16 tile row `lane`; its block factors ----
         {
-          const uint32_t vr = kb + (lane >> 4) * PAGE_BYTES + PAGE * ROWB + (lane & 15) * ROWB;
+          const uint8_t* const vr = kb + loff_v;
 #pragma unroll
           for (int blk = 0; blk < 2; ++blk)
 #pragma unroll
             for (int wq = 0; wq < 4; ++wq) {
-              const uint32_t w = lds_u32(vr + blk * BLK + 4 + 4 * wq);
-              const uint32_t ch = 4 * blk + wq;
-              sts_v4(vt + lane * 128 + (((ch ^ lane) & 7) << 4), nib2h<6>(w), nib2h<2>(w),
-                     nib2h<-2>(w), nib2h<-6>(w));
+              const uint32_t w = *reinterpret_cast<const uint32_t*>(vr + blk * BLK + 4 + 4 * wq);
+              *reinterpret_cast<uint4*>(vtw + (4 * blk + wq) * 16) =
+                  make_uint4(nib2h<6>(w), nib2h<2>(w), nib2h<-2>(w), nib2h<-6>(w));
             }
-          // block headers of token `lane` as the fp32 factors the score and P.V steps use:
+          // block factors of token `lane` as the fp32 values the score and P.V steps use:
           // score = sum_blk 16 d (q.(1 + n/16)) + (dmin - 16 d) qs; zero for masked tokens
-          const uint32_t kr = vr - PAGE * ROWB;
-          const float2 k0 = hdr2f(lds_u32(kr)), k1 = hdr2f(lds_u32(kr + BLK));
-          const float2 v0 = hdr2f(lds_u32(vr)), v1 = hdr2f(lds_u32(vr + BLK));
-          const bool live = inner || ((pos0 + lane >= sb) && (pos0 + lane < se));
+          const uint8_t* const kr = vr - PAGE * ROWB;
+          const float2 k0 = hdr2f(*reinterpret_cast<const uint32_t*>(kr));
+          const float2 k1 = hdr2f(*reinterpret_cast<const uint32_t*>(kr + BLK));
+          const float2 v0 = hdr2f(*reinterpret_cast<const uint32_t*>(vr));
+          const float2 v1 = hdr2f(*reinterpret_cast<const uint32_t*>(vr + BLK));
+          const bool live = inner || ((pos0 + lane >= sb) && (pos0 + lane < se) && ((vm >> (lane >> 4)) & 1));
           const float a0 = 16.0f * k0.x, a1 = 16.0f * k1.x, b0 = 16.0f * v0.x, b1 = 16.0f * v1.x;
           const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-          const uint32_t sw = ((lane >> 2) & 1) << 4;
-          sts_f4(hd + lane * 32 + sw, live ? make_float4(a0, k0.y - a0, a1, k1.y - a1) : zero);
-          sts_f4(hd + lane * 32 + (sw ^ 16), live ? make_float4(b0, v0.y - b0, b1, v1.y - b1) : zero);
+          *reinterpret_cast<float4*>(htw) = live ? make_float4(a0, k0.y - a0, a1, k1.y - a1) : zero;
+          *reinterpret_cast<float4*>(htw + 16) = live ? make_float4(b0, v0.y - b0, b1, v1.y - b1) : zero;
         }
-        __syncwarp();   // V tile rows and headers written by all lanes
-        // ---- S = Q K^T: 4 n-tiles of 8 tokens, 2 blocks x 2 k-steps ----
-        float sc[4][2][4];
-#pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
-          const int tk = 8 * nt + g;
-          const uint32_t kr = kb + (tk >> 4) * PAGE_BYTES + (tk & 15) * ROWB;
-#pragma unroll
-          for (int blk = 0; blk < 2; ++blk) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) sc[nt][blk][j] = 0.f;
-            const uint32_t w = lds_u32(kr + blk * BLK + 4 + 4 * tig);
-            mma_f16(sc[nt][blk], qa[blk][0], nib2h<6>(w), nib2h<2>(w));
-            mma_f16(sc[nt][blk], qa[blk][1], nib2h<-2>(w), nib2h<-6>(w));
-          }
-        }
+        __syncwarp();   // V tile rows and factors written by all lanes
+        // ---- S = Q K^T: 4 n-tiles of 8 tokens, 2 blocks x 2 k-steps; each
+        //      n-tile's scores are fixed up as soon as its MMAs are done ----
         float sv[4][2];
+        {
+          const uint8_t* const kq = kb + loff_k;
 #pragma unroll
-        for (int nt = 0; nt < 4; ++nt)
+          for (int nt = 0; nt < 4; ++nt) {
+            float sc[2][4];
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int tt = 8 * nt + 2 * tig + e;
-            const float4 h = lds_f4(hd + tt * 32 + (((tt >> 2) & 1) << 4));   // a0, c0, a1, c1
-            const float t0 = sc[nt][0][e] + sc[nt][0][2 + e];            // sum q (1 + n/16), hi + lo rows
-            const float t1 = sc[nt][1][e] + sc[nt][1][2 + e];
-            sv[nt][e] = fmaf(h.x, t0, fmaf(h.z, t1, fmaf(h.y, qs[0], h.w * qs[1])));
+            for (int blk = 0; blk < 2; ++blk) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) sc[blk][j] = 0.f;
+              const uint32_t w = *reinterpret_cast<const uint32_t*>(kq + nt_off(nt) + blk * BLK);
+              mma_f16(sc[blk], qa[blk][0], nib2h<6>(w), nib2h<2>(w));
+              mma_f16(sc[blk], qa[blk][1], nib2h<-2>(w), nib2h<-6>(w));
+            }
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              // token 8 nt + 2 tig + e: a0, c0, a1, c1
+              const float4 h = *reinterpret_cast<const float4*>(htr + (8 * nt + e) * HT_STRIDE);
+              const float t0 = sc[0][e] + sc[0][2 + e];            // sum q (1 + n/16), hi + lo rows
+              const float t1 = sc[1][e] + sc[1][2 + e];
+              sv[nt][e] = fmaf(h.x, t0, fmaf(h.z, t1, fmaf(h.y, qs[0], h.w * qs[1])));
+            }
           }
-        if (!inner) {   // the sequence range starts or ends inside this warp's 32 tokens
+        }
+        if (!inner) {   // the range starts or ends, or a page is missing, inside this warp's 32 tokens
 #pragma unroll
           for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
               const int pos = pos0 + 8 * nt + 2 * tig + e;
-              if (pos < sb || pos >= se) sv[nt][e] = -INFINITY;
+              if (pos < sb || pos >= se || !((vm >> (nt >> 1)) & 1)) sv[nt][e] = -INFINITY;
             }
         }
         // ---- online softmax ----
@@ -540,11 +732,10 @@ __global__ void __launch_bounds__(THREADS, 2) decode_q4_kernel(const Params p) {
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int nt = 2 * kt + (e >> 1);
-            const int tt = 8 * nt + 2 * tig + (e & 1);
             const float pe = sv[nt][e & 1];
             // 16 d_V and dmin_V - 16 d_V of both blocks (zero for masked tokens, whose
             // stage bytes may be stale)
-            const float4 h = lds_f4(hd + tt * 32 + ((((tt >> 2) & 1) ^ 1) << 4));
+            const float4 h = *reinterpret_cast<const float4*>(htr + (8 * nt + (e & 1)) * HT_STRIDE + 16);
             pv[0][e] = pe * h.x;
             pv[1][e] = pe * h.z;
             cb[0] = fmaf(pe, h.y, cb[0]);
@@ -562,7 +753,10 @@ __global__ void __launch_bounds__(THREADS, 2) decode_q4_kernel(const Params p) {
 #pragma unroll
           for (int np = 0; np < 4; ++np) {
             uint32_t b0, b1, b2, b3;
-            ldsm_x4_t(vt + voff[kt][np], b0, b1, b2, b3);
+            asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(b0), "=r"(b1), "=r"(b2), "=r"(b3)
+                         : "r"(vtr + kt * 16 * VT_STRIDE + np * 32)
+                         : "memory");
             const int blk = np >> 1;
             mma_f16(o[2 * np], pa[blk][kt], b0, b1);
             mma_f16(o[2 * np + 1], pa[blk][kt], b2, b3);
@@ -572,8 +766,8 @@ __global__ void __launch_bounds__(THREADS, 2) decode_q4_kernel(const Params p) {
       if (lane == 0) mbar_arrive(&s.empty[stage]);
     }
 
-    // ---- segment end: the two token halves of each KV head merge in shared
-    //      memory, one partial per (CTA, sequence, KV head) goes to the workspace ----
+    // ---- segment end: the 4 warps of each KV head (2 groups x 2 token halves)
+    //      fold their partials in shared memory into the CTA's partial ----
     l += __shfl_xor_sync(0xffffffffu, l, 1);
     l += __shfl_xor_sync(0xffffffffu, l, 2);
 #pragma unroll
@@ -581,52 +775,111 @@ __global__ void __launch_bounds__(THREADS, 2) decode_q4_kernel(const Params p) {
       cb[blk] += __shfl_xor_sync(0xffffffffu, cb[blk], 1);
       cb[blk] += __shfl_xor_sync(0xffffffffu, cb[blk], 2);
     }
-    named_sync();                       // every warp is done with its V tile
-    float* mine = reinterpret_cast<float*>(s.vt[warp]);   // [GROUP][HD + 2]
+    consumer_sync();                    // every warp is done with its V tile
+    {
+      float* mine = reinterpret_cast<float*>(s.vt[warp]);   // [GROUP][CP]
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
+      for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int c = 8 * nt + 2 * tig + e;
-        mine[g * (HD + 2) + perm_dim(c)] = o[nt][e] + o[nt][2 + e] + cb[nt >> 2];
-      }
-    if (tig == 0) {
-      mine[g * (HD + 2) + HD] = m;
-      mine[g * (HD + 2) + HD + 1] = l;
-    }
-    named_sync();
-    if (th == 0) {
-      // lane -> head lane>>2, dims 16*(lane&3) .. +15; partner warp holds the other half
-      const float* a0 = reinterpret_cast<const float*>(s.vt[warp]);
-      const float* a1 = reinterpret_cast<const float*>(s.vt[warp + 4]);
-      const int mh = lane >> 2, md = 16 * (lane & 3);
-      const float m0 = a0[mh * (HD + 2) + HD], l0 = a0[mh * (HD + 2) + HD + 1];
-      const float m1 = a1[mh * (HD + 2) + HD], l1 = a1[mh * (HD + 2) + HD + 1];
-      const float M = fmaxf(m0, m1);
-      const float w0 = (l0 > 0.f) ? exp2f(m0 - M) : 0.f, w1 = (l1 > 0.f) ? exp2f(m1 - M) : 0.f;
-      float* dst = p.cta_part + ((((int64_t)blockIdx.x + b) * NKV + kvh) * GROUP + mh) * (HD + 2);
-#pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        const float v0 = (l0 > 0.f) ? a0[mh * (HD + 2) + md + e] : 0.f;
-        const float v1 = (l1 > 0.f) ? a1[mh * (HD + 2) + md + e] : 0.f;
-        __stcg(dst + md + e, w0 * v0 + w1 * v1);
-      }
-      if ((lane & 3) == 0) {
-        __stcg(dst + HD, M);
-        __stcg(dst + HD + 1, w0 * l0 + w1 * l1);
+        for (int e = 0; e < 2; ++e) {
+          const int c = 8 * nt + 2 * tig + e;
+          mine[g * CP + perm_dim(c)] = o[nt][e] + o[nt][2 + e] + cb[nt >> 2];
+        }
+      if (tig == 0) {
+        mine[g * CP + HD] = m;
+        mine[g * CP + HD + 1] = l;
       }
     }
-    named_sync();                       // partner tiles are read before the next segment writes them
+    consumer_sync();
+    const int pe_ = s.prefix[b + 1];
+    const int first_b = pb / W, last_b = (pe_ - 1) / W, n_b = last_b - first_b + 1;
+    {
+      // thread -> (query head mr = KV head mr / 8, head mr % 8; dims md4 ..): the
+      // partials of warps kv, kv + 4, kv + 8, kv + 12
+      const int kv = mr >> 3, hh = mr & 7;
+      float ms[4], ls[4];
+      float4 os[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float* src = reinterpret_cast<const float*>(s.vt[kv + 4 * j]) + hh * CP;
+        ms[j] = src[HD];
+        ls[j] = src[HD + 1];
+        os[j] = *reinterpret_cast<const float4*>(src + md4);
+      }
+      float M = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (ls[j] > 0.f) M = fmaxf(M, ms[j]);
+      float L = 0.f;
+      float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (!(ls[j] > 0.f)) continue;
+        const float w = exp2f(ms[j] - M);
+        L = fmaf(w, ls[j], L);
+        O.x = fmaf(w, os[j].x, O.x);
+        O.y = fmaf(w, os[j].y, O.y);
+        O.z = fmaf(w, os[j].z, O.z);
+        O.w = fmaf(w, os[j].w, O.w);
+      }
+      if (n_b == 1 && p.mode != kModeRing) finish_row(p, b, mr, md4, O, M, L);   // this CTA alone
+      else store_slot(p, blockIdx.x + b, mr, md4, O, M, L);
+    }
+    consumer_sync();   // partials stored (and shared partials read) before the count-in
+    if (n_b > 1 && p.mode != kModeRing) {
+      // two-level count-in: groups of G consecutive CTAs, then the groups
+      const int G = n_b <= 16 ? n_b : (int)ceilf(sqrtf((float)n_b));
+      const int ngroups = (n_b + G - 1) / G;
+      const int gi = (blockIdx.x - first_b) / G;
+      const int gfirst = first_b + gi * G;
+      const int gsize = min(G, n_b - gi * G);
+      if (t == 0) {
+        const int old = atom_add_acq_rel(&p.gcnt[gfirst + b], 1);
+        const int last = old == gsize - 1;
+        if (last) atomicExch(&p.gcnt[gfirst + b], 0);
+        s.flag = last;
+      }
+      consumer_sync();
+      const int last = s.flag;
+      consumer_sync();
+      if (last) {
+        float4 O;
+        float M, L;
+        merge_slots(p, gfirst + b, 1, gsize, mr, md4, O, M, L);
+        if (ngroups == 1) {
+          finish_row(p, b, mr, md4, O, M, L);
+        } else {
+          store_slot(p, gfirst + b, mr, md4, O, M, L);
+          consumer_sync();
+          if (t == 0) {
+            const int old = atom_add_acq_rel(&p.scnt[b], 1);
+            const int last2 = old == ngroups - 1;
+            if (last2) atomicExch(&p.scnt[b], 0);
+            s.flag = last2;
+          }
+          consumer_sync();
+          const int last2 = s.flag;
+          consumer_sync();
+          if (last2) {
+            merge_slots(p, first_b + b, G, ngroups, mr, md4, O, M, L);
+            finish_row(p, b, mr, md4, O, M, L);
+          }
+        }
+      }
+    }
     i = seg_hi;
+  }
+  // sequences with nothing to attend: CTA 0 writes their (empty) results
+  if (blockIdx.x == 0 && p.mode != kModeRing) {
+    for (int b = 0; b < p.batch; ++b)
+      if (s.prefix[b + 1] == s.prefix[b])
+        finish_row(p, b, mr, md4, make_float4(0.f, 0.f, 0.f, 0.f), -INFINITY, 0.f);
   }
 }
 
 // ============================================================================
-// reduce of the per-CTA partials: one CTA per (sequence, query head) row
+// config 3: the fp32 ring tokens and the reduce of the decode's CTA partials
 // ============================================================================
-// 8 warps take the covering CTAs round-robin (lane = 2 dims, four partial
-// loads in flight), then warp 0 folds the 8 warp results.  Output is the
-// partial format (o/l, m natural, l) or, with `final_out`, o/l alone.
 struct RingArgs {
   const float* q;          // [batch][H][HD]
   const float* ring;       // [batch][NKV][K|V][ring_tokens][HD]
@@ -750,195 +1003,7 @@ __device__ int ring_partial_cta(const RingArgs& ra, int b, int kvh, RingSmem& sm
   return n;
 }
 
-// ---- split-KV exchange over peer memory ----------------------------------
-// Every rank owns a mailbox with the same layout.  A rank writes its partial
-// of row r into slot [rank] of EVERY rank's mailbox (stores over NVLink) as
-// 64-bit words: value bits low, the step's epoch high.  An aligned 64-bit
-// store is single-copy atomic, so a reader that sees the epoch in a word sees
-// its value: no fence and no separate flag (the scheme of NCCL's LL
-// protocol).  A reader polls its row's words of every rank until all carry
-// the epoch, then combines.  Each row's epoch is a counter kept by the row's
-// CTA in its own mailbox header; buf = epoch & 1 double-buffers consecutive
-// steps: a rank writes step s+1 only after reading every rank's step-s words,
-// and every rank has read step s-1 before it writes step s.
-constexpr int MAX_RANKS = 8;
-struct Exchange {
-  uint8_t* mbox[MAX_RANKS];   // mailbox of rank r ([rank] = this rank's own)
-  int32_t world, rank, rows;  // world 0: no exchange
-  long long timeout_ns;       // bound on the wait for the other ranks
-};
-__host__ __device__ constexpr size_t mbox_data_off(int rows) {
-  return (size_t(rows) * 4 + 255) & ~size_t(255);          // after the per-row epochs
-}
-__host__ __device__ constexpr size_t mbox_bytes(int rows) {
-  return mbox_data_off(rows) + size_t(2) * MAX_RANKS * rows * (HD + 2) * 8;
-}
-
-__device__ __forceinline__ void st_word(uint64_t* p, float v, uint32_t epoch) {
-  const uint64_t w = ((uint64_t)epoch << 32) | __float_as_uint(v);
-  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
-}
-__device__ __forceinline__ uint64_t ld_word(const uint64_t* p) {
-  uint64_t w;
-  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
-  return w;
-}
-__device__ __forceinline__ unsigned long long global_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
-
-// One CTA per (sequence, query head) row.  The covering CTAs' partials are
-// taken by the 8 warps round-robin with up to RU of them loaded before any is
-// folded (one L2 round trip for up to 8 RU CTAs); warp 0 combines.  Without an exchange the row is written as
-// the partial format (o/l, m natural, l) or, with `final_out`, o/l alone;
-// with an exchange it is sent to every rank and the ranks' partials of the
-// row are combined into `final_out`.
-constexpr int RU = 20;
-__global__ void __launch_bounds__(256) q4_reduce_kernel(const float* __restrict__ cta_part,
-                                                       const int32_t* __restrict__ meta, int batch,
-                                                       float* __restrict__ part,
-                                                       float* __restrict__ final_out,
-                                                       const __grid_constant__ Exchange ex, int32_t* err) {
-  __shared__ float red[8][HD + 2];
-  pdl_wait();
-  const int row = blockIdx.x;                 // b * 32 + h
-  const int b = row / (NKV * GROUP), h = row % (NKV * GROUP);
-  const int kvh = h / GROUP, hh = h % GROUP;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int cf = meta[2 * b], cl = meta[2 * b + 1];
-  float M = -INFINITY, L = 0.f, o0 = 0.f, o1 = 0.f;
-  for (int cbase = cf; cbase <= cl; cbase += 8 * RU) {
-    float2 ml[RU], ov[RU];
-#pragma unroll
-    for (int u = 0; u < RU; ++u) {
-      const int c = cbase + warp + 8 * u;
-      if (c <= cl) {
-        const float* src = cta_part + ((((int64_t)c + b) * NKV + kvh) * GROUP + hh) * (HD + 2);
-        ml[u] = __ldcg(reinterpret_cast<const float2*>(src + HD));
-        ov[u] = __ldcg(reinterpret_cast<const float2*>(src) + lane);
-      } else {
-        ml[u] = make_float2(-INFINITY, 0.f);
-        ov[u] = make_float2(0.f, 0.f);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < RU; ++u) {
-      if (!(ml[u].y > 0.f)) continue;
-      const float Mn = fmaxf(M, ml[u].x);
-      const float sa = exp2f(M - Mn), sb = exp2f(ml[u].x - Mn);
-      L = L * sa + ml[u].y * sb;
-      o0 = o0 * sa + ov[u].x * sb;
-      o1 = o1 * sa + ov[u].y * sb;
-      M = Mn;
-    }
-  }
-  red[warp][2 * lane] = o0;
-  red[warp][2 * lane + 1] = o1;
-  if (lane == 0) {
-    red[warp][HD] = M;
-    red[warp][HD + 1] = L;
-  }
-  constexpr int nparts = 8;
-  __syncthreads();
-  if (warp != 0) return;
-  float Mt = -INFINITY;
-  for (int w = 0; w < nparts; ++w)
-    if (red[w][HD + 1] > 0.f) Mt = fmaxf(Mt, red[w][HD]);
-  float den = 0.f, a0 = 0.f, a1 = 0.f;
-  for (int w = 0; w < nparts; ++w) {
-    if (!(red[w][HD + 1] > 0.f)) continue;
-    const float wt = exp2f(red[w][HD] - Mt);
-    den = fmaf(wt, red[w][HD + 1], den);
-    a0 = fmaf(wt, red[w][2 * lane], a0);
-    a1 = fmaf(wt, red[w][2 * lane + 1], a1);
-  }
-  const float inv = den > 0.f ? 1.0f / den : 0.f;
-  const float mnat = den > 0.f ? Mt * 0.6931471805599453f : -INFINITY;   // log2 -> natural units
-  if (ex.world == 0) {
-    if (final_out) {
-      final_out[(int64_t)row * HD + 2 * lane] = a0 * inv;
-      final_out[(int64_t)row * HD + 2 * lane + 1] = a1 * inv;
-    } else {
-      float* dst = part + (int64_t)row * (HD + 2);
-      dst[2 * lane] = a0 * inv;
-      dst[2 * lane + 1] = a1 * inv;
-      if (lane == 0) {
-        dst[HD] = mnat;
-        dst[HD + 1] = den;
-      }
-    }
-    return;
-  }
-
-  // ---- exchange: this rank's row partial to every rank, then combine ----
-  int* epochs = reinterpret_cast<int*>(ex.mbox[ex.rank]);     // [rows] steps done per row
-  uint32_t epoch = 0;
-  if (lane == 0) epoch = (uint32_t)(*reinterpret_cast<volatile int*>(epochs + row)) + 1u;
-  epoch = __shfl_sync(0xffffffffu, epoch, 0);
-  const int buf = epoch & 1;
-  const size_t slot = ((size_t)(buf * MAX_RANKS + ex.rank) * ex.rows + row) * (HD + 2);
-  for (int r = 0; r < ex.world; ++r) {
-    uint64_t* dst = reinterpret_cast<uint64_t*>(ex.mbox[r] + mbox_data_off(ex.rows)) + slot;
-    st_word(dst + 2 * lane, a0 * inv, epoch);
-    st_word(dst + 2 * lane + 1, a1 * inv, epoch);
-    if (lane == 0) {
-      st_word(dst + HD, mnat, epoch);
-      st_word(dst + HD + 1, den, epoch);
-    }
-  }
-  // every rank's words of this row, from this rank's own mailbox
-  const uint64_t* box = reinterpret_cast<const uint64_t*>(ex.mbox[ex.rank] + mbox_data_off(ex.rows));
-  float v0[MAX_RANKS], v1[MAX_RANKS], vm[MAX_RANKS], vl[MAX_RANKS];
-  bool ok = true;
-  const unsigned long long t0 = global_ns();
-#pragma unroll
-  for (int r = 0; r < MAX_RANKS; ++r) {
-    v0[r] = v1[r] = 0.f;
-    vm[r] = -INFINITY;
-    vl[r] = 0.f;
-    if (r >= ex.world || !ok) continue;
-    const uint64_t* src = box + ((size_t)(buf * MAX_RANKS + r) * ex.rows + row) * (HD + 2);
-    uint32_t spins = 0;
-    while (true) {
-      const uint64_t w0 = ld_word(src + 2 * lane), w1 = ld_word(src + 2 * lane + 1);
-      const uint64_t wm = ld_word(src + HD), wl = ld_word(src + HD + 1);
-      const bool here = (uint32_t)(w0 >> 32) == epoch && (uint32_t)(w1 >> 32) == epoch &&
-                        (uint32_t)(wm >> 32) == epoch && (uint32_t)(wl >> 32) == epoch;
-      if (__all_sync(0xffffffffu, here)) {
-        v0[r] = __uint_as_float((uint32_t)w0);
-        v1[r] = __uint_as_float((uint32_t)w1);
-        vm[r] = __uint_as_float((uint32_t)wm);
-        vl[r] = __uint_as_float((uint32_t)wl);
-        break;
-      }
-      if (++spins > 32) __nanosleep(64);
-      if ((long long)(global_ns() - t0) > ex.timeout_ns) {
-        ok = false;
-        break;
-      }
-    }
-  }
-  if (!ok && lane == 0) record_error(err, kErrWaitTimeout);
-  float Mr = -INFINITY;
-#pragma unroll
-  for (int r = 0; r < MAX_RANKS; ++r)
-    if (vl[r] > 0.f) Mr = fmaxf(Mr, vm[r]);
-  float dr = 0.f, c0 = 0.f, c1 = 0.f;
-#pragma unroll
-  for (int r = 0; r < MAX_RANKS; ++r) {
-    if (!(vl[r] > 0.f)) continue;
-    const float wt = vl[r] * expf(vm[r] - Mr);
-    dr += wt;
-    c0 = fmaf(wt, v0[r], c0);
-    c1 = fmaf(wt, v1[r], c1);
-  }
-  const float ir = dr > 0.f ? 1.0f / dr : 0.f;
-  final_out[(int64_t)row * HD + 2 * lane] = c0 * ir;
-  final_out[(int64_t)row * HD + 2 * lane + 1] = c1 * ir;
-  if (lane == 0) *reinterpret_cast<volatile int*>(epochs + row) = (int)epoch;
-}
+constexpr int RU = 20;   // CTA partials loaded per round trip in the ring reduce
 
 // Config 3: the fp32 ring tokens' partial and the reduce in one launch.  CTA =
 // (sequence, KV head), warp = query head.  Launched with programmatic dependent
@@ -973,7 +1038,7 @@ __global__ void __launch_bounds__(256) q4_reduce_ring_kernel(const float* __rest
     for (int u = 0; u < RU; ++u) {
       const int c = cbase + u;
       if (c <= cl) {
-        const float* src = cta_part + ((((int64_t)c + b) * NKV + kvh) * GROUP + hh) * (HD + 2);
+        const float* src = cta_part + ((((int64_t)c + b) * NKV + kvh) * GROUP + hh) * CP;
         ml[u] = __ldcg(reinterpret_cast<const float2*>(src + HD));
         ov[u] = __ldcg(reinterpret_cast<const float2*>(src) + lane);
       } else {
@@ -1029,23 +1094,30 @@ __global__ void lse_combine_kernel(const float* __restrict__ parts, int G, int64
   *reinterpret_cast<float4*>(out + r * HD + d4) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
 }
 
-size_t smem_bytes() { return sizeof(Smem) + 128; }
-// two CTAs per SM: 2 x (dynamic + 1 KB reserved) within the 228 KB of an SM
-static_assert(sizeof(Smem) + 128 + 1024 <= 114 * 1024, "decode_q4 shared memory must allow 2 CTAs per SM");
+size_t smem_bytes() { return sizeof(Smem); }
+static_assert(sizeof(Smem) <= 227 * 1024, "decode_q4 shared memory must fit one CTA per SM");
 
+// Workspace: [counters: group (MAX_GRID + MAX_SEQS) | sequence (MAX_SEQS)]
+// [meta: batch x 2][CTA partials: (MAX_GRID + batch) x ROWS x CP floats].
+// The counter block has a fixed size and must be zero before the first call;
+// the kernel leaves it at zero.
 struct WsLayout {
-  size_t meta, cta_part, total;
+  size_t gcnt, scnt, meta, cta_part, total;
 };
 
 WsLayout ws_layout(int batch) {
   const int b = batch < MAX_SEQS ? batch : MAX_SEQS;
   auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
   WsLayout w;
-  w.meta = 0;
-  w.cta_part = al((size_t)b * 2 * sizeof(int32_t));
-  w.total = w.cta_part + al((size_t)(MAX_GRID + b) * NKV * GROUP * (HD + 2) * sizeof(float));
+  w.gcnt = 0;
+  w.scnt = al((size_t)(MAX_GRID + MAX_SEQS) * sizeof(int32_t));
+  w.meta = w.scnt + al((size_t)MAX_SEQS * sizeof(int32_t));
+  w.cta_part = w.meta + al((size_t)b * 2 * sizeof(int32_t));
+  w.total = w.cta_part + al((size_t)(MAX_GRID + b) * ROWS * CP * sizeof(float));
   return w;
 }
+
+size_t counter_bytes() { return ws_layout(1).meta; }
 
 int32_t check_shape(int32_t n_heads, int32_t n_kv_heads, int32_t head_dim) {
   if (n_kv_heads != NKV || n_heads != NKV * GROUP || head_dim != HD)
@@ -1055,10 +1127,17 @@ int32_t check_shape(int32_t n_heads, int32_t n_kv_heads, int32_t head_dim) {
   return NYION_OK;
 }
 
+// The library-owned workspace (when `ws` is null) or a check of the caller's.
+int32_t resolve_workspace(void** ws, size_t ws_bytes, size_t need, cudaStream_t stream, const char* who) {
+  if (!*ws) return internal_workspace(need, ws, kWsCounters, counter_bytes(), stream);
+  if (ws_bytes < need) return fail(NYION_ERR_WORKSPACE, "%s: workspace %zu < %zu", who, ws_bytes, need);
+  return NYION_OK;
+}
+
+// One decode launch per MAX_SEQS sequences (mode Part / Final / Exchange), or,
+// in ring mode, the decode then the ring + reduce kernel.
 int32_t launch_partial(Params base, int batch, const int32_t* tok_begin, const int32_t* tok_end,
-                       const float* q, float* part, const int32_t* table, void* ws,
-                       cudaStream_t stream, float* final_out = nullptr, RingArgs ra = RingArgs{},
-                       const Exchange& ex = Exchange{}) {
+                       const float* q, void* ws, cudaStream_t stream, RingArgs ra = RingArgs{}) {
   DeviceInfo* dev = nullptr;
   int32_t st = device_info(&dev);
   if (st) return st;
@@ -1068,43 +1147,43 @@ int32_t launch_partial(Params base, int batch, const int32_t* tok_begin, const i
   if (st) return st;
   const int grid = dev->num_sms * occ < MAX_GRID ? dev->num_sms * occ : MAX_GRID;
   const WsLayout w = ws_layout(batch);
+  uint8_t* wsb = static_cast<uint8_t*>(ws);
   for (int b0 = 0; b0 < batch; b0 += MAX_SEQS) {
     Params p = base;
     const int nb = batch - b0 < MAX_SEQS ? batch - b0 : MAX_SEQS;
     p.batch = nb;
     p.tok_begin = tok_begin ? tok_begin + b0 : nullptr;
     p.tok_end = tok_end ? tok_end + b0 : nullptr;
-    p.q = q + (int64_t)b0 * NKV * GROUP * HD;
-    p.part = part + (int64_t)b0 * NKV * GROUP * (HD + 2);
-    p.table = table + (int64_t)b0 * base.max_pages;
+    p.q = q + (int64_t)b0 * ROWS * HD;
+    if (base.part) p.part = base.part + (int64_t)b0 * ROWS * (HD + 2);
+    if (base.out) p.out = base.out + (int64_t)b0 * ROWS * HD;
+    p.table = base.table + (int64_t)b0 * base.max_pages;
     p.seq_lens = base.seq_lens ? base.seq_lens + b0 : nullptr;
-    p.meta = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws) + w.meta);
-    p.cta_part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + w.cta_part);
+    p.gcnt = reinterpret_cast<int32_t*>(wsb + w.gcnt);
+    p.scnt = reinterpret_cast<int32_t*>(wsb + w.scnt);
+    p.meta = reinterpret_cast<int32_t*>(wsb + w.meta);
+    p.cta_part = reinterpret_cast<float*>(wsb + w.cta_part);
     p.err = dev->err_word;
-    st = check_cuda(launch_pdl(decode_q4_kernel, dim3(grid), dim3(THREADS), smem, stream, p),
-                    "decode_q4 launch");
+    st = check_cuda(launch_pdl(decode_q4_kernel, dim3(grid), dim3(THREADS), smem, stream, p), "decode_q4 launch");
     if (st) return st;
-    float* fo = final_out ? final_out + (int64_t)b0 * NKV * GROUP * HD : nullptr;
-    const float* cp = p.cta_part;
-    const int32_t* mt = p.meta;
-    if (ra.ring) {   // config 3: ring partial + reduce in one launch (final output only)
+    if (p.mode == kModeRing) {   // config 3: ring partial + reduce in one launch (final output)
       RingArgs r = ra;
-      r.q = q + (int64_t)b0 * NKV * GROUP * HD;
+      r.q = q + (int64_t)b0 * ROWS * HD;
       r.ring = ra.ring + (int64_t)b0 * NKV * 2 * ra.ring_tokens * HD;
       r.seq_lens = ra.seq_lens + b0;
-      st = check_cuda(launch_pdl(q4_reduce_ring_kernel, dim3(nb * NKV), dim3(256), 0, stream, cp, mt, fo, r),
+      st = check_cuda(launch_pdl(q4_reduce_ring_kernel, dim3(nb * NKV), dim3(256), 0, stream,
+                                 (const float*)p.cta_part, (const int32_t*)p.meta, p.out, r),
                       "q4_reduce_ring launch");
-    } else {
-      st = check_cuda(launch_pdl(q4_reduce_kernel, dim3(nb * NKV * GROUP), dim3(256), 0, stream, cp, mt, nb, p.part,
-                                 fo, ex, dev->err_word),
-                      "q4_reduce launch");
+      if (st) return st;
     }
-    if (st) return st;
   }
   return NYION_OK;
 }
 
 }  // namespace q4
+
+size_t q4_counter_bytes() { return q4::counter_bytes(); }
+
 }  // namespace nyion
 
 using namespace nyion;
@@ -1155,22 +1234,20 @@ extern "C" int32_t nyion_attn_decode_q4_partial(const float* q, const uint8_t* k
     return fail(NYION_ERR_INVALID, "decode_q4_partial: batch, max_pages, n_pool_pages must be > 0");
   if (reinterpret_cast<uintptr_t>(kv_pool) % 16)
     return fail(NYION_ERR_INVALID, "decode_q4_partial: kv_pool must be 16-byte aligned");
-  const size_t need = ws_layout(batch).total;
-  if (!workspace) {
-    st = internal_workspace(need, &workspace);
-    if (st) return st;
-  } else if (workspace_bytes < need) {
-    return fail(NYION_ERR_WORKSPACE, "decode_q4_partial: workspace %zu < %zu", workspace_bytes, need);
-  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = resolve_workspace(&workspace, workspace_bytes, ws_layout(batch).total, s, "decode_q4_partial");
+  if (st) return st;
   Params p{};
   p.pool = kv_pool;
+  p.table = page_table;
   p.u_begin = u_begin;
   p.u_end = u_end;
   p.max_pages = max_pages;
   p.n_pool_pages = n_pool_pages;
   p.qscale = (scale > 0.f ? scale : 1.0f / sqrtf((float)head_dim)) * 1.4426950408889634f;
-  return launch_partial(p, batch, tok_begin, tok_end, q, part, page_table, workspace,
-                        static_cast<cudaStream_t>(stream));
+  p.mode = kModePart;
+  p.part = part;
+  return launch_partial(p, batch, tok_begin, tok_end, q, workspace, s);
 }
 
 extern "C" int32_t nyion_attn_lse_combine(const float* parts, int32_t n_parts, int64_t rows,
@@ -1195,34 +1272,29 @@ extern "C" int32_t nyion_attn_decode_q4_window_ring(
     return fail(NYION_ERR_INVALID, "decode_q4_window_ring: null pointer argument");
   if (ring_tokens <= 0 || window <= 0 || batch <= 0)
     return fail(NYION_ERR_INVALID, "decode_q4_window_ring: ring_tokens, window, batch must be > 0");
-  // workspace: [q4 partial workspace][2 partial arrays of batch*H*(HD+2) floats][tok ranges]
+  if (ring_tokens > RING_MAX)
+    return fail(NYION_ERR_UNSUPPORTED, "decode_q4_window_ring: ring_tokens %d > %d", ring_tokens, RING_MAX);
+  // workspace: [q4 decode workspace][2 partial arrays of batch*H*(HD+2) floats][tok ranges]
   // (the documented size; the fused ring reduce writes `out` directly and leaves the
   // partial arrays unused)
   const size_t q4ws = ws_layout(batch).total;
   const size_t rows = (size_t)batch * n_heads;
   const size_t parts_bytes = 2 * rows * (HD + 2) * sizeof(float);
   const size_t range_bytes = 2 * (size_t)batch * sizeof(int32_t);
-  const size_t need = q4ws + parts_bytes + range_bytes;
-  if (!workspace) {
-    st = internal_workspace(need, &workspace);
-    if (st) return st;
-  } else if (workspace_bytes < need) {
-    return fail(NYION_ERR_WORKSPACE, "decode_q4_window_ring: workspace %zu < %zu", workspace_bytes, need);
-  }
-  if (ring_tokens > RING_MAX)
-    return fail(NYION_ERR_UNSUPPORTED, "decode_q4_window_ring: ring_tokens %d > %d", ring_tokens, RING_MAX);
-  uint8_t* w = static_cast<uint8_t*>(workspace);
-  float* parts = reinterpret_cast<float*>(w + q4ws);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = resolve_workspace(&workspace, workspace_bytes, q4ws + parts_bytes + range_bytes, s, "decode_q4_window_ring");
+  if (st) return st;
   Params p{};
   p.pool = kv_pool;
+  p.table = page_table;
   p.max_pages = max_pages;
   p.n_pool_pages = n_pool_pages;
   p.seq_lens = seq_lens;
   p.window = window;
   p.ring_tokens = ring_tokens;
-  const float sc = (scale > 0.f ? scale : 1.0f / sqrtf((float)head_dim));
-  p.qscale = sc * 1.4426950408889634f;
+  p.qscale = (scale > 0.f ? scale : 1.0f / sqrtf((float)head_dim)) * 1.4426950408889634f;
+  p.mode = kModeRing;
+  p.out = out;
   RingArgs ra{};
   ra.q = q;
   ra.ring = ring;
@@ -1230,11 +1302,11 @@ extern "C" int32_t nyion_attn_decode_q4_window_ring(
   ra.ring_tokens = ring_tokens;
   ra.window = window;
   ra.qscale = p.qscale;
-  return launch_partial(p, batch, nullptr, nullptr, q, parts, page_table, w, s, out, ra);
+  return launch_partial(p, batch, nullptr, nullptr, q, workspace, s, ra);
 }
 
 
-// ---- split-KV decode with the exchange fused into the reduce ---------------
+// ---- split-KV decode with the exchange fused into the decode launch --------
 
 extern "C" size_t nyion_attn_splitkv_mailbox_bytes(int32_t batch, int32_t n_heads) {
   if (batch <= 0 || n_heads <= 0) return 0;
@@ -1297,31 +1369,27 @@ extern "C" int32_t nyion_attn_decode_q4_splitkv(
                 MAX_RANKS);
   if (reinterpret_cast<uintptr_t>(kv_pool) % 16)
     return fail(NYION_ERR_INVALID, "decode_q4_splitkv: kv_pool must be 16-byte aligned");
-  Exchange ex{};
+  Params p{};
   for (int r = 0; r < world; ++r) {
     if (!mailboxes[r]) return fail(NYION_ERR_INVALID, "decode_q4_splitkv: mailbox of rank %d is null", r);
-    ex.mbox[r] = static_cast<uint8_t*>(mailboxes[r]);
+    p.ex.mbox[r] = static_cast<uint8_t*>(mailboxes[r]);
   }
-  ex.world = world;
-  ex.rank = rank;
-  ex.rows = batch * n_heads;
-  ex.timeout_ns = (long long)(timeout_ms > 0 ? timeout_ms : 2000) * 1000000LL;
-  const size_t need = ws_layout(batch).total;
-  if (!workspace) {
-    st = internal_workspace(need, &workspace);
-    if (st) return st;
-  } else if (workspace_bytes < need) {
-    return fail(NYION_ERR_WORKSPACE, "decode_q4_splitkv: workspace %zu < %zu", workspace_bytes, need);
-  }
-  Params p{};
+  p.ex.world = world;
+  p.ex.rank = rank;
+  p.ex.rows = batch * n_heads;
+  p.ex.timeout_ns = (long long)(timeout_ms > 0 ? timeout_ms : 2000) * 1000000LL;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = resolve_workspace(&workspace, workspace_bytes, ws_layout(batch).total, s, "decode_q4_splitkv");
+  if (st) return st;
   p.pool = kv_pool;
+  p.table = page_table;
   p.u_begin = u_begin;
   p.u_end = u_end;
   p.max_pages = max_pages;
   p.n_pool_pages = n_pool_pages;
   p.qscale = (scale > 0.f ? scale : 1.0f / sqrtf((float)head_dim)) * 1.4426950408889634f;
-  // the partial buffer is not written in exchange mode; the CTA partials go
-  // to the workspace and the combined rows to `out`
-  return launch_partial(p, batch, nullptr, nullptr, q, out, page_table, workspace,
-                        static_cast<cudaStream_t>(stream), out, RingArgs{}, ex);
+  // one rank: the merged rows are the output (no exchange needed)
+  p.mode = world > 1 ? kModeExchange : kModeFinal;
+  p.out = out;
+  return launch_partial(p, batch, nullptr, nullptr, q, workspace, s);
 }

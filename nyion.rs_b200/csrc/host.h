@@ -113,6 +113,10 @@ int32_t contig_zoned_f32(const float* q, const float* k_arena, const float* v_ar
                          int n_layers, int layer, int64_t n_pages, int n, float sl2, void* ws, size_t ws_bytes,
                          cudaStream_t stream);
 
+// Leading bytes of the 4-bit decode's workspace that hold its merge counters
+// (decode_q4.cu): zero before the first call, left at zero by every call.
+size_t q4_counter_bytes();
+
 // Handle behind gpu_graph_create_attention[_half]: the instantiated graph
 // and the workspace it owns (freed by gpu_graph_destroy).
 struct AttnGraph {

@@ -68,9 +68,9 @@ class SplitKVDecoder:
     mode: str = "p2p"
     timeout_ms: int = 2000
 
-    # kernels one p2p step launches on each rank (the decode, then the reduce
-    # with the exchange fused in)
-    LAUNCHES_PER_STEP = 2
+    # kernels one p2p step launches on each rank: the decode, whose last CTAs
+    # merge the partials and run the exchange
+    LAUNCHES_PER_STEP = 1
 
     def __post_init__(self):
         self.lo, self.hi = rank_range(self.rank, self.world, self.total_tokens)
