@@ -8,19 +8,24 @@
 // low nibble for even i; d = absmax / 7, q = clamp(round((x - dmin) / d), 0, 15),
 // dequant x' = f32(d) * q + f32(dmin).
 //
-// Q4 decode on B200.  A nibble n becomes the fp16 value 1 + n/16 with one
-// shift and one LOP3 per pair of values ((w << s) & 0x03C003C0 | 0x3C003C00),
-// so the block's dot product  sum q_i (d n_i + dmin)  becomes
-//   d * 16 * (sum q_i (1 + n_i/16) - sum q_i) + dmin * sum q_i,
-// with sum q_i (1 + n_i/16) on the tensor cores (mma.sync m16n8k16 f16, fp32
-// accumulate; q split into fp16 hi + lo rows) and the rest a per-score fix-up.
-// P.V uses the same identity: v = 16 d (1 + n/16) + (dmin - 16 d), so
-// o = sum_t (16 p_t d_t) v'_t  +  sum_t p_t (dmin_t - 16 d_t) per block.
-// Only the nibbles of V are staged again in shared memory, as an fp16 tile for
-// ldmatrix.trans; K nibbles go straight from a 4-byte load into the B
-// fragments.  The dims inside a 32-value block are visited in a fixed
-// permutation (pairs (0,4), (1,5), (2,6), (3,7) of each 8-value group) that q
-// and the output share.
+// Q4 decode on B200.  A nibble n placed in the low mantissa bits of an fp16
+// with a zero exponent field is the subnormal n * 2^-24 (bits 0-3) or
+// n * 2^-20 (bits 4-7): one LOP3 (a mask) per pair of values, no offset to
+// cancel, and the tensor cores multiply subnormal fp16 inputs exactly.  A
+// 32-bit word of nibbles gives four fp16x2 registers with one shift and four
+// masks.  The block's dot product  sum q_i (d n_i + dmin)  is
+//   d * 2^16 * sum q'_i n'_i + dmin * sum q_i
+// with q'_i = q_i * 2^8 (low nibbles) or 2^4 (high nibbles), so that every
+// product q'_i n'_i is q_i n_i 2^-16, on mma.sync m16n8k16 f16 with fp32
+// accumulation (q' split into fp16 hi + lo rows); the per-token factors and
+// the dmin term are a per-score fix-up.  P.V:  o = sum_t (p_t d_t) n_t +
+// sum_t p_t dmin_t  per block, with p d split into fp16 hi + lo rows (A) and
+// the V nibbles as subnormal B fragments built in registers straight from two
+// tokens' nibble words (one PRMT per pair of halfwords); the powers of two of
+// the nibble positions are restored on the output.  The dims of the K side
+// are visited in a fixed permutation (pairs (0,4), (1,5), (2,6), (3,7) of each
+// 8-value group) that q shares; the V side's output column c of n-tile
+// (block, j) is dim 32 block + 4 c + j.
 //
 // Work split: the (sequence, 64-token chunk) units of a call are flattened
 // and cut into equal contiguous ranges, one persistent CTA per SM.  A CTA
@@ -137,7 +142,8 @@ __global__ void dequant_kernel(const uint8_t* __restrict__ src, float* __restric
 // Q4 paged decode with the split-KV merge (and the rank exchange) in-launch
 // ============================================================================
 
-constexpr int STAGES = 4;               // 20 KB each
+constexpr int STAGE_SHIFT = 3;
+constexpr int STAGES = 1 << STAGE_SHIFT;   // 20 KB each
 constexpr int GROUPS = 2;               // consumer groups: stage s is consumed by group s % GROUPS
 constexpr int NCW = GROUPS * NKV * 2;   // 16 consumer warps: group x KV head x 32-token half
 constexpr int NCT = NCW * 32;           // 512 consumer threads
@@ -145,12 +151,12 @@ constexpr int THREADS = NCT + 32;       // + the producer warp
 constexpr int MAX_SEQS = 512;
 constexpr int MAX_GRID = 1024;
 constexpr int RING = 32;                // chunks whose page ids the producer stages ahead
-constexpr int VT_STRIDE = 144;          // bytes per token row of a warp's fp16 V tile (128 + 16)
-constexpr int HT_STRIDE = 48;           // bytes per token of a warp's factor table (32 + 16)
+constexpr int PAIR_STRIDE = 80;         // bytes per token pair of a warp's factor table (64 + 16)
 constexpr int ROWS = NKV * GROUP;       // query heads of a sequence
 constexpr int CP = HD + 4;              // floats per row of a CTA partial: o[64], m, l, 2 unused
+constexpr int WK_BYTES = GROUP * CP * 4;   // per-warp region: factor table, then the segment partial
+static_assert(16 * PAIR_STRIDE <= WK_BYTES, "the factor table fits the per-warp region");
 static_assert(STAGES % GROUPS == 0, "a stage must always be consumed by the same warps");
-static_assert(STAGES == 4, "the stage and phase arithmetic of the chunk loops assumes 4 stages");
 static_assert(NCT == ROWS * 16, "merge mapping: 16 threads per query head, 4 dims each");
 
 enum : int32_t { kModePart = 0, kModeFinal = 1, kModeExchange = 2, kModeRing = 3 };
@@ -219,8 +225,10 @@ struct Params {
 
 struct Smem {
   uint8_t kv[STAGES][STAGE_BYTES];
-  uint8_t vt[NCW][32 * VT_STRIDE];   // per warp: V chunk as fp16 [32 tokens][64] (row padded)
-  uint8_t ht[NCW][32 * HT_STRIDE];   // per warp and token: K factors | V factors (row padded)
+  // per warp: the factor table of the chunk (token pair j at j * PAIR_STRIDE:
+  // K {16 d0, dmin0 - 16 d0, 16 d1, dmin1 - 16 d1} then V, each value for both
+  // tokens of the pair), then at the end of a sequence its partial [GROUP][CP]
+  uint8_t wk[NCW][WK_BYTES];
   uint64_t full[STAGES], empty[STAGES];
   int32_t vmask[STAGES];             // bit pg: page pg of the stage was copied
   int32_t prefix[MAX_SEQS + 1];      // flat chunk index where sequence b starts
@@ -275,13 +283,6 @@ __device__ __forceinline__ void rows_finish(Smem& s, const Params& p, const RowJ
     s.rows[slot][lane][pg] = v;
   }
   s.rows[slot][lane][4] = j.b;
-}
-
-// fp16x2 {1 + n_a/16, 1 + n_b/16} from the nibbles at bits [s+0..3] and [s+16..19] of w
-template <int SHIFT>
-__device__ __forceinline__ uint32_t nib2h(uint32_t w) {
-  const uint32_t x = SHIFT >= 0 ? (w << SHIFT) : (w >> (-SHIFT));
-  return (x & 0x03C003C0u) | 0x3C003C00u;
 }
 
 __device__ __forceinline__ float2 hdr2f(uint32_t w) {   // (d, dmin) of a block header word
@@ -527,13 +528,13 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
         rows_start(job, s, p, begin + k + RING + lane, end);
       }
       bool ok = true;
-      if (k >= STAGES) ok = mbar_wait_bounded(&s.empty[stage], (uint32_t)(((k >> 2) - 1) & 1));
+      if (k >= STAGES) ok = mbar_wait_bounded(&s.empty[stage], (uint32_t)(((k >> STAGE_SHIFT) - 1) & 1));
       if (!__all_sync(0xffffffffu, ok)) {
         record_error(p.err, kErrWaitTimeout);
         if (lane == 0) {
           atomicExch(&s.abort_, 1);
           for (int c = k - 1; c >= 0 && c >= k - STAGES; --c)
-            mbar_wait_bounded(&s.full[c & 3], (uint32_t)((c >> 2) & 1));
+            mbar_wait_bounded(&s.full[c & (STAGES - 1)], (uint32_t)((c >> STAGE_SHIFT) & 1));
         }
         return;
       }
@@ -565,15 +566,24 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
   // ================= consumer warps =================
   const int grp = warp >> 3, kvh = warp & 3, th = (warp >> 2) & 1;
   const int g = lane >> 2, tig = lane & 3;
-  const int woff = th * 2 * PAGE_BYTES + kvh * PAGE_KV;                        // the warp's 2 pages, its KV head
-  const int loff_v = (lane >> 4) * PAGE_BYTES + PAGE * ROWB + (lane & 15) * ROWB;   // V row of token `lane`
-  const int loff_k = g * ROWB + 4 + 4 * tig;                                  // K word tig of token g, block 0
-  uint8_t* const vtw = s.vt[warp] + lane * VT_STRIDE;
-  const uint32_t vtr = smem_u32(s.vt[warp]) + (8 * ((lane >> 3) & 1) + (lane & 7)) * VT_STRIDE + (lane >> 4) * 16;
-  uint8_t* const htw = s.ht[warp] + lane * HT_STRIDE;
-  const uint8_t* const htr = s.ht[warp] + 2 * tig * HT_STRIDE;
+  const int woff = th * 2 * PAGE_BYTES + kvh * PAGE_KV;   // the warp's 2 pages, its KV head
+  // K B-fragments: word tig of block 0 of token g (n-tile 0)
+  const int loff_k = g * ROWB + 4 + 4 * tig;
+  // V B-fragments: word g / 2 of block 0 of token 2 tig (k-step 0); the lane
+  // takes half g % 2 of that word from two tokens at once
+  const int loff_v = PAGE * ROWB + 2 * tig * ROWB + 4 + 4 * (g >> 1);
+  const uint32_t vsel = (g & 1) ? 0x7632u : 0x5410u;    // [A.b(2h), A.b(2h+1), B.b(2h), B.b(2h+1)]
+  const uint32_t vsel2 = (g & 1) ? 0x0703u : 0x0501u;   // [A.b(2h+1), -, B.b(2h+1), -]
+  // factor table: lane L fills pair L % 16 (tokens 2 (L % 16), + 1) with K
+  // (L < 16) or V factors, from the two tokens' header words
+  const int fj = lane & 15, fpart = lane >> 4;
+  const int loff_f = (fj >> 3) * PAGE_BYTES + ((2 * fj) & 15) * ROWB + fpart * PAGE * ROWB;
+  uint8_t* const ftw = s.wk[warp] + fj * PAIR_STRIDE + fpart * 32;
+  // the lane's token pairs in the fix-up: pair 4 nt + tig
+  const uint8_t* const ftr = s.wk[warp] + tig * PAIR_STRIDE;
   // merge mapping: thread -> query head r of the sequence, dims d4 .. d4 + 3
   const int mr = t >> 4, md4 = (t & 15) * 4;
+  const float2 neg1 = make_float2(-1.f, -1.f);
 
   int i = begin;
   while (i < end) {
@@ -584,9 +594,10 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
     // q fragments, dims permuted: k-step (blk, ks) pairs dims 32blk + 8tig + {ks*2 + (0,4)} in
     // a0/a1 and {ks*2 + (1,5)} in a2/a3, hi rows 0-7 and lo rows 8-15
     uint32_t qa[2][2][4];
-    float qs[2];      // sum of the (hi + lo) q values of head g over each block
+    float2 qs0, qs1;   // sum of the (hi + lo) q values of head g over each block, twice
     {
       const float* qp = p.q + ((int64_t)b * H + kvh * GROUP + g) * HD;
+      float qsum[2];
 #pragma unroll
       for (int blk = 0; blk < 2; ++blk) {
         float x[8];
@@ -597,73 +608,85 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
 #pragma unroll
         for (int ks = 0; ks < 2; ++ks) {
           uint32_t h0, l0, h1, l1;
-          split_f16x2(x[2 * ks] * p.qscale, x[2 * ks + 4] * p.qscale, h0, l0);
-          split_f16x2(x[2 * ks + 1] * p.qscale, x[2 * ks + 5] * p.qscale, h1, l1);
+          // even elements meet low nibbles (n 2^-24): q 2^8; odd ones high nibbles (n 2^-20): q 2^4
+          const float se = p.qscale * 256.0f, so = p.qscale * 16.0f;
+          split_f16x2(x[2 * ks] * se, x[2 * ks + 4] * se, h0, l0);
+          split_f16x2(x[2 * ks + 1] * so, x[2 * ks + 5] * so, h1, l1);
           qa[blk][ks][0] = h0; qa[blk][ks][1] = l0; qa[blk][ks][2] = h1; qa[blk][ks][3] = l1;
           const float2 fh0 = __half22float2(*reinterpret_cast<const __half2*>(&h0));
           const float2 fl0 = __half22float2(*reinterpret_cast<const __half2*>(&l0));
           const float2 fh1 = __half22float2(*reinterpret_cast<const __half2*>(&h1));
           const float2 fl1 = __half22float2(*reinterpret_cast<const __half2*>(&l1));
-          sum += (fh0.x + fl0.x) + (fh0.y + fl0.y) + (fh1.x + fl1.x) + (fh1.y + fl1.y);
+          // sum of the q values the tensor cores see, back at scale (exact powers of two)
+          sum += ((fh0.x + fl0.x) + (fh0.y + fl0.y)) * (1.0f / 256.0f) +
+                 ((fh1.x + fl1.x) + (fh1.y + fl1.y)) * (1.0f / 16.0f);
         }
         sum += __shfl_xor_sync(0xffffffffu, sum, 1);
         sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-        qs[blk] = sum;
+        qsum[blk] = sum;
       }
+      qs0 = make_float2(qsum[0], qsum[0]);
+      qs1 = make_float2(qsum[1], qsum[1]);
     }
+    // O accumulators: n-tile (blk, j) column c = dim 32 blk + 4 c + j; rows g (P' hi)
+    // and g + 8 (P' lo) of head g
     float o[8][4];
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
       for (int j = 0; j < 4; ++j) o[nt][j] = 0.f;
-    float cb[2] = {0.f, 0.f};   // sum_t p_t (dmin - 16 d) per V block (this thread's tokens)
-    float m = -INFINITY, l = 0.f;
+    // per V block: sum_t p_t dmin, and sum_t p_t, for this lane's even / odd tokens
+    float2 cb0 = make_float2(0.f, 0.f), cb1 = make_float2(0.f, 0.f), l2 = make_float2(0.f, 0.f);
+    float m = -INFINITY;   // reference max (log2 units) of head g
 
     int k = i - begin;
     k += (k & 1) ^ grp;         // this group's chunks: k = grp (mod 2)
     for (; k < seg_hi - begin; k += 2) {
       const int stage = k & (STAGES - 1);
       if (!s.abort_) {
-        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&s.full[stage], (uint32_t)((k >> 2) & 1)))) {
+        if (!__all_sync(0xffffffffu,
+                        mbar_wait_bounded(&s.full[stage], (uint32_t)((k >> STAGE_SHIFT) & 1)))) {
           record_error(p.err, kErrWaitTimeout);
           if (lane == 0) atomicExch(&s.abort_, 1);
         }
       }
       const int chunk = c0b + (begin + k - pb);
-      const int pos0 = chunk * CHUNK + 32 * th;       // absolute position of this warp's token 0
+      const int pos0 = chunk * CHUNK + 32 * th;         // absolute position of this warp's token 0
       const int vm = (s.vmask[stage] >> (2 * th)) & 3;  // this warp's two pages were copied
       const bool any = vm != 0 && (pos0 < se) && (pos0 + 32 > sb);
       const bool inner = vm == 3 && (pos0 >= sb) && (pos0 + 32 <= se);   // no token of this warp is masked
       if (any) {
         const uint8_t* const kb = s.kv[stage] + woff;
-        // ---- V nibbles of token `lane` -> fp16 tile row `lane`; its block factors ----
+        // ---- factor table: pair fj's K (or V) block factors ----
         {
-          const uint8_t* const vr = kb + loff_v;
-#pragma unroll
-          for (int blk = 0; blk < 2; ++blk)
-#pragma unroll
-            for (int wq = 0; wq < 4; ++wq) {
-              const uint32_t w = *reinterpret_cast<const uint32_t*>(vr + blk * BLK + 4 + 4 * wq);
-              *reinterpret_cast<uint4*>(vtw + (4 * blk + wq) * 16) =
-                  make_uint4(nib2h<6>(w), nib2h<2>(w), nib2h<-2>(w), nib2h<-6>(w));
-            }
-          // block factors of token `lane` as the fp32 values the score and P.V steps use:
-          // score = sum_blk 16 d (q.(1 + n/16)) + (dmin - 16 d) qs; zero for masked tokens
-          const uint8_t* const kr = vr - PAGE * ROWB;
-          const float2 k0 = hdr2f(*reinterpret_cast<const uint32_t*>(kr));
-          const float2 k1 = hdr2f(*reinterpret_cast<const uint32_t*>(kr + BLK));
-          const float2 v0 = hdr2f(*reinterpret_cast<const uint32_t*>(vr));
-          const float2 v1 = hdr2f(*reinterpret_cast<const uint32_t*>(vr + BLK));
-          const bool live = inner || ((pos0 + lane >= sb) && (pos0 + lane < se) && ((vm >> (lane >> 4)) & 1));
-          const float a0 = 16.0f * k0.x, a1 = 16.0f * k1.x, b0 = 16.0f * v0.x, b1 = 16.0f * v1.x;
-          const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-          *reinterpret_cast<float4*>(htw) = live ? make_float4(a0, k0.y - a0, a1, k1.y - a1) : zero;
-          *reinterpret_cast<float4*>(htw + 16) = live ? make_float4(b0, v0.y - b0, b1, v1.y - b1) : zero;
+          const uint8_t* const hr = kb + loff_f;
+          const uint32_t wa0 = *reinterpret_cast<const uint32_t*>(hr);            // token 2 fj, block 0
+          const uint32_t wa1 = *reinterpret_cast<const uint32_t*>(hr + BLK);      // token 2 fj, block 1
+          const uint32_t wb0 = *reinterpret_cast<const uint32_t*>(hr + ROWB);     // token 2 fj + 1
+          const uint32_t wb1 = *reinterpret_cast<const uint32_t*>(hr + ROWB + BLK);
+          const float2 fa0 = hdr2f(wa0), fa1 = hdr2f(wa1), fb0 = hdr2f(wb0), fb1 = hdr2f(wb1);
+          float2 d0 = make_float2(fa0.x, fb0.x), dm0 = make_float2(fa0.y, fb0.y);
+          float2 d1 = make_float2(fa1.x, fb1.x), dm1 = make_float2(fa1.y, fb1.y);
+          if (!inner) {   // zero factors for masked tokens (their stage bytes may be stale)
+            const int p0 = pos0 + 2 * fj;
+            const bool pv = (vm >> (fj >> 3)) & 1;
+            const bool l0 = pv && p0 >= sb && p0 < se, l1 = pv && p0 + 1 >= sb && p0 + 1 < se;
+            if (!l0) d0.x = dm0.x = d1.x = dm1.x = 0.f;
+            if (!l1) d0.y = dm0.y = d1.y = dm1.y = 0.f;
+          }
+          // K: {2^16 d, dmin} (the scores' nibble products carry 2^-16); V: {d, dmin};
+          // each value for both tokens of the pair
+          const float2 sc = fpart ? make_float2(1.f, 1.f) : make_float2(65536.f, 65536.f);
+          const float2 a0 = __fmul2_rn(d0, sc), a1 = __fmul2_rn(d1, sc);
+          *reinterpret_cast<float4*>(ftw) = make_float4(a0.x, a0.y, dm0.x, dm0.y);
+          *reinterpret_cast<float4*>(ftw + 16) = make_float4(a1.x, a1.y, dm1.x, dm1.y);
         }
-        __syncwarp();   // V tile rows and factors written by all lanes
-        // ---- S = Q K^T: 4 n-tiles of 8 tokens, 2 blocks x 2 k-steps; each
-        //      n-tile's scores are fixed up as soon as its MMAs are done ----
-        float sv[4][2];
+        __syncwarp();   // the factor table is complete
+        // ---- S = Q K^T per n-tile of 8 tokens, fixed up at once into
+        //      d = score - mref for the lane's tokens 8 nt + 2 tig + (0, 1) ----
+        const float mref = m == -INFINITY ? 0.f : m;    // nothing attended yet: scores as they are
+        const float2 negm = make_float2(-mref, -mref);
+        float2 dv[4];
         {
           const uint8_t* const kq = kb + loff_k;
 #pragma unroll
@@ -674,93 +697,101 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
 #pragma unroll
               for (int j = 0; j < 4; ++j) sc[blk][j] = 0.f;
               const uint32_t w = *reinterpret_cast<const uint32_t*>(kq + nt_off(nt) + blk * BLK);
-              mma_f16(sc[blk], qa[blk][0], nib2h<6>(w), nib2h<2>(w));
-              mma_f16(sc[blk], qa[blk][1], nib2h<-2>(w), nib2h<-6>(w));
+              const uint32_t w8 = w >> 8;
+              mma_f16(sc[blk], qa[blk][0], w & 0x000F000Fu, w & 0x00F000F0u);
+              mma_f16(sc[blk], qa[blk][1], w8 & 0x000F000Fu, w8 & 0x00F000F0u);
             }
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              // token 8 nt + 2 tig + e: a0, c0, a1, c1
-              const float4 h = *reinterpret_cast<const float4*>(htr + (8 * nt + e) * HT_STRIDE);
-              const float t0 = sc[0][e] + sc[0][2 + e];            // sum q (1 + n/16), hi + lo rows
-              const float t1 = sc[1][e] + sc[1][2 + e];
-              sv[nt][e] = fmaf(h.x, t0, fmaf(h.z, t1, fmaf(h.y, qs[0], h.w * qs[1])));
-            }
+            // sum q' n' per block, hi + lo rows, both tokens
+            const float2 t0 = __fadd2_rn(make_float2(sc[0][0], sc[0][1]), make_float2(sc[0][2], sc[0][3]));
+            const float2 t1 = __fadd2_rn(make_float2(sc[1][0], sc[1][1]), make_float2(sc[1][2], sc[1][3]));
+            const float4 fk0 = *reinterpret_cast<const float4*>(ftr + nt * 4 * PAIR_STRIDE);        // a0 | c0
+            const float4 fk1 = *reinterpret_cast<const float4*>(ftr + nt * 4 * PAIR_STRIDE + 16);   // a1 | c1
+            float2 x = __ffma2_rn(make_float2(fk1.z, fk1.w), qs1, negm);
+            x = __ffma2_rn(make_float2(fk0.z, fk0.w), qs0, x);
+            x = __ffma2_rn(make_float2(fk1.x, fk1.y), t1, x);
+            dv[nt] = __ffma2_rn(make_float2(fk0.x, fk0.y), t0, x);
           }
         }
         if (!inner) {   // the range starts or ends, or a page is missing, inside this warp's 32 tokens
 #pragma unroll
-          for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int pos = pos0 + 8 * nt + 2 * tig + e;
-              if (pos < sb || pos >= se || !((vm >> (nt >> 1)) & 1)) sv[nt][e] = -INFINITY;
-            }
+          for (int nt = 0; nt < 4; ++nt) {
+            const int pos = pos0 + 8 * nt + 2 * tig;
+            const bool pv = (vm >> (nt >> 1)) & 1;
+            if (!(pv && pos >= sb && pos < se)) dv[nt].x = -INFINITY;
+            if (!(pv && pos + 1 >= sb && pos + 1 < se)) dv[nt].y = -INFINITY;
+          }
         }
-        // ---- online softmax ----
-        float mx = sv[0][0];
+        // ---- online softmax: the reference max moves only when the chunk max
+        //      passes it by more than 2 (log2 units), so p <= 4 and most
+        //      chunks skip the rescale ----
+        float mx = fmaxf(dv[0].x, dv[0].y);
 #pragma unroll
-        for (int nt = 0; nt < 4; ++nt) mx = fmaxf(mx, fmaxf(sv[nt][0], sv[nt][1]));
+        for (int nt = 1; nt < 4; ++nt) mx = fmaxf(mx, fmaxf(dv[nt].x, dv[nt].y));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        // lazy rescale: the reference max m moves only when the chunk max passes it by
-        // more than 2 (log2 units), so p <= 4 and most chunks skip the rescale
-        if (mx > m + 2.0f) {
-          const float al = exp2f(m - mx);                               // m = -inf: 0
-          l *= al;
+        if (mx > 2.0f || (m == -INFINITY && mx > -INFINITY)) {
+          const float al = m == -INFINITY ? 0.f : exp2f(-mx);
+          const float2 al2 = make_float2(al, al);
+          l2 = __fmul2_rn(l2, al2);
+          cb0 = __fmul2_rn(cb0, al2);
+          cb1 = __fmul2_rn(cb1, al2);
 #pragma unroll
-          for (int nt = 0; nt < 8; ++nt)
+          for (int nt = 0; nt < 8; ++nt) {
+            const float2 a = __fmul2_rn(make_float2(o[nt][0], o[nt][1]), al2);
+            const float2 c = __fmul2_rn(make_float2(o[nt][2], o[nt][3]), al2);
+            o[nt][0] = a.x; o[nt][1] = a.y; o[nt][2] = c.x; o[nt][3] = c.y;
+          }
+          m = mref + mx;
+          const float2 nmx = make_float2(-mx, -mx);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) o[nt][j] *= al;
-          cb[0] *= al;
-          cb[1] *= al;
-          m = mx;
+          for (int nt = 0; nt < 4; ++nt) dv[nt] = __fadd2_rn(dv[nt], nmx);
         }
-        const float mref = m == -INFINITY ? 0.f : m;                    // all masked so far: p = 0
-        float ps = 0.f;
-#pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
-          sv[nt][0] = exp2f(sv[nt][0] - mref);
-          sv[nt][1] = exp2f(sv[nt][1] - mref);
-          ps += sv[nt][0] + sv[nt][1];
-        }
-        l += ps;
-        // ---- P'_blk = 16 p d_V (A operand), correction terms ----
+        // ---- p, P'_blk = p d_V (the A operand, hi + lo), dmin terms ----
         uint32_t pa[2][2][4];   // [blk][kt]
 #pragma unroll
-        for (int kt = 0; kt < 2; ++kt) {
-          float pv[2][4];       // [blk][token e: 16kt + 2tig + {0,1,8,9}]
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int nt = 2 * kt + (e >> 1);
-            const float pe = sv[nt][e & 1];
-            // 16 d_V and dmin_V - 16 d_V of both blocks (zero for masked tokens, whose
-            // stage bytes may be stale)
-            const float4 h = *reinterpret_cast<const float4*>(htr + (8 * nt + (e & 1)) * HT_STRIDE + 16);
-            pv[0][e] = pe * h.x;
-            pv[1][e] = pe * h.z;
-            cb[0] = fmaf(pe, h.y, cb[0]);
-            cb[1] = fmaf(pe, h.w, cb[1]);
-          }
+        for (int nt = 0; nt < 4; ++nt) {
+          const float2 pp = make_float2(exp2f(dv[nt].x), exp2f(dv[nt].y));
+          l2 = __fadd2_rn(l2, pp);
+          const float4 fv0 = *reinterpret_cast<const float4*>(ftr + nt * 4 * PAIR_STRIDE + 32);   // d0 | dmin0
+          const float4 fv1 = *reinterpret_cast<const float4*>(ftr + nt * 4 * PAIR_STRIDE + 48);   // d1 | dmin1
+          const float2 pv0 = __fmul2_rn(pp, make_float2(fv0.x, fv0.y));
+          const float2 pv1 = __fmul2_rn(pp, make_float2(fv1.x, fv1.y));
+          cb0 = __ffma2_rn(pp, make_float2(fv0.z, fv0.w), cb0);
+          cb1 = __ffma2_rn(pp, make_float2(fv1.z, fv1.w), cb1);
+          // n-tile nt: k-step nt / 2, tokens 2 tig (+1) -> a0 / a1 (even nt) or a2 / a3 (odd nt)
+          const int kt = nt >> 1, r = (nt & 1) * 2;
 #pragma unroll
           for (int blk = 0; blk < 2; ++blk) {
-            split_f16x2(pv[blk][0], pv[blk][1], pa[blk][kt][0], pa[blk][kt][1]);
-            split_f16x2(pv[blk][2], pv[blk][3], pa[blk][kt][2], pa[blk][kt][3]);
+            const float2 x = blk ? pv1 : pv0;
+            const __half2 hi = __float22half2_rn(x);
+            const float2 res = __ffma2_rn(__half22float2(hi), neg1, x);
+            const __half2 lo = __float22half2_rn(res);
+            pa[blk][kt][r] = *reinterpret_cast<const uint32_t*>(&hi);
+            pa[blk][kt][r + 1] = *reinterpret_cast<const uint32_t*>(&lo);
           }
         }
-        // ---- O += P' V': k = 16 tokens, n-tiles of 8 (permuted) dims ----
+        // ---- O += P' V': B fragments straight from two tokens' nibble words ----
+        {
+          const uint8_t* const vq = kb + loff_v;
 #pragma unroll
-        for (int kt = 0; kt < 2; ++kt)
+          for (int kt = 0; kt < 2; ++kt)
 #pragma unroll
-          for (int np = 0; np < 4; ++np) {
-            uint32_t b0, b1, b2, b3;
-            asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-                         : "=r"(b0), "=r"(b1), "=r"(b2), "=r"(b3)
-                         : "r"(vtr + kt * 16 * VT_STRIDE + np * 32)
-                         : "memory");
-            const int blk = np >> 1;
-            mma_f16(o[2 * np], pa[blk][kt], b0, b1);
-            mma_f16(o[2 * np + 1], pa[blk][kt], b2, b3);
-          }
+            for (int blk = 0; blk < 2; ++blk) {
+              const uint8_t* const vw = vq + kt * PAGE_BYTES + blk * BLK;
+              const uint32_t w00 = *reinterpret_cast<const uint32_t*>(vw);              // token 2 tig
+              const uint32_t w01 = *reinterpret_cast<const uint32_t*>(vw + ROWB);       // token 2 tig + 1
+              const uint32_t w10 = *reinterpret_cast<const uint32_t*>(vw + 8 * ROWB);   // token 2 tig + 8
+              const uint32_t w11 = *reinterpret_cast<const uint32_t*>(vw + 9 * ROWB);   // token 2 tig + 9
+              // byte 2h (dims 4g, 4g + 1) and byte 2h + 1 (dims 4g + 2, 4g + 3) of each
+              // token's halfword, the first token in the low half of the register
+              const uint32_t u0 = __byte_perm(w00, w01, vsel), u1 = __byte_perm(w10, w11, vsel);
+              const uint32_t v0 = __byte_perm(w00, w01, vsel2), v1 = __byte_perm(w10, w11, vsel2);
+              mma_f16(o[4 * blk + 0], pa[blk][kt], u0 & 0x000F000Fu, u1 & 0x000F000Fu);
+              mma_f16(o[4 * blk + 1], pa[blk][kt], u0 & 0x00F000F0u, u1 & 0x00F000F0u);
+              mma_f16(o[4 * blk + 2], pa[blk][kt], v0 & 0x000F000Fu, v1 & 0x000F000Fu);
+              mma_f16(o[4 * blk + 3], pa[blk][kt], v0 & 0x00F000F0u, v1 & 0x00F000F0u);
+            }
+        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.empty[stage]);
@@ -768,23 +799,27 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
 
     // ---- segment end: the 4 warps of each KV head (2 groups x 2 token halves)
     //      fold their partials in shared memory into the CTA's partial ----
+    float l = l2.x + l2.y;
+    float cbs[2] = {cb0.x + cb0.y, cb1.x + cb1.y};
     l += __shfl_xor_sync(0xffffffffu, l, 1);
     l += __shfl_xor_sync(0xffffffffu, l, 2);
 #pragma unroll
     for (int blk = 0; blk < 2; ++blk) {
-      cb[blk] += __shfl_xor_sync(0xffffffffu, cb[blk], 1);
-      cb[blk] += __shfl_xor_sync(0xffffffffu, cb[blk], 2);
+      cbs[blk] += __shfl_xor_sync(0xffffffffu, cbs[blk], 1);
+      cbs[blk] += __shfl_xor_sync(0xffffffffu, cbs[blk], 2);
     }
-    consumer_sync();                    // every warp is done with its V tile
+    consumer_sync();                    // every warp is done with its factor table
     {
-      float* mine = reinterpret_cast<float*>(s.vt[warp]);   // [GROUP][CP]
+      float* mine = reinterpret_cast<float*>(s.wk[warp]);   // [GROUP][CP]
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt)
+      for (int blk = 0; blk < 2; ++blk)
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int c = 8 * nt + 2 * tig + e;
-          mine[g * CP + perm_dim(c)] = o[nt][e] + o[nt][2 + e] + cb[nt >> 2];
-        }
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+          for (int e = 0; e < 2; ++e)
+            // j even: low nibbles (n 2^-24), j odd: high nibbles (n 2^-20)
+            mine[g * CP + 32 * blk + 8 * tig + 4 * e + j] =
+                fmaf(o[4 * blk + j][e] + o[4 * blk + j][2 + e], (j & 1) ? 1048576.0f : 16777216.0f, cbs[blk]);
       if (tig == 0) {
         mine[g * CP + HD] = m;
         mine[g * CP + HD + 1] = l;
@@ -801,7 +836,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
       float4 os[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float* src = reinterpret_cast<const float*>(s.vt[kv + 4 * j]) + hh * CP;
+        const float* src = reinterpret_cast<const float*>(s.wk[kv + 4 * j]) + hh * CP;
         ms[j] = src[HD];
         ls[j] = src[HD + 1];
         os[j] = *reinterpret_cast<const float4*>(src + md4);
