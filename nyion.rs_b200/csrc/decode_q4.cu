@@ -653,7 +653,9 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
       const int chunk = c0b + (begin + k - pb);
       const int pos0 = chunk * CHUNK + 32 * th;         // absolute position of this warp's token 0
       const int vm = (s.vmask[stage] >> (2 * th)) & 3;  // this warp's two pages were copied
-      const bool any = vm != 0 && (pos0 < se) && (pos0 + 32 > sb);
+      // the body runs whenever the range meets the warp's tokens; missing pages
+      // (rare: bad page ids) go through the masking path like range ends
+      const bool any = (pos0 < se) && (pos0 + 32 > sb);
       const bool inner = vm == 3 && (pos0 >= sb) && (pos0 + 32 <= se);   // no token of this warp is masked
       if (any) {
         const uint8_t* const kb = s.kv[stage] + woff;
@@ -687,30 +689,26 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
         const float mref = m == -INFINITY ? 0.f : m;    // nothing attended yet: scores as they are
         const float2 negm = make_float2(-mref, -mref);
         float2 dv[4];
-        {
-          const uint8_t* const kq = kb + loff_k;
 #pragma unroll
-          for (int nt = 0; nt < 4; ++nt) {
-            float sc[2][4];
+        for (int nt = 0; nt < 4; ++nt) {
+          float sc[2][4];
 #pragma unroll
-            for (int blk = 0; blk < 2; ++blk) {
+          for (int blk = 0; blk < 2; ++blk) {
 #pragma unroll
-              for (int j = 0; j < 4; ++j) sc[blk][j] = 0.f;
-              const uint32_t w = *reinterpret_cast<const uint32_t*>(kq + nt_off(nt) + blk * BLK);
-              const uint32_t w8 = w >> 8;
-              mma_f16(sc[blk], qa[blk][0], w & 0x000F000Fu, w & 0x00F000F0u);
-              mma_f16(sc[blk], qa[blk][1], w8 & 0x000F000Fu, w8 & 0x00F000F0u);
-            }
-            // sum q' n' per block, hi + lo rows, both tokens
-            const float2 t0 = __fadd2_rn(make_float2(sc[0][0], sc[0][1]), make_float2(sc[0][2], sc[0][3]));
-            const float2 t1 = __fadd2_rn(make_float2(sc[1][0], sc[1][1]), make_float2(sc[1][2], sc[1][3]));
-            const float4 fk0 = *reinterpret_cast<const float4*>(ftr + nt * 4 * PAIR_STRIDE);        // a0 | c0
-            const float4 fk1 = *reinterpret_cast<const float4*>(ftr + nt * 4 * PAIR_STRIDE + 16);   // a1 | c1
-            float2 x = __ffma2_rn(make_float2(fk1.z, fk1.w), qs1, negm);
-            x = __ffma2_rn(make_float2(fk0.z, fk0.w), qs0, x);
-            x = __ffma2_rn(make_float2(fk1.x, fk1.y), t1, x);
-            dv[nt] = __ffma2_rn(make_float2(fk0.x, fk0.y), t0, x);
+            for (int j = 0; j < 4; ++j) sc[blk][j] = 0.f;
+            const uint32_t w = *reinterpret_cast<const uint32_t*>(kb + loff_k + nt_off(nt) + blk * BLK), w8 = w >> 8;
+            mma_f16(sc[blk], qa[blk][0], w & 0x000F000Fu, w & 0x00F000F0u);
+            mma_f16(sc[blk], qa[blk][1], w8 & 0x000F000Fu, w8 & 0x00F000F0u);
           }
+          // sum q' n' per block, hi + lo rows, both tokens
+          const float2 t0 = __fadd2_rn(make_float2(sc[0][0], sc[0][1]), make_float2(sc[0][2], sc[0][3]));
+          const float2 t1 = __fadd2_rn(make_float2(sc[1][0], sc[1][1]), make_float2(sc[1][2], sc[1][3]));
+          const float4 fk0 = *reinterpret_cast<const float4*>(ftr + nt * 4 * PAIR_STRIDE);        // a0 | c0
+          const float4 fk1 = *reinterpret_cast<const float4*>(ftr + nt * 4 * PAIR_STRIDE + 16);   // a1 | c1
+          float2 x = __ffma2_rn(make_float2(fk1.z, fk1.w), qs1, negm);
+          x = __ffma2_rn(make_float2(fk0.z, fk0.w), qs0, x);
+          x = __ffma2_rn(make_float2(fk1.x, fk1.y), t1, x);
+          dv[nt] = __ffma2_rn(make_float2(fk0.x, fk0.y), t0, x);
         }
         if (!inner) {   // the range starts or ends, or a page is missing, inside this warp's 32 tokens
 #pragma unroll
@@ -721,9 +719,14 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
             if (!(pv && pos + 1 >= sb && pos + 1 < se)) dv[nt].y = -INFINITY;
           }
         }
-        // ---- online softmax: the reference max moves only when the chunk max
-        //      passes it by more than 2 (log2 units), so p <= 4 and most
-        //      chunks skip the rescale ----
+        // ---- online softmax.  p = 2^d is taken at once against the current
+        //      reference max (d <= 2 in almost every chunk); the chunk max,
+        //      reduced over the lanes meanwhile, only decides whether the
+        //      reference moves (when d passes 2, so that p <= 4), in which case
+        //      the state is rescaled and p recomputed ----
+        float2 pp[4];
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) pp[nt] = make_float2(exp2f(dv[nt].x), exp2f(dv[nt].y));
         float mx = fmaxf(dv[0].x, dv[0].y);
 #pragma unroll
         for (int nt = 1; nt < 4; ++nt) mx = fmaxf(mx, fmaxf(dv[nt].x, dv[nt].y));
@@ -742,22 +745,20 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
             o[nt][0] = a.x; o[nt][1] = a.y; o[nt][2] = c.x; o[nt][3] = c.y;
           }
           m = mref + mx;
-          const float2 nmx = make_float2(-mx, -mx);
 #pragma unroll
-          for (int nt = 0; nt < 4; ++nt) dv[nt] = __fadd2_rn(dv[nt], nmx);
+          for (int nt = 0; nt < 4; ++nt) pp[nt] = make_float2(exp2f(dv[nt].x - mx), exp2f(dv[nt].y - mx));
         }
-        // ---- p, P'_blk = p d_V (the A operand, hi + lo), dmin terms ----
+        // ---- P'_blk = p d_V (the A operand, hi + lo), dmin terms ----
         uint32_t pa[2][2][4];   // [blk][kt]
 #pragma unroll
         for (int nt = 0; nt < 4; ++nt) {
-          const float2 pp = make_float2(exp2f(dv[nt].x), exp2f(dv[nt].y));
-          l2 = __fadd2_rn(l2, pp);
+          l2 = __fadd2_rn(l2, pp[nt]);
           const float4 fv0 = *reinterpret_cast<const float4*>(ftr + nt * 4 * PAIR_STRIDE + 32);   // d0 | dmin0
           const float4 fv1 = *reinterpret_cast<const float4*>(ftr + nt * 4 * PAIR_STRIDE + 48);   // d1 | dmin1
-          const float2 pv0 = __fmul2_rn(pp, make_float2(fv0.x, fv0.y));
-          const float2 pv1 = __fmul2_rn(pp, make_float2(fv1.x, fv1.y));
-          cb0 = __ffma2_rn(pp, make_float2(fv0.z, fv0.w), cb0);
-          cb1 = __ffma2_rn(pp, make_float2(fv1.z, fv1.w), cb1);
+          const float2 pv0 = __fmul2_rn(pp[nt], make_float2(fv0.x, fv0.y));
+          const float2 pv1 = __fmul2_rn(pp[nt], make_float2(fv1.x, fv1.y));
+          cb0 = __ffma2_rn(pp[nt], make_float2(fv0.z, fv0.w), cb0);
+          cb1 = __ffma2_rn(pp[nt], make_float2(fv1.z, fv1.w), cb1);
           // n-tile nt: k-step nt / 2, tokens 2 tig (+1) -> a0 / a1 (even nt) or a2 / a3 (odd nt)
           const int kt = nt >> 1, r = (nt & 1) * 2;
 #pragma unroll
