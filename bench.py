@@ -296,7 +296,7 @@ def l2_flush_buffer(torch, dev):
 
 
 def timed_graph(torch, fn, stream, steps, warmup, barrier, dist=None, world=1, dev=None, graph=True,
-                flush=None, align=None, clocks=None):
+                flush=None, align=None, clocks=None, per_rank=None):
     """CUDA-event time of fn() per call (graph replay when capture works), max over ranks.
     With `flush` (a buffer larger than L2), every timed step is preceded by a
     write of the whole buffer and then by `align` (a one-word all-reduce, so
@@ -352,6 +352,10 @@ def timed_graph(torch, fn, stream, steps, warmup, barrier, dist=None, world=1, d
         barrier()
     ms = sum(per) / len(per)
     if world > 1:
+        if per_rank is not None:   # every rank's own mean, gathered for the report
+            allv = [torch.zeros(1, device=dev) for _ in range(world)]
+            dist.all_gather(allv, torch.tensor([ms], device=dev))
+            per_rank.extend(float(v.item()) for v in allv)
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
@@ -402,11 +406,20 @@ def run_config5(A, S, torch, dev, stream, args, barrier, dist, world, rank, with
     align = (lambda: dist.all_reduce(tiny)) if world > 1 else None
     res = {}
     clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
+    ranks = {"p2p": [], "collective": [], "local": []}
     for m in ("p2p", "collective"):
         d = decs[m]
         fn = lambda d=d: d.step(q, pool, table, stream=stream)
         res[m] = timed_graph(torch, fn, stream, args.steps, args.warmup, barrier, dist, world, dev, flush=flush,
-                             align=align, clocks=clocks if m == "p2p" else None)
+                             align=align, clocks=clocks if m == "p2p" else None, per_rank=ranks[m])
+    if world > 1:
+        # the rank's own decode of its shard, merged locally, without the exchange
+        part = torch.empty(1, H, D + 2, device=dev)
+        lws = A.Q4Workspace(1, device=dev)
+        fn = lambda: A.decode_q4_partial(q, pool, table, u_begin=dec.lo, u_end=dec.hi, part=part, workspace=lws,
+                                         stream=stream)
+        res["local"] = timed_graph(torch, fn, stream, args.steps, args.warmup, barrier, dist, world, dev,
+                                   flush=flush, align=align, per_rank=ranks["local"])
     out_p2p = decs["p2p"].step(q, pool, table, stream=stream).clone()
     out_col = decs["collective"].step(q, pool, table, stream=stream).clone()
     torch.cuda.synchronize()
@@ -455,6 +468,7 @@ def run_config5(A, S, torch, dev, stream, args, barrier, dist, world, rank, with
         "host_out_matches_device": host_ok, "shard_bytes": shard_bytes, "launches_per_step": launches,
         "collective_ms": res["collective"][0], "p2p_vs_collective_max_abs": diff, "device_error": err,
         "parity": parity, "h2d": int(qh.numel() * 4), "d2h": int(oh.numel() * 4),
+        "per_rank_ms": ranks, "local_ms": res["local"][0] if "local" in res else None,
     }
 
 
@@ -945,7 +959,8 @@ def run_gpu(args, rank, world):
             "split_kv": {"timing": c5["mode"], "collective_baseline_ms_per_step": c5["collective_ms"],
                          "p2p_vs_collective_max_abs": c5["p2p_vs_collective_max_abs"],
                          "bytes_per_gpu": c5["shard_bytes"], "exchange_bytes_per_gpu": world * H * (D + 2) * 4,
-                         **c5["parity"]},
+                         "per_rank_ms": c5["per_rank_ms"],
+                         "rank_decode_alone_ms": c5["local_ms"], **c5["parity"]},
             "device_error": c5["device_error"],
         }
         line.update(extra)

@@ -238,6 +238,7 @@ struct Smem {
   int32_t warp_tot[THREADS / 32];
   int32_t flag;
   int32_t abort_;
+  uint32_t ep[ROWS];                 // exchange epochs of the rows a CTA finishes
 };
 
 __device__ __forceinline__ int seek_seq(const Smem& s, int batch, int i) {
@@ -310,6 +311,25 @@ __device__ __forceinline__ int atom_add_acq_rel(int32_t* p, int v) {
 // the warp's first page
 __device__ __forceinline__ constexpr int nt_off(int nt) { return (nt >> 1) * PAGE_BYTES + (nt & 1) * 8 * ROWB; }
 
+// (O, M, L) += (Oo, Mo, Lo): two partials (o relative to m in log2 units, l)
+__device__ __forceinline__ void merge_pair(float4& O, float& M, float& L, float4 Oo, float Mo, float Lo) {
+  if (!(Lo > 0.f)) return;
+  if (!(L > 0.f)) {
+    O = Oo;
+    M = Mo;
+    L = Lo;
+    return;
+  }
+  const float Mn = fmaxf(M, Mo);
+  const float sa = exp2f(M - Mn), sb = exp2f(Mo - Mn);
+  L = L * sa + Lo * sb;
+  O.x = O.x * sa + Oo.x * sb;
+  O.y = O.y * sa + Oo.y * sb;
+  O.z = O.z * sa + Oo.z * sb;
+  O.w = O.w * sa + Oo.w * sb;
+  M = Mn;
+}
+
 // Merge of n partials at slots first, first + stride, ... for this thread's
 // (query head r, dims d4 .. d4 + 3): o relative to M (log2), L.
 __device__ __forceinline__ void merge_slots(const Params& p, int first, int stride, int n, int r, int d4,
@@ -355,8 +375,9 @@ __device__ __forceinline__ void store_slot(const Params& p, int slot, int r, int
 
 // The result of sequence b for this thread's (query head r, dims d4 .. d4+3)
 // from its merged (O relative to M in log2 units, L): the partial, the
-// output, or the exchange with the other ranks and the combined output.
-__device__ void finish_row(const Params& p, int b, int r, int d4, float4 O, float M, float L) {
+// output, or the exchange with the other ranks (step `epoch`) and the
+// combined output.
+__device__ void finish_row(const Params& p, int b, int r, int d4, float4 O, float M, float L, uint32_t epoch) {
   const float inv = L > 0.f ? 1.0f / L : 0.f;
   const float4 o = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
   const float mnat = L > 0.f ? M * 0.6931471805599453f : -INFINITY;   // log2 -> natural units
@@ -379,9 +400,6 @@ __device__ void finish_row(const Params& p, int b, int r, int d4, float4 O, floa
   }
   // ---- exchange: this rank's row to every rank, then the ranks' rows combined ----
   const Exchange& ex = p.ex;
-  int* epochs = reinterpret_cast<int*>(ex.mbox[ex.rank]);     // [rows] steps done per row
-  const uint32_t epoch = (uint32_t)(*reinterpret_cast<volatile int*>(epochs + row)) + 1u;
-  __syncwarp();   // every lane has read the epoch before any lane can update it
   const int buf = epoch & 1;
   const size_t slot = ((size_t)(buf * MAX_RANKS + ex.rank) * ex.rows + row) * (HD + 2);
   for (int rk = 0; rk < ex.world; ++rk) {
@@ -434,8 +452,34 @@ __device__ void finish_row(const Params& p, int b, int r, int d4, float4 O, floa
   if (!ok) record_error(p.err, kErrWaitTimeout);
   const float ir = den > 0.f ? 1.0f / den : 0.f;
   *reinterpret_cast<float4*>(p.out + row * HD + d4) = make_float4(acc.x * ir, acc.y * ir, acc.z * ir, acc.w * ir);
-  __syncwarp();
-  if (d4 == 0) *reinterpret_cast<volatile int*>(epochs + row) = (int)epoch;
+}
+
+// finish_row for the rows a CTA holds, called by all consumer threads (thread
+// -> row r when `valid`); in exchange mode each row's epoch counter (in this
+// rank's mailbox header) is read before and advanced after the exchange.
+__device__ void finish_block(const Params& p, Smem& s, int b, bool valid, int r, int d4, float4 O, float M, float L) {
+  int* epochs = p.mode == kModeExchange ? reinterpret_cast<int*>(p.ex.mbox[p.ex.rank]) + (int64_t)b * ROWS : nullptr;
+  if (epochs) {
+    if (valid && d4 == 0) s.ep[r] = (uint32_t)(*reinterpret_cast<volatile int*>(epochs + r)) + 1u;
+    consumer_sync();
+  }
+  if (valid) finish_row(p, b, r, d4, O, M, L, epochs ? s.ep[r] : 0u);
+  if (epochs) {
+    consumer_sync();
+    if (valid && d4 == 0) *reinterpret_cast<volatile int*>(epochs + r) = (int)s.ep[r];
+  }
+}
+
+// Bounded wait until *c >= target (acquire at gpu scope); false on timeout.
+__device__ bool wait_count(const int32_t* c, int target, long long timeout_ns) {
+  const unsigned long long t0 = global_ns();
+  while (true) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(c) : "memory");
+    if (v >= target) return true;
+    if ((long long)(global_ns() - t0) > timeout_ns) return false;
+    __nanosleep(64);
+  }
 }
 
 __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_constant__ Params p) {
@@ -858,48 +902,76 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
         O.z = fmaf(w, os[j].z, O.z);
         O.w = fmaf(w, os[j].w, O.w);
       }
-      if (n_b == 1 && p.mode != kModeRing) finish_row(p, b, mr, md4, O, M, L);   // this CTA alone
+      if (n_b == 1 && p.mode != kModeRing) finish_block(p, s, b, true, mr, md4, O, M, L);   // this CTA alone
       else store_slot(p, blockIdx.x + b, mr, md4, O, M, L);
     }
     consumer_sync();   // partials stored (and shared partials read) before the count-in
     if (n_b > 1 && p.mode != kModeRing) {
-      // two-level count-in: groups of G consecutive CTAs, then the groups
-      const int G = n_b <= 16 ? n_b : (int)ceilf(sqrtf((float)n_b));
-      const int ngroups = (n_b + G - 1) / G;
-      const int gi = (blockIdx.x - first_b) / G;
-      const int gfirst = first_b + gi * G;
-      const int gsize = min(G, n_b - gi * G);
-      if (t == 0) {
-        const int old = atom_add_acq_rel(&p.gcnt[gfirst + b], 1);
-        const int last = old == gsize - 1;
-        if (last) atomicExch(&p.gcnt[gfirst + b], 0);
-        s.flag = last;
-      }
+      // Row-parallel merge: the last R CTAs to count in (R = the query heads, or
+      // the covering CTAs if fewer) each merge rows j, j + R, ... of the sequence
+      // once every covering CTA has counted in (all CTAs of the grid are
+      // resident, one per SM, so the wait ends; it is bounded all the same).
+      const int R = min(n_b, ROWS);
+      if (t == 0) s.flag = atom_add_acq_rel(&p.gcnt[b], 1);
       consumer_sync();
-      const int last = s.flag;
+      const int ticket = s.flag;
       consumer_sync();
-      if (last) {
-        float4 O;
-        float M, L;
-        merge_slots(p, gfirst + b, 1, gsize, mr, md4, O, M, L);
-        if (ngroups == 1) {
-          finish_row(p, b, mr, md4, O, M, L);
-        } else {
-          store_slot(p, gfirst + b, mr, md4, O, M, L);
-          consumer_sync();
-          if (t == 0) {
-            const int old = atom_add_acq_rel(&p.scnt[b], 1);
-            const int last2 = old == ngroups - 1;
-            if (last2) atomicExch(&p.scnt[b], 0);
-            s.flag = last2;
+      if (ticket >= n_b - R) {
+        const int j = ticket - (n_b - R);
+        if (t == 0 && !wait_count(&p.gcnt[b], n_b, p.mode == kModeExchange ? p.ex.timeout_ns : 2000000000LL))
+          record_error(p.err, kErrWaitTimeout);
+        consumer_sync();
+        // thread -> partial group pg = t / 16 (covering CTAs pg, pg + 32, ...), dims d4;
+        // the 32 groups are folded pairwise: lanes 16 apart by a shuffle, then a
+        // tree over the 16 warps through shared memory
+        const int pg = t >> 4, d4 = (t & 15) * 4;
+        float4* ro = reinterpret_cast<float4*>(s.wk[0]);                    // [16 warps][16] o
+        float2* rml = reinterpret_cast<float2*>(s.wk[0] + 16 * 16 * 16);     // [16 warps][16] (m, l)
+        float4* fo = reinterpret_cast<float4*>(s.wk[0] + 16 * 16 * 24);     // [rows][16] merged o
+        float2* fml = reinterpret_cast<float2*>(s.wk[0] + 16 * 16 * 24 + ROWS / 2 * 16 * 16);   // [rows][16]
+        const int nr = (ROWS - j + R - 1) / R;
+        for (int rs = 0; rs < nr; ++rs) {
+          const int r = j + rs * R;
+          float4 O;
+          float M, L;
+          merge_slots(p, first_b + b + pg, 32, n_b > pg ? (n_b - pg + 31) / 32 : 0, r, d4, O, M, L);
+          {
+            const float Mo = __shfl_xor_sync(0xffffffffu, M, 16), Lo = __shfl_xor_sync(0xffffffffu, L, 16);
+            const float4 Oo = make_float4(__shfl_xor_sync(0xffffffffu, O.x, 16), __shfl_xor_sync(0xffffffffu, O.y, 16),
+                                          __shfl_xor_sync(0xffffffffu, O.z, 16), __shfl_xor_sync(0xffffffffu, O.w, 16));
+            merge_pair(O, M, L, Oo, Mo, Lo);
+          }
+          if (lane < 16) {
+            ro[warp * 16 + lane] = O;
+            rml[warp * 16 + lane] = make_float2(M, L);
+          }
+#pragma unroll
+          for (int half = 8; half >= 1; half >>= 1) {
+            consumer_sync();
+            if (warp < half && lane < 16) {
+              const float4 Oo = ro[(warp + half) * 16 + lane];
+              const float2 mo = rml[(warp + half) * 16 + lane];
+              merge_pair(O, M, L, Oo, mo.x, mo.y);
+              ro[warp * 16 + lane] = O;
+              rml[warp * 16 + lane] = make_float2(M, L);
+            }
+          }
+          if (warp == 0 && lane < 16) {
+            fo[rs * 16 + lane] = O;
+            fml[rs * 16 + lane] = make_float2(M, L);
           }
           consumer_sync();
-          const int last2 = s.flag;
-          consumer_sync();
-          if (last2) {
-            merge_slots(p, first_b + b, G, ngroups, mr, md4, O, M, L);
-            finish_row(p, b, mr, md4, O, M, L);
-          }
+        }
+        // thread -> merged row slot rs = t / 16 (row j + rs R), dims d4
+        const int rs = t >> 4;
+        const bool valid = rs < nr;
+        const float2 ml = valid ? fml[rs * 16 + (t & 15)] : make_float2(-INFINITY, 0.f);
+        finish_block(p, s, b, valid, valid ? j + rs * R : 0, d4, valid ? fo[rs * 16 + (t & 15)] : make_float4(0.f, 0.f, 0.f, 0.f),
+                     ml.x, ml.y);
+        consumer_sync();
+        if (t == 0 && atom_add_acq_rel(&p.scnt[b], 1) == R - 1) {   // the last merger resets the counters
+          atomicExch(&p.gcnt[b], 0);
+          atomicExch(&p.scnt[b], 0);
         }
       }
     }
@@ -909,7 +981,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
   if (blockIdx.x == 0 && p.mode != kModeRing) {
     for (int b = 0; b < p.batch; ++b)
       if (s.prefix[b + 1] == s.prefix[b])
-        finish_row(p, b, mr, md4, make_float4(0.f, 0.f, 0.f, 0.f), -INFINITY, 0.f);
+        finish_block(p, s, b, true, mr, md4, make_float4(0.f, 0.f, 0.f, 0.f), -INFINITY, 0.f);
   }
 }
 
