@@ -74,6 +74,33 @@ int32_t nyion_attn_workspace_reset(void* workspace, size_t bytes, void* stream);
 int32_t nyion_attn_host_map(const void* host, void** device_ptr);
 int32_t nyion_attn_copy_async(void* dst, const void* src, size_t bytes, void* stream);
 
+/* ------------------------------------------------------ HBM arena ---------
+ * The device side of HeterogeneousMemoryAllocator: the five operations of the
+ * reference's DeviceAllocator trait (swamp-tensors/src/hma.rs:215-221;
+ * implemented for Vulkan in swamp-gpu/src/lib.rs:101-150), from which the KV
+ * page pools, page tables and per-step buffers are carved.
+ * nyion_attn_arena_create reserves `capacity` bytes of HBM on the current
+ * device with one cudaMalloc; allocate_device carves 256-byte-aligned blocks
+ * from it (best fit; freed blocks coalesce), so allocating and freeing pages
+ * calls neither cudaMalloc nor cudaFree.  allocate_unified returns managed
+ * memory (host- and device-addressable; the reference's UnifiedMapped).
+ * Allocations are named by a handle; *dev_ptr / *ptr is the device address
+ * the attention entry points take.  upload / download copy min(bytes, size)
+ * bytes between host memory and the allocation's start (synchronous for a
+ * NULL stream, else on `stream`), as the reference's upload / download copy
+ * min(src, dst) bytes.  No free range large enough: NYION_ERR_WORKSPACE (the
+ * reference's None).  Unknown handle: NYION_ERR_INVALID.  Thread-safe.
+ * nyion_attn_arena_info reports the reservation, the bytes in live device
+ * blocks and the largest free range. */
+int32_t nyion_attn_arena_create(size_t capacity, void** arena);
+int32_t nyion_attn_arena_destroy(void* arena);
+int32_t nyion_attn_arena_allocate_device(void* arena, size_t size, uint64_t* handle, void** dev_ptr);
+int32_t nyion_attn_arena_allocate_unified(void* arena, size_t size, uint64_t* handle, void** ptr);
+int32_t nyion_attn_arena_free(void* arena, uint64_t handle);
+int32_t nyion_attn_arena_upload(void* arena, uint64_t handle, const void* src, size_t bytes, void* stream);
+int32_t nyion_attn_arena_download(void* arena, uint64_t handle, void* dst, size_t bytes, void* stream);
+int32_t nyion_attn_arena_info(void* arena, size_t* capacity, size_t* used, size_t* largest_free);
+
 /* ---------------------------------------------------- paged fp32 decode ----
  * GQA decode attention with online softmax over an fp32 paged KV pool, one
  * query token per sequence.  Replaces the per-head score/softmax/AXPY loops

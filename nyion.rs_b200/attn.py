@@ -44,6 +44,14 @@ def lib() -> C.CDLL:
             "nyion_attn_workspace_reset": (i32, [vp, sz, vp]),
             "nyion_attn_host_map": (i32, [vp, C.POINTER(vp)]),
             "nyion_attn_copy_async": (i32, [vp, vp, sz, vp]),
+            "nyion_attn_arena_create": (i32, [sz, C.POINTER(vp)]),
+            "nyion_attn_arena_destroy": (i32, [vp]),
+            "nyion_attn_arena_allocate_device": (i32, [vp, sz, C.POINTER(C.c_uint64), C.POINTER(vp)]),
+            "nyion_attn_arena_allocate_unified": (i32, [vp, sz, C.POINTER(C.c_uint64), C.POINTER(vp)]),
+            "nyion_attn_arena_free": (i32, [vp, C.c_uint64]),
+            "nyion_attn_arena_upload": (i32, [vp, C.c_uint64, vp, sz, vp]),
+            "nyion_attn_arena_download": (i32, [vp, C.c_uint64, vp, sz, vp]),
+            "nyion_attn_arena_info": (i32, [vp, C.POINTER(sz), C.POINTER(sz), C.POINTER(sz)]),
             "nyion_attn_decode_paged_f32": (i32, [vp, vp, i64, vp, i32, vp, vp, i32, i32, i32, i32,
                                                   i32, f32, vp, sz, vp]),
             "nyion_attn_decode_zoned_f32": (i32, [vp, vp, vp, vp, i64, i32, i32, i64, i64, i32, i32,
@@ -194,6 +202,47 @@ def copy_async(dst, src, stream=None, dst_addr: int | None = None, src_addr: int
                                       _stream_ptr(stream)))
 
 
+class Arena:
+    """The HBM arena (nyion_attn_arena_*): the device side of the reference's
+    HeterogeneousMemoryAllocator.  allocate() returns (handle, device address);
+    upload / download move bytes between host numpy arrays and an allocation
+    (synchronously unless a stream is given)."""
+
+    def __init__(self, capacity: int):
+        ptr = C.c_void_p()
+        check(lib().nyion_attn_arena_create(capacity, C.byref(ptr)))
+        self.ptr = ptr.value
+
+    def allocate(self, size: int, unified: bool = False) -> tuple[int, int]:
+        h, p = C.c_uint64(), C.c_void_p()
+        fn = lib().nyion_attn_arena_allocate_unified if unified else lib().nyion_attn_arena_allocate_device
+        check(fn(self.ptr, size, C.byref(h), C.byref(p)))
+        return int(h.value), int(p.value)
+
+    def free(self, handle: int) -> None:
+        check(lib().nyion_attn_arena_free(self.ptr, handle))
+
+    def upload(self, handle: int, data, stream=None) -> None:
+        import numpy as np
+        buf = np.ascontiguousarray(data)
+        check(lib().nyion_attn_arena_upload(self.ptr, handle, buf.ctypes.data, buf.nbytes,
+                                            _stream_ptr(stream) if stream is not None else None))
+
+    def download(self, handle: int, out, stream=None) -> None:
+        check(lib().nyion_attn_arena_download(self.ptr, handle, out.ctypes.data, out.nbytes,
+                                              _stream_ptr(stream) if stream is not None else None))
+
+    def info(self) -> tuple[int, int, int]:
+        c, u, f = C.c_size_t(), C.c_size_t(), C.c_size_t()
+        check(lib().nyion_attn_arena_info(self.ptr, C.byref(c), C.byref(u), C.byref(f)))
+        return int(c.value), int(u.value), int(f.value)
+
+    def close(self) -> None:
+        if self.ptr:
+            check(lib().nyion_attn_arena_destroy(self.ptr))
+            self.ptr = None
+
+
 class Workspace:
     """Device workspace for the decode entry points (zeroed once)."""
 
@@ -242,15 +291,15 @@ def _zone_pages(k_arena, n_layers: int, n_kv: int, D: int) -> int:
 
 
 def decode_zoned_f32(q, k_arena, v_arena, n_layers: int, layer: int, seq_len: int, q_pos: int,
-                     out=None, stream=None):
+                     out=None, stream=None, n_kv: int | None = None):
     """ops::attention over reference-layout zone pages (nyion_attn_decode_zoned_f32).
 
     q [H, D] f32; k_arena / v_arena: flat f32 arenas holding consecutive zone
-    pages [n_layers][n_kv][slots][D]; returns out [H, D].
+    pages [n_layers][n_kv][slots][D]; returns out [H, D].  n_kv defaults to H / 8.
     """
     torch = _torch()
     H, D = q.shape
-    n_kv = H // 8
+    n_kv = n_kv or H // 8
     if out is None:
         out = torch.empty_like(q)
     check(lib().nyion_attn_decode_zoned_f32(_ptr(out), _ptr(q), _ptr(k_arena), _ptr(v_arena),

@@ -32,6 +32,32 @@ int32_t run(const float* q, const void* k, const void* v, int64_t stride, int se
             const int32_t* d_seq_len, int window, float* out, int n_heads, int n_kv, int head_dim,
             float scale, void* ws, size_t ws_bytes, cudaStream_t stream) {
   if (!q || !k || !v || !out) return fail(NYION_ERR_INVALID, "f16 decode: null pointer argument");
+  if (!(head_dim == HD && n_kv > 0 && n_heads == n_kv * GROUP) && generic_shape_ok(n_heads, n_kv, head_dim)) {
+    const int max_tokens = d_seq_len ? window : seq_len;
+    if (max_tokens <= 0 || stride < max_tokens)
+      return fail(NYION_ERR_INVALID, "f16 decode: length %d must be in [1, stride=%lld]", max_tokens,
+                  (long long)stride);
+    GenericCall c;
+    c.who = "f16 decode";
+    c.q = q;
+    c.k = k;
+    c.v = v;
+    c.n_heads = n_heads;
+    c.n_kv = n_kv;
+    c.head_dim = head_dim;
+    c.rows = 1;
+    c.u_begin = 0;
+    c.u_end = seq_len;
+    c.d_len = d_seq_len;
+    c.window = window;
+    c.stride = stride;
+    c.scale = scale;
+    c.out = out;
+    c.max_tokens = max_tokens;
+    c.fmt = kGenF16;
+    c.layout = kGenRows;
+    return generic_decode(c, stream);
+  }
   if (head_dim != HD || n_kv <= 0 || n_heads != n_kv * GROUP)
     return fail(NYION_ERR_UNSUPPORTED, "f16 decode: this build takes head_dim 64 and GQA group 8 (got %d, %d/%d)",
                 head_dim, n_heads, n_kv);

@@ -611,6 +611,10 @@ int32_t pool_map(CUtensorMap* m, const float* pool, int64_t n_blocks) {
                      CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+bool specialised(int32_t n_heads, int32_t n_kv_heads, int32_t head_dim) {
+  return head_dim == HD && n_kv_heads > 0 && n_heads == n_kv_heads * GROUP;
+}
+
 int32_t check_common(int32_t n_heads, int32_t n_kv_heads, int32_t head_dim) {
   if (n_kv_heads <= 0 || n_heads <= 0 || n_heads % n_kv_heads)
     return fail(NYION_ERR_INVALID, "n_heads (%d) must be a positive multiple of n_kv_heads (%d)",
@@ -787,6 +791,33 @@ extern "C" int32_t nyion_attn_decode_paged_f32(const float* q, const float* kv_p
                                                int32_t n_kv_heads, int32_t head_dim,
                                                int32_t page_tokens, float scale, void* workspace,
                                                size_t workspace_bytes, void* stream) {
+  if (!specialised(n_heads, n_kv_heads, head_dim) && generic_shape_ok(n_heads, n_kv_heads, head_dim)) {
+    // other shapes: the generic kernel (library-owned workspace)
+    if (!q || !kv_pool || !page_table || !seq_lens || !out)
+      return fail(NYION_ERR_INVALID, "decode_paged_f32: null pointer argument");
+    if (batch <= 0 || max_pages <= 0 || n_pool_pages <= 0)
+      return fail(NYION_ERR_INVALID, "decode_paged_f32: batch, max_pages and n_pool_pages must be > 0");
+    if (page_tokens != PAGE)
+      return fail(NYION_ERR_UNSUPPORTED, "decode_paged_f32: page_tokens must be 16 (got %d)", page_tokens);
+    GenericCall c;
+    c.who = "decode_paged_f32";
+    c.q = q;
+    c.k = kv_pool;
+    c.table = page_table;
+    c.max_pages = max_pages;
+    c.n_pool_pages = n_pool_pages;
+    c.n_heads = n_heads;
+    c.n_kv = n_kv_heads;
+    c.head_dim = head_dim;
+    c.rows = batch;
+    c.lens = seq_lens;
+    c.scale = scale;
+    c.out = out;
+    c.max_tokens = (int64_t)max_pages * PAGE;
+    c.fmt = kGenF32;
+    c.layout = kGenPaged;
+    return generic_decode(c, static_cast<cudaStream_t>(stream));
+  }
   int32_t st = check_common(n_heads, n_kv_heads, head_dim);
   if (st) return st;
   if (!q || !kv_pool || !page_table || !seq_lens || !out)
@@ -849,7 +880,8 @@ extern "C" int32_t nyion_attn_decode_zoned_f32(float* out, const float* q, const
                                                int64_t seq_len, int64_t q_pos, int32_t n_heads,
                                                int32_t n_kv_heads, int32_t head_dim,
                                                void* stream) {
-  int32_t st = check_common(n_heads, n_kv_heads, head_dim);
+  const bool generic = !specialised(n_heads, n_kv_heads, head_dim) && generic_shape_ok(n_heads, n_kv_heads, head_dim);
+  int32_t st = generic ? NYION_OK : check_common(n_heads, n_kv_heads, head_dim);
   if (st) return st;
   if (!out || !q || !k_arena || !v_arena)
     return fail(NYION_ERR_INVALID, "decode_zoned_f32: null pointer argument");
@@ -859,6 +891,27 @@ extern "C" int32_t nyion_attn_decode_zoned_f32(float* out, const float* q, const
   // ops.rs:183 valid_end = min(q_pos, seq_len - 1): tokens [0, valid_end] are attended
   int64_t valid_end = q_pos < seq_len - 1 ? q_pos : seq_len - 1;
   if (valid_end + 1 > (1ll << 30)) return fail(NYION_ERR_INVALID, "decode_zoned_f32: context too long");
+  if (generic) {
+    GenericCall c;
+    c.who = "decode_zoned_f32";
+    c.q = q;
+    c.k = k_arena;
+    c.v = v_arena;
+    c.n_heads = n_heads;
+    c.n_kv = n_kv_heads;
+    c.head_dim = head_dim;
+    c.rows = 1;
+    c.u_begin = 0;
+    c.u_end = (int32_t)(valid_end + 1);
+    c.n_layers = n_layers;
+    c.layer = layer_idx;
+    c.n_pages = n_arena_pages;
+    c.out = out;
+    c.max_tokens = valid_end + 1;
+    c.fmt = kGenF32;
+    c.layout = kGenZoned;
+    return generic_decode(c, static_cast<cudaStream_t>(stream));
+  }
   if (valid_end + 1 <= zoned_small_max())
     return zoned_small(out, q, k_arena, v_arena, n_arena_pages, n_layers, layer_idx, valid_end + 1, n_kv_heads,
                        head_dim, nullptr, stream);
@@ -872,11 +925,31 @@ extern "C" int32_t nyion_attn_decode_zoned_f32(float* out, const float* q, const
 static int32_t contig_decode(const float* d_q, const float* d_k, const float* d_v, float* d_out,
                              int n_heads, int n_kv_heads, int seq_len, int head_dim, int kv_stride,
                              void* ws, cudaStream_t stream) {
-  int32_t st = check_common(n_heads, n_kv_heads, head_dim);
+  const bool generic = !specialised(n_heads, n_kv_heads, head_dim) && generic_shape_ok(n_heads, n_kv_heads, head_dim);
+  int32_t st = generic ? NYION_OK : check_common(n_heads, n_kv_heads, head_dim);
   if (st) return st;
   if (!d_q || !d_k || !d_v || !d_out) return fail(NYION_ERR_INVALID, "null pointer argument");
   if (seq_len <= 0 || kv_stride < seq_len)
     return fail(NYION_ERR_INVALID, "seq_len %d must be in [1, kv_stride=%d]", seq_len, kv_stride);
+  if (generic) {
+    GenericCall c;
+    c.who = "gpu_attention";
+    c.q = d_q;
+    c.k = d_k;
+    c.v = d_v;
+    c.n_heads = n_heads;
+    c.n_kv = n_kv_heads;
+    c.head_dim = head_dim;
+    c.rows = 1;
+    c.u_begin = 0;
+    c.u_end = seq_len;
+    c.stride = kv_stride;
+    c.out = d_out;
+    c.max_tokens = seq_len;
+    c.fmt = kGenF32;
+    c.layout = kGenRows;
+    return generic_decode(c, stream);
+  }
   const float sl2 = (1.0f / sqrtf((float)head_dim)) * 1.4426950408889634f;
   return contig_rows_f32(d_q, d_k, d_v, d_out, n_kv_heads, kv_stride, seq_len, sl2, ws,
                          ws ? contig_workspace_bytes(n_kv_heads, seq_len) : 0, stream);

@@ -1173,33 +1173,37 @@ __global__ void __launch_bounds__(256) q4_reduce_ring_kernel(const float* __rest
 // ============================================================================
 // log-sum-exp combine: parts [G][rows][HD+2] -> out [rows][HD]
 // ============================================================================
+template <int D>
 __global__ void lse_combine_kernel(const float* __restrict__ parts, int G, int64_t rows,
                                    float* __restrict__ out) {
+  // 16 threads per row, D / 16 dims each
+  constexpr int PER = D / 16;
   const int64_t r = (int64_t)blockIdx.x * (blockDim.x / 16) + (threadIdx.x >> 4);
-  const int d4 = (threadIdx.x & 15) * 4;
+  const int d0 = (threadIdx.x & 15) * PER;
   if (r >= rows) return;
   float M = -INFINITY;
   for (int gi = 0; gi < G; ++gi) {
-    const float* pp = parts + ((int64_t)gi * rows + r) * (HD + 2);
-    if (pp[HD + 1] > 0.f) M = fmaxf(M, pp[HD]);
+    const float* pp = parts + ((int64_t)gi * rows + r) * (D + 2);
+    if (pp[D + 1] > 0.f) M = fmaxf(M, pp[D]);
   }
   float den = 0.f;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float acc[PER];
+#pragma unroll
+  for (int j = 0; j < PER; ++j) acc[j] = 0.f;
   if (M != -INFINITY) {
     for (int gi = 0; gi < G; ++gi) {
-      const float* pp = parts + ((int64_t)gi * rows + r) * (HD + 2);
-      const float lg = pp[HD + 1];
+      const float* pp = parts + ((int64_t)gi * rows + r) * (D + 2);
+      const float lg = pp[D + 1];
       if (!(lg > 0.f)) continue;
-      const float w = lg * expf(pp[HD] - M);
+      const float w = lg * expf(pp[D] - M);
       den += w;
-      acc.x = fmaf(w, pp[d4], acc.x);
-      acc.y = fmaf(w, pp[d4 + 1], acc.y);
-      acc.z = fmaf(w, pp[d4 + 2], acc.z);
-      acc.w = fmaf(w, pp[d4 + 3], acc.w);
+#pragma unroll
+      for (int j = 0; j < PER; ++j) acc[j] = fmaf(w, pp[d0 + j], acc[j]);
     }
   }
   const float inv = den > 0.f ? 1.0f / den : 0.f;
-  *reinterpret_cast<float4*>(out + r * HD + d4) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+#pragma unroll
+  for (int j = 0; j < PER; ++j) out[r * D + d0 + j] = acc[j] * inv;
 }
 
 size_t smem_bytes() { return sizeof(Smem); }
@@ -1226,6 +1230,10 @@ WsLayout ws_layout(int batch) {
 }
 
 size_t counter_bytes() { return ws_layout(1).meta; }
+
+bool specialised(int32_t n_heads, int32_t n_kv_heads, int32_t head_dim) {
+  return n_kv_heads == NKV && n_heads == NKV * GROUP && head_dim == HD;
+}
 
 int32_t check_shape(int32_t n_heads, int32_t n_kv_heads, int32_t head_dim) {
   if (n_kv_heads != NKV || n_heads != NKV * GROUP || head_dim != HD)
@@ -1332,6 +1340,36 @@ extern "C" int32_t nyion_attn_decode_q4_partial(const float* q, const uint8_t* k
                                                 int32_t head_dim, int32_t page_tokens, float scale,
                                                 void* workspace, size_t workspace_bytes,
                                                 void* stream) {
+  if (!specialised(n_heads, n_kv_heads, head_dim) && generic_shape_ok(n_heads, n_kv_heads, head_dim)) {
+    // other shapes: the generic kernel over the 4-bit pool [pages][n_kv][K|V][16][head_dim / 32 * 20]
+    if (!q || !kv_pool || !page_table || !part)
+      return fail(NYION_ERR_INVALID, "decode_q4_partial: null pointer argument");
+    if (page_tokens != PAGE) return fail(NYION_ERR_UNSUPPORTED, "decode_q4_partial: page_tokens must be 16");
+    if (batch <= 0 || max_pages <= 0 || n_pool_pages <= 0)
+      return fail(NYION_ERR_INVALID, "decode_q4_partial: batch, max_pages, n_pool_pages must be > 0");
+    GenericCall c;
+    c.who = "decode_q4_partial";
+    c.q = q;
+    c.k = kv_pool;
+    c.table = page_table;
+    c.max_pages = max_pages;
+    c.n_pool_pages = n_pool_pages;
+    c.n_heads = n_heads;
+    c.n_kv = n_kv_heads;
+    c.head_dim = head_dim;
+    c.rows = batch;
+    c.tok_begin = tok_begin;
+    c.tok_end = tok_end;
+    c.u_begin = u_begin;
+    c.u_end = u_end;
+    c.scale = scale;
+    c.part_mode = 1;
+    c.out = part;
+    c.max_tokens = (int64_t)max_pages * PAGE;
+    c.fmt = kGenQ4;
+    c.layout = kGenPaged;
+    return generic_decode(c, static_cast<cudaStream_t>(stream));
+  }
   int32_t st = check_shape(n_heads, n_kv_heads, head_dim);
   if (st) return st;
   if (!q || !kv_pool || !page_table || !part)
@@ -1362,9 +1400,12 @@ extern "C" int32_t nyion_attn_lse_combine(const float* parts, int32_t n_parts, i
                                           int32_t head_dim, float* out, void* stream) {
   if (!parts || !out || n_parts <= 0 || rows <= 0)
     return fail(NYION_ERR_INVALID, "lse_combine: bad arguments");
-  if (head_dim != HD) return fail(NYION_ERR_UNSUPPORTED, "lse_combine: head_dim must be 64");
-  lse_combine_kernel<<<(unsigned)((rows + 15) / 16), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      parts, n_parts, rows, out);
+  if (head_dim != 64 && head_dim != 128) return fail(NYION_ERR_UNSUPPORTED, "lse_combine: head_dim must be 64 or 128");
+  const unsigned grid = (unsigned)((rows + 15) / 16);
+  if (head_dim == 64)
+    lse_combine_kernel<64><<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(parts, n_parts, rows, out);
+  else
+    lse_combine_kernel<128><<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(parts, n_parts, rows, out);
   return check_cuda(cudaGetLastError(), "lse_combine launch");
 }
 
@@ -1464,6 +1505,33 @@ extern "C" int32_t nyion_attn_decode_q4_splitkv(
     int32_t n_kv_heads, int32_t head_dim, int32_t page_tokens, float scale, void* const* mailboxes,
     int32_t world, int32_t rank, int32_t timeout_ms, void* workspace, size_t workspace_bytes,
     void* stream) {
+  if (!specialised(n_heads, n_kv_heads, head_dim) && generic_shape_ok(n_heads, n_kv_heads, head_dim) && world == 1) {
+    // other shapes on one rank: the generic kernel's merged rows are the output
+    if (!q || !kv_pool || !page_table || !out)
+      return fail(NYION_ERR_INVALID, "decode_q4_splitkv: null pointer argument");
+    if (page_tokens != PAGE) return fail(NYION_ERR_UNSUPPORTED, "decode_q4_splitkv: page_tokens must be 16");
+    if (batch <= 0 || max_pages <= 0 || n_pool_pages <= 0 || rank != 0)
+      return fail(NYION_ERR_INVALID, "decode_q4_splitkv: bad sizes or rank");
+    GenericCall c;
+    c.who = "decode_q4_splitkv";
+    c.q = q;
+    c.k = kv_pool;
+    c.table = page_table;
+    c.max_pages = max_pages;
+    c.n_pool_pages = n_pool_pages;
+    c.n_heads = n_heads;
+    c.n_kv = n_kv_heads;
+    c.head_dim = head_dim;
+    c.rows = batch;
+    c.u_begin = u_begin;
+    c.u_end = u_end;
+    c.scale = scale;
+    c.out = out;
+    c.max_tokens = (int64_t)max_pages * PAGE;
+    c.fmt = kGenQ4;
+    c.layout = kGenPaged;
+    return generic_decode(c, static_cast<cudaStream_t>(stream));
+  }
   int32_t st = check_shape(n_heads, n_kv_heads, head_dim);
   if (st) return st;
   if (!q || !kv_pool || !page_table || !out || !mailboxes)

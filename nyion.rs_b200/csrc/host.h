@@ -117,6 +117,42 @@ int32_t contig_zoned_f32(const float* q, const float* k_arena, const float* v_ar
 // (decode_q4.cu): zero before the first call, left at zero by every call.
 size_t q4_counter_bytes();
 
+// Decode for the shapes the specialised kernels do not take (decode_generic.cu):
+// head_dim 64 or 128, 1 to 8 query heads per KV head, any number of KV heads.
+enum GenFormat : int32_t { kGenF32 = 0, kGenF16 = 1, kGenBF16 = 2, kGenQ4 = 3 };
+enum GenLayout : int32_t { kGenPaged = 0, kGenRows = 1, kGenZoned = 2 };
+struct GenericCall {
+  const char* who = "decode";
+  const void* q = nullptr;          // [rows][n_heads][head_dim] f32 (bf16 when q_bf16)
+  int32_t q_bf16 = 0;
+  const void* k = nullptr;          // paged: the pool; rows / zoned: K
+  const void* v = nullptr;          // rows / zoned: V
+  const int32_t* table = nullptr;   // paged: [rows][max_pages], or one row shared by all rows
+  int32_t table_shared = 0, max_pages = 0;
+  int64_t n_pool_pages = 0;
+  int32_t n_heads = 0, n_kv = 0, head_dim = 0, rows = 0;
+  // attended tokens of row b: [0, lens[b]); [tok_begin[b], tok_end[b]) or [u_begin, u_end);
+  // causal_base >= 0: [0, causal_base + b + 1); d_len: [0, min(*d_len, window))
+  const int32_t* lens = nullptr;
+  const int32_t* tok_begin = nullptr;
+  const int32_t* tok_end = nullptr;
+  int32_t u_begin = 0, u_end = 0;
+  int64_t causal_base = -1;
+  const int32_t* d_len = nullptr;
+  int32_t window = 0;
+  int64_t stride = 0;               // rows layout: tokens per KV head
+  int32_t n_layers = 0, layer = 0;  // zoned layout
+  int64_t n_pages = 0;              // zoned: arena pages
+  float scale = 0.f;                // <= 0: 1 / sqrt(head_dim)
+  int32_t part_mode = 0;            // 0: out [rows][H][hd]; 1: [rows][H][hd + 2] (o / l, m natural, l)
+  float* out = nullptr;
+  int64_t max_tokens = 0;           // bound on any row's attended tokens (sizes the splits)
+  int32_t fmt = kGenF32, layout = kGenPaged;
+};
+bool generic_shape_ok(int n_heads, int n_kv_heads, int head_dim);
+// Uses the library-owned workspace (allocated on first use: not under stream capture).
+int32_t generic_decode(const GenericCall& c, cudaStream_t stream);
+
 // Handle behind gpu_graph_create_attention[_half]: the instantiated graph
 // and the workspace it owns (freed by gpu_graph_destroy).
 struct AttnGraph {

@@ -582,6 +582,36 @@ extern "C" int32_t nyion_attn_prefill_paged_bf16(const void* q, const void* kv_p
                                                  void* stream) {
   if (!q || !kv_pool || !page_table || !out)
     return fail(NYION_ERR_INVALID, "prefill_paged_bf16: null pointer argument");
+  if (!(head_dim == HD && n_kv_heads > 0 && n_heads == n_kv_heads * GROUP) &&
+      generic_shape_ok(n_heads, n_kv_heads, head_dim)) {
+    // other shapes: the reference's loop (executor.rs:106-138) as one launch of the
+    // generic decode, query position i attending the q_start + i + 1 tokens before it
+    if (page_tokens != PAGE) return fail(NYION_ERR_UNSUPPORTED, "prefill_paged_bf16: page_tokens must be 16");
+    if (n_q <= 0 || q_start < 0 || max_pages <= 0 || n_pool_pages <= 0 || n_q > (1ll << 30))
+      return fail(NYION_ERR_INVALID, "prefill_paged_bf16: bad sizes");
+    if ((q_start + n_q + PAGE - 1) / PAGE > max_pages)
+      return fail(NYION_ERR_INVALID, "prefill_paged_bf16: page table shorter than the context");
+    GenericCall c;
+    c.who = "prefill_paged_bf16";
+    c.q = q;
+    c.q_bf16 = 1;
+    c.k = kv_pool;
+    c.table = page_table;
+    c.table_shared = 1;
+    c.max_pages = max_pages;
+    c.n_pool_pages = n_pool_pages;
+    c.n_heads = n_heads;
+    c.n_kv = n_kv_heads;
+    c.head_dim = head_dim;
+    c.rows = (int32_t)n_q;
+    c.causal_base = q_start;
+    c.scale = scale;
+    c.out = out;
+    c.max_tokens = q_start + n_q;
+    c.fmt = kGenBF16;
+    c.layout = kGenPaged;
+    return generic_decode(c, static_cast<cudaStream_t>(stream));
+  }
   if (head_dim != HD || n_kv_heads <= 0 || n_heads != n_kv_heads * GROUP)
     return fail(NYION_ERR_UNSUPPORTED,
                 "prefill_paged_bf16: this build takes head_dim 64 and GQA group 8 (got %d, %d/%d)",

@@ -167,8 +167,11 @@ def test_unsupported_shape_is_an_error(cuda_device):
     L = A.lib()
     x = torch.zeros(16, device=cuda_device)
     rc = L.gpu_attention_device(x.data_ptr(), x.data_ptr(), x.data_ptr(), x.data_ptr(),
-                                4, 4, 1, 128, 1)
+                                4, 4, 1, 96, 1)                   # head_dim 96: neither 64 nor 128
     assert rc == -1 and "head_dim" in A.last_error()
+    rc = L.gpu_attention_device(x.data_ptr(), x.data_ptr(), x.data_ptr(), x.data_ptr(),
+                                64, 4, 1, 64, 1)                  # 16 query heads per KV head
+    assert rc == -1
 
 
 @pytest.mark.parametrize("ctx,qpos,prior", [(1, 0, 0.0), (128, 127, 0.0), (300, 200, 0.5), (512, 511, 0.0),

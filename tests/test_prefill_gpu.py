@@ -106,7 +106,7 @@ def test_prefill_bad_page_id_sets_device_error(cuda_device):
 def test_prefill_rejects_unsupported(cuda_device):
     pool = torch.zeros(4, 4, 2, PT, D, dtype=torch.bfloat16, device=cuda_device)
     table = torch.arange(4, dtype=torch.int32, device=cuda_device)
-    q = torch.zeros(10, 16, D, dtype=torch.bfloat16, device=cuda_device)   # group 4
+    q = torch.zeros(10, 64, D, dtype=torch.bfloat16, device=cuda_device)   # group 16
     with pytest.raises(A.NyionError):
         A.prefill_paged_bf16(q, pool, table, 0)
     q = torch.zeros(100, 32, D, dtype=torch.bfloat16, device=cuda_device)  # context > table
