@@ -327,6 +327,10 @@ def timed_graph(torch, fn, stream, steps, warmup, barrier, dist=None, world=1, d
         torch.cuda.synchronize()
         barrier()
         with clocks if clocks is not None else contextlib.nullcontext():
+            # a ~20 ms spin kernel first, so that the host has queued every timed
+            # step before the device reaches the first event: no host-side delay
+            # (the clock sampler starting, the interpreter) can fall inside a step
+            torch.cuda._sleep(40_000_000)
             if flush is None:
                 e0 = torch.cuda.Event(enable_timing=True)
                 e1 = torch.cuda.Event(enable_timing=True)

@@ -142,22 +142,25 @@ __global__ void dequant_kernel(const uint8_t* __restrict__ src, float* __restric
 // Q4 paged decode with the split-KV merge (and the rank exchange) in-launch
 // ============================================================================
 
-constexpr int STAGE_SHIFT = 3;
-constexpr int STAGES = 1 << STAGE_SHIFT;   // 20 KB each
-constexpr int GROUPS = 2;               // consumer groups: stage s is consumed by group s % GROUPS
-constexpr int NCW = GROUPS * NKV * 2;   // 16 consumer warps: group x KV head x 32-token half
-constexpr int NCT = NCW * 32;           // 512 consumer threads
+#ifndef NYION_Q4_GROUPS
+#define NYION_Q4_GROUPS 2
+#endif
+constexpr int GROUPS = NYION_Q4_GROUPS; // consumer groups: stage s is consumed by group s % GROUPS
+constexpr int STAGES = GROUPS == 2 ? 8 : 6;   // 20 KB each
+constexpr int NCW = GROUPS * NKV * 2;   // consumer warps: group x KV head x 32-token half
+constexpr int NCT = NCW * 32;           // consumer threads
 constexpr int THREADS = NCT + 32;       // + the producer warp
 constexpr int MAX_SEQS = 512;
 constexpr int MAX_GRID = 1024;
 constexpr int RING = 32;                // chunks whose page ids the producer stages ahead
 constexpr int PAIR_STRIDE = 80;         // bytes per token pair of a warp's factor table (64 + 16)
 constexpr int ROWS = NKV * GROUP;       // query heads of a sequence
+constexpr int MT = ROWS * 16;           // threads of the merge mapping (16 per query head)
 constexpr int CP = HD + 4;              // floats per row of a CTA partial: o[64], m, l, 2 unused
 constexpr int WK_BYTES = GROUP * CP * 4;   // per-warp region: factor table, then the segment partial
 static_assert(16 * PAIR_STRIDE <= WK_BYTES, "the factor table fits the per-warp region");
 static_assert(STAGES % GROUPS == 0, "a stage must always be consumed by the same warps");
-static_assert(NCT == ROWS * 16, "merge mapping: 16 threads per query head, 4 dims each");
+static_assert(MT == ROWS * 16 && NCT >= MT, "merge mapping: 16 threads per query head, 4 dims each");
 
 enum : int32_t { kModePart = 0, kModeFinal = 1, kModeExchange = 2, kModeRing = 3 };
 
@@ -216,7 +219,7 @@ struct Params {
   float* part;                 // kModePart: [batch][H][HD + 2] (o / l, m natural log, l)
   float* out;                  // kModeFinal, kModeExchange: [batch][H][HD]
   float* cta_part;             // [MAX_GRID + batch][ROWS][CP]: o (relative to m), m (log2), l
-  int32_t* gcnt;               // [MAX_GRID + MAX_SEQS] group counters (zero between calls)
+  int32_t* gcnt;               // [MAX_GRID + MAX_SEQS]: arrivals [b], merge tickets [MAX_SEQS + b] (zero between calls)
   int32_t* scnt;               // [MAX_SEQS] sequence counters (zero between calls)
   int32_t* meta;               // kModeRing: [batch][2] first and last CTA covering sequence b
   int32_t* err;
@@ -572,13 +575,13 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
         rows_start(job, s, p, begin + k + RING + lane, end);
       }
       bool ok = true;
-      if (k >= STAGES) ok = mbar_wait_bounded(&s.empty[stage], (uint32_t)(((k >> STAGE_SHIFT) - 1) & 1));
+      if (k >= STAGES) ok = mbar_wait_bounded(&s.empty[stage], (uint32_t)((k / STAGES - 1) & 1));
       if (!__all_sync(0xffffffffu, ok)) {
         record_error(p.err, kErrWaitTimeout);
         if (lane == 0) {
           atomicExch(&s.abort_, 1);
           for (int c = k - 1; c >= 0 && c >= k - STAGES; --c)
-            mbar_wait_bounded(&s.full[c & (STAGES - 1)], (uint32_t)((c >> STAGE_SHIFT) & 1));
+            mbar_wait_bounded(&s.full[c % STAGES], (uint32_t)((c / STAGES) & 1));
         }
         return;
       }
@@ -602,7 +605,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
                       PAGE_BYTES, &s.full[stage]);
       }
       __syncwarp();
-      stage = (stage + 1) & (STAGES - 1);
+      stage = stage + 1 == STAGES ? 0 : stage + 1;
     }
     return;
   }
@@ -684,12 +687,12 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
     float m = -INFINITY;   // reference max (log2 units) of head g
 
     int k = i - begin;
-    k += (k & 1) ^ grp;         // this group's chunks: k = grp (mod 2)
-    for (; k < seg_hi - begin; k += 2) {
-      const int stage = k & (STAGES - 1);
+    k += (grp - k % GROUPS + GROUPS) % GROUPS;   // this group's chunks: k = grp (mod GROUPS)
+    for (; k < seg_hi - begin; k += GROUPS) {
+      const int stage = k % STAGES;
       if (!s.abort_) {
         if (!__all_sync(0xffffffffu,
-                        mbar_wait_bounded(&s.full[stage], (uint32_t)((k >> STAGE_SHIFT) & 1)))) {
+                        mbar_wait_bounded(&s.full[stage], (uint32_t)((k / STAGES) & 1)))) {
           record_error(p.err, kErrWaitTimeout);
           if (lane == 0) atomicExch(&s.abort_, 1);
         }
@@ -792,58 +795,54 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
 #pragma unroll
           for (int nt = 0; nt < 4; ++nt) pp[nt] = make_float2(exp2f(dv[nt].x - mx), exp2f(dv[nt].y - mx));
         }
-        // ---- P'_blk = p d_V (the A operand, hi + lo), dmin terms ----
-        uint32_t pa[2][2][4];   // [blk][kt]
+        // ---- per V block: P'_blk = p d_V (the A operand, hi + lo) and the dmin
+        //      term, then O += P'_blk V'_blk with the B fragments built straight
+        //      from two tokens' nibble words (one block at a time keeps fewer
+        //      registers live) ----
 #pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
-          l2 = __fadd2_rn(l2, pp[nt]);
-          const float4 fv0 = *reinterpret_cast<const float4*>(ftr + nt * 4 * PAIR_STRIDE + 32);   // d0 | dmin0
-          const float4 fv1 = *reinterpret_cast<const float4*>(ftr + nt * 4 * PAIR_STRIDE + 48);   // d1 | dmin1
-          const float2 pv0 = __fmul2_rn(pp[nt], make_float2(fv0.x, fv0.y));
-          const float2 pv1 = __fmul2_rn(pp[nt], make_float2(fv1.x, fv1.y));
-          cb0 = __ffma2_rn(pp[nt], make_float2(fv0.z, fv0.w), cb0);
-          cb1 = __ffma2_rn(pp[nt], make_float2(fv1.z, fv1.w), cb1);
-          // n-tile nt: k-step nt / 2, tokens 2 tig (+1) -> a0 / a1 (even nt) or a2 / a3 (odd nt)
-          const int kt = nt >> 1, r = (nt & 1) * 2;
+        for (int nt = 0; nt < 4; ++nt) l2 = __fadd2_rn(l2, pp[nt]);
+        const uint8_t* const vq = kb + loff_v;
 #pragma unroll
-          for (int blk = 0; blk < 2; ++blk) {
-            const float2 x = blk ? pv1 : pv0;
+        for (int blk = 0; blk < 2; ++blk) {
+          uint32_t pa[2][4];   // [kt]
+#pragma unroll
+          for (int nt = 0; nt < 4; ++nt) {
+            const float4 fv = *reinterpret_cast<const float4*>(ftr + nt * 4 * PAIR_STRIDE + 32 + 16 * blk);   // d | dmin
+            const float2 x = __fmul2_rn(pp[nt], make_float2(fv.x, fv.y));
+            if (blk == 0) cb0 = __ffma2_rn(pp[nt], make_float2(fv.z, fv.w), cb0);
+            else cb1 = __ffma2_rn(pp[nt], make_float2(fv.z, fv.w), cb1);
+            // n-tile nt: k-step nt / 2, tokens 2 tig (+1) -> a0 / a1 (even nt) or a2 / a3 (odd nt)
+            const int kt = nt >> 1, r = (nt & 1) * 2;
             const __half2 hi = __float22half2_rn(x);
             const float2 res = __ffma2_rn(__half22float2(hi), neg1, x);
             const __half2 lo = __float22half2_rn(res);
-            pa[blk][kt][r] = *reinterpret_cast<const uint32_t*>(&hi);
-            pa[blk][kt][r + 1] = *reinterpret_cast<const uint32_t*>(&lo);
+            pa[kt][r] = *reinterpret_cast<const uint32_t*>(&hi);
+            pa[kt][r + 1] = *reinterpret_cast<const uint32_t*>(&lo);
           }
-        }
-        // ---- O += P' V': B fragments straight from two tokens' nibble words ----
-        {
-          const uint8_t* const vq = kb + loff_v;
 #pragma unroll
-          for (int kt = 0; kt < 2; ++kt)
-#pragma unroll
-            for (int blk = 0; blk < 2; ++blk) {
-              const uint8_t* const vw = vq + kt * PAGE_BYTES + blk * BLK;
-              const uint32_t w00 = *reinterpret_cast<const uint32_t*>(vw);              // token 2 tig
-              const uint32_t w01 = *reinterpret_cast<const uint32_t*>(vw + ROWB);       // token 2 tig + 1
-              const uint32_t w10 = *reinterpret_cast<const uint32_t*>(vw + 8 * ROWB);   // token 2 tig + 8
-              const uint32_t w11 = *reinterpret_cast<const uint32_t*>(vw + 9 * ROWB);   // token 2 tig + 9
-              // byte 2h (dims 4g, 4g + 1) and byte 2h + 1 (dims 4g + 2, 4g + 3) of each
-              // token's halfword, the first token in the low half of the register
-              const uint32_t u0 = __byte_perm(w00, w01, vsel), u1 = __byte_perm(w10, w11, vsel);
-              const uint32_t v0 = __byte_perm(w00, w01, vsel2), v1 = __byte_perm(w10, w11, vsel2);
-              mma_f16(o[4 * blk + 0], pa[blk][kt], u0 & 0x000F000Fu, u1 & 0x000F000Fu);
-              mma_f16(o[4 * blk + 1], pa[blk][kt], u0 & 0x00F000F0u, u1 & 0x00F000F0u);
-              mma_f16(o[4 * blk + 2], pa[blk][kt], v0 & 0x000F000Fu, v1 & 0x000F000Fu);
-              mma_f16(o[4 * blk + 3], pa[blk][kt], v0 & 0x00F000F0u, v1 & 0x00F000F0u);
-            }
+          for (int kt = 0; kt < 2; ++kt) {
+            const uint8_t* const vw = vq + kt * PAGE_BYTES + blk * BLK;
+            const uint32_t w00 = *reinterpret_cast<const uint32_t*>(vw);              // token 2 tig
+            const uint32_t w01 = *reinterpret_cast<const uint32_t*>(vw + ROWB);       // token 2 tig + 1
+            const uint32_t w10 = *reinterpret_cast<const uint32_t*>(vw + 8 * ROWB);   // token 2 tig + 8
+            const uint32_t w11 = *reinterpret_cast<const uint32_t*>(vw + 9 * ROWB);   // token 2 tig + 9
+            // byte 2h (dims 4g, 4g + 1) and byte 2h + 1 (dims 4g + 2, 4g + 3) of each
+            // token's halfword, the first token in the low half of the register
+            const uint32_t u0 = __byte_perm(w00, w01, vsel), u1 = __byte_perm(w10, w11, vsel);
+            const uint32_t v0 = __byte_perm(w00, w01, vsel2), v1 = __byte_perm(w10, w11, vsel2);
+            mma_f16(o[4 * blk + 0], pa[kt], u0 & 0x000F000Fu, u1 & 0x000F000Fu);
+            mma_f16(o[4 * blk + 1], pa[kt], u0 & 0x00F000F0u, u1 & 0x00F000F0u);
+            mma_f16(o[4 * blk + 2], pa[kt], v0 & 0x000F000Fu, v1 & 0x000F000Fu);
+            mma_f16(o[4 * blk + 3], pa[kt], v0 & 0x00F000F0u, v1 & 0x00F000F0u);
+          }
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.empty[stage]);
     }
 
-    // ---- segment end: the 4 warps of each KV head (2 groups x 2 token halves)
-    //      fold their partials in shared memory into the CTA's partial ----
+    // ---- segment end: the 2 GROUPS warps of each KV head (groups x token
+    //      halves) fold their partials in shared memory into the CTA's partial ----
     float l = l2.x + l2.y;
     float cbs[2] = {cb0.x + cb0.y, cb1.x + cb1.y};
     l += __shfl_xor_sync(0xffffffffu, l, 1);
@@ -874,13 +873,14 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
     const int pe_ = s.prefix[b + 1];
     const int first_b = pb / W, last_b = (pe_ - 1) / W, n_b = last_b - first_b + 1;
     {
-      // thread -> (query head mr = KV head mr / 8, head mr % 8; dims md4 ..): the
-      // partials of warps kv, kv + 4, kv + 8, kv + 12
-      const int kv = mr >> 3, hh = mr & 7;
-      float ms[4], ls[4];
-      float4 os[4];
+      // thread t < MT -> (query head mr = KV head mr / 8, head mr % 8; dims md4 ..):
+      // the partials of warps kv, kv + 4, kv + 8, ...
+      constexpr int NW = NCW / NKV;
+      const int kv = (mr >> 3) & (NKV - 1), hh = mr & 7;
+      float ms[NW], ls[NW];
+      float4 os[NW];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < NW; ++j) {
         const float* src = reinterpret_cast<const float*>(s.wk[kv + 4 * j]) + hh * CP;
         ms[j] = src[HD];
         ls[j] = src[HD + 1];
@@ -888,12 +888,12 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
       }
       float M = -INFINITY;
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
+      for (int j = 0; j < NW; ++j)
         if (ls[j] > 0.f) M = fmaxf(M, ms[j]);
       float L = 0.f;
       float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < NW; ++j) {
         if (!(ls[j] > 0.f)) continue;
         const float w = exp2f(ms[j] - M);
         L = fmaf(w, ls[j], L);
@@ -902,22 +902,32 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
         O.z = fmaf(w, os[j].z, O.z);
         O.w = fmaf(w, os[j].w, O.w);
       }
-      if (n_b == 1 && p.mode != kModeRing) finish_block(p, s, b, true, mr, md4, O, M, L);   // this CTA alone
-      else store_slot(p, blockIdx.x + b, mr, md4, O, M, L);
+      if (n_b == 1 && p.mode != kModeRing) finish_block(p, s, b, t < MT, mr, md4, O, M, L);   // this CTA alone
+      else if (t < MT) store_slot(p, blockIdx.x + b, mr, md4, O, M, L);
     }
     consumer_sync();   // partials stored (and shared partials read) before the count-in
     if (n_b > 1 && p.mode != kModeRing) {
-      // Row-parallel merge: the last R CTAs to count in (R = the query heads, or
-      // the covering CTAs if fewer) each merge rows j, j + R, ... of the sequence
-      // once every covering CTA has counted in (all CTAs of the grid are
-      // resident, one per SM, so the wait ends; it is bounded all the same).
-      const int R = min(n_b, ROWS);
-      if (t == 0) s.flag = atom_add_acq_rel(&p.gcnt[b], 1);
+      // Row-parallel merge: every covering CTA counts in (gcnt[b]); of the
+      // eligible ones, the last R to take a merge ticket (gcnt[MAX_SEQS + b]; R =
+      // the query heads, or the eligible CTAs if fewer) each merge rows j, j + R,
+      // ... of the sequence once every covering CTA has counted in (all CTAs of
+      // the grid are resident, one per SM, so the wait ends; it is bounded all
+      // the same).  The last covering CTA is not eligible when its range goes on
+      // past this sequence: it reaches b first (b's last chunks lead its range)
+      // and the other CTAs reach b only at the end of theirs, so a wait there
+      // would hold back its later sequences and chain the sequences' merges.
+      const bool more = seg_hi < end;
+      const int n_m = n_b - (min(total, (last_b + 1) * W) > pe_ ? 1 : 0);
+      const int R = min(n_m, ROWS);
+      if (t == 0) {
+        atom_add_acq_rel(&p.gcnt[b], 1);
+        s.flag = more ? -1 : atomicAdd(&p.gcnt[MAX_SEQS + b], 1);
+      }
       consumer_sync();
       const int ticket = s.flag;
       consumer_sync();
-      if (ticket >= n_b - R) {
-        const int j = ticket - (n_b - R);
+      if (ticket >= n_m - R) {
+        const int j = ticket - (n_m - R);
         if (t == 0 && !wait_count(&p.gcnt[b], n_b, p.mode == kModeExchange ? p.ex.timeout_ns : 2000000000LL))
           record_error(p.err, kErrWaitTimeout);
         consumer_sync();
@@ -925,25 +935,27 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
         // the 32 groups are folded pairwise: lanes 16 apart by a shuffle, then a
         // tree over the 16 warps through shared memory
         const int pg = t >> 4, d4 = (t & 15) * 4;
-        float4* ro = reinterpret_cast<float4*>(s.wk[0]);                    // [16 warps][16] o
-        float2* rml = reinterpret_cast<float2*>(s.wk[0] + 16 * 16 * 16);     // [16 warps][16] (m, l)
-        float4* fo = reinterpret_cast<float4*>(s.wk[0] + 16 * 16 * 24);     // [rows][16] merged o
-        float2* fml = reinterpret_cast<float2*>(s.wk[0] + 16 * 16 * 24 + ROWS / 2 * 16 * 16);   // [rows][16]
+        uint8_t* const wk = &s.wk[0][0];   // the per-warp regions as one flat scratch area
+        float4* ro = reinterpret_cast<float4*>(wk);                         // [16 warps][16] o
+        float2* rml = reinterpret_cast<float2*>(wk + 16 * 16 * 16);          // [16 warps][16] (m, l)
+        float4* fo = reinterpret_cast<float4*>(wk + 16 * 16 * 24);          // [rows][16] merged o
+        float2* fml = reinterpret_cast<float2*>(wk + 16 * 16 * 24 + ROWS * 16 * 16);   // [rows][16]
+        static_assert(16 * 16 * 24 + ROWS * 16 * 24 <= NCW * WK_BYTES, "merge scratch fits the warp regions");
         const int nr = (ROWS - j + R - 1) / R;
         for (int rs = 0; rs < nr; ++rs) {
           const int r = j + rs * R;
-          float4 O;
-          float M, L;
-          merge_slots(p, first_b + b + pg, 32, n_b > pg ? (n_b - pg + 31) / 32 : 0, r, d4, O, M, L);
-          {
+          float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+          float M = -INFINITY, L = 0.f;
+          if (t < MT) {   // whole warps
+            merge_slots(p, first_b + b + pg, 32, n_b > pg ? (n_b - pg + 31) / 32 : 0, r, d4, O, M, L);
             const float Mo = __shfl_xor_sync(0xffffffffu, M, 16), Lo = __shfl_xor_sync(0xffffffffu, L, 16);
             const float4 Oo = make_float4(__shfl_xor_sync(0xffffffffu, O.x, 16), __shfl_xor_sync(0xffffffffu, O.y, 16),
                                           __shfl_xor_sync(0xffffffffu, O.z, 16), __shfl_xor_sync(0xffffffffu, O.w, 16));
             merge_pair(O, M, L, Oo, Mo, Lo);
-          }
-          if (lane < 16) {
-            ro[warp * 16 + lane] = O;
-            rml[warp * 16 + lane] = make_float2(M, L);
+            if (lane < 16) {
+              ro[warp * 16 + lane] = O;
+              rml[warp * 16 + lane] = make_float2(M, L);
+            }
           }
 #pragma unroll
           for (int half = 8; half >= 1; half >>= 1) {
@@ -971,6 +983,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
         consumer_sync();
         if (t == 0 && atom_add_acq_rel(&p.scnt[b], 1) == R - 1) {   // the last merger resets the counters
           atomicExch(&p.gcnt[b], 0);
+          atomicExch(&p.gcnt[MAX_SEQS + b], 0);
           atomicExch(&p.scnt[b], 0);
         }
       }
@@ -981,7 +994,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
   if (blockIdx.x == 0 && p.mode != kModeRing) {
     for (int b = 0; b < p.batch; ++b)
       if (s.prefix[b + 1] == s.prefix[b])
-        finish_block(p, s, b, true, mr, md4, make_float4(0.f, 0.f, 0.f, 0.f), -INFINITY, 0.f);
+        finish_block(p, s, b, t < MT, mr, md4, make_float4(0.f, 0.f, 0.f, 0.f), -INFINITY, 0.f);
   }
 }
 
