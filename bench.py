@@ -303,6 +303,7 @@ def timed_graph(torch, fn, stream, steps, warmup, barrier, dist=None, world=1, d
     that the ranks leave their flushes together), both outside the step's own
     event pair.  `clocks`: a ClockSampler context entered around the timed loop."""
     g = None
+    torch.cuda.synchronize()   # inputs built on other streams are complete
     with torch.cuda.stream(stream):
         for _ in range(max(3, warmup)):
             fn()

@@ -241,7 +241,6 @@ struct Smem {
   int32_t warp_tot[THREADS / 32];
   int32_t flag;
   int32_t abort_;
-  uint32_t ep[ROWS];                 // exchange epochs of the rows a CTA finishes
 };
 
 __device__ __forceinline__ int seek_seq(const Smem& s, int batch, int i) {
@@ -298,6 +297,14 @@ __device__ __forceinline__ float2 hdr2f(uint32_t w) {   // (d, dmin) of a block 
 __device__ __forceinline__ int perm_dim(int c) {
   const int base = c & ~7, e = c & 7;
   return base + ((e & 1) ? 4 : 0) + (e >> 1);
+}
+
+// 2^x by the MUFU instruction (ex2.approx.ftz: relative error ~2^-22, subnormal
+// results flushed to zero, 2^-inf = 0)
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ void consumer_sync() {
@@ -380,7 +387,7 @@ __device__ __forceinline__ void store_slot(const Params& p, int slot, int r, int
 // from its merged (O relative to M in log2 units, L): the partial, the
 // output, or the exchange with the other ranks (step `epoch`) and the
 // combined output.
-__device__ void finish_row(const Params& p, int b, int r, int d4, float4 O, float M, float L, uint32_t epoch) {
+__device__ __noinline__ void finish_row(const Params& p, int b, int r, int d4, float4 O, float M, float L, uint32_t epoch) {
   const float inv = L > 0.f ? 1.0f / L : 0.f;
   const float4 o = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
   const float mnat = L > 0.f ? M * 0.6931471805599453f : -INFINITY;   // log2 -> natural units
@@ -397,15 +404,16 @@ __device__ void finish_row(const Params& p, int b, int r, int d4, float4 O, floa
     }
     return;
   }
-  if (p.mode == kModeFinal) {
+  if (p.mode == kModeFinal || p.ex.world == 1) {   // one rank: this partial is the result
     *reinterpret_cast<float4*>(p.out + row * HD + d4) = o;
     return;
   }
-  // ---- exchange: this rank's row to every rank, then the ranks' rows combined ----
+  // ---- exchange: this rank's row to every other rank, then the ranks' rows combined ----
   const Exchange& ex = p.ex;
   const int buf = epoch & 1;
   const size_t slot = ((size_t)(buf * MAX_RANKS + ex.rank) * ex.rows + row) * (HD + 2);
   for (int rk = 0; rk < ex.world; ++rk) {
+    if (rk == ex.rank) continue;
     uint64_t* dst = reinterpret_cast<uint64_t*>(ex.mbox[rk] + mbox_data_off(ex.rows)) + slot;
     st_word(dst + d4, o.x, epoch);
     st_word(dst + d4 + 1, o.y, epoch);
@@ -416,16 +424,33 @@ __device__ void finish_row(const Params& p, int b, int r, int d4, float4 O, floa
       st_word(dst + HD + 1, L, epoch);
     }
   }
+  // each other rank's words, polled (bounded) until all six carry this step's
+  // epoch, folded in as they arrive; this rank's own row from registers.  One
+  // rank at a time: holding several ranks' words in flight costs registers that
+  // the chunk loop of the kernel needs
   const uint64_t* box = reinterpret_cast<const uint64_t*>(ex.mbox[ex.rank] + mbox_data_off(ex.rows));
-  bool ok = true;
   const unsigned long long t0 = global_ns();
   float Mr = -INFINITY, den = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  auto fold = [&](float4 orr, float mr, float lr) {
+    if (!(lr > 0.f)) return;
+    const float Mn = fmaxf(Mr, mr);
+    const float sa = expf(Mr - Mn), sb = lr * expf(mr - Mn);
+    den = den * sa + sb;
+    acc.x = acc.x * sa + orr.x * sb;
+    acc.y = acc.y * sa + orr.y * sb;
+    acc.z = acc.z * sa + orr.z * sb;
+    acc.w = acc.w * sa + orr.w * sb;
+    Mr = Mn;
+  };
+  fold(o, mnat, L);
+  bool ok = true;
   for (int rk = 0; rk < ex.world && ok; ++rk) {
+    if (rk == ex.rank) continue;
     const uint64_t* src = box + ((size_t)(buf * MAX_RANKS + rk) * ex.rows + row) * (HD + 2);
     uint32_t spins = 0;
-    uint64_t w[6];
     while (true) {
+      uint64_t w[6];
 #pragma unroll
       for (int i = 0; i < 4; ++i) w[i] = ld_word(src + d4 + i);
       w[4] = ld_word(src + HD);
@@ -433,44 +458,44 @@ __device__ void finish_row(const Params& p, int b, int r, int d4, float4 O, floa
       bool here = true;
 #pragma unroll
       for (int i = 0; i < 6; ++i) here &= (uint32_t)(w[i] >> 32) == epoch;
-      if (here) break;
+      if (here) {
+        fold(make_float4(__uint_as_float((uint32_t)w[0]), __uint_as_float((uint32_t)w[1]),
+                         __uint_as_float((uint32_t)w[2]), __uint_as_float((uint32_t)w[3])),
+             __uint_as_float((uint32_t)w[4]), __uint_as_float((uint32_t)w[5]));
+        break;
+      }
       if (++spins > 32) __nanosleep(64);
       if ((long long)(global_ns() - t0) > ex.timeout_ns) {
         ok = false;
         break;
       }
     }
-    if (!ok) break;
-    const float mr = __uint_as_float((uint32_t)w[4]), lr = __uint_as_float((uint32_t)w[5]);
-    if (!(lr > 0.f)) continue;
-    const float Mn = fmaxf(Mr, mr);
-    const float sa = expf(Mr - Mn), sb = lr * expf(mr - Mn);
-    den = den * sa + sb;
-    acc.x = acc.x * sa + __uint_as_float((uint32_t)w[0]) * sb;
-    acc.y = acc.y * sa + __uint_as_float((uint32_t)w[1]) * sb;
-    acc.z = acc.z * sa + __uint_as_float((uint32_t)w[2]) * sb;
-    acc.w = acc.w * sa + __uint_as_float((uint32_t)w[3]) * sb;
-    Mr = Mn;
   }
   if (!ok) record_error(p.err, kErrWaitTimeout);
   const float ir = den > 0.f ? 1.0f / den : 0.f;
   *reinterpret_cast<float4*>(p.out + row * HD + d4) = make_float4(acc.x * ir, acc.y * ir, acc.z * ir, acc.w * ir);
 }
 
-// finish_row for the rows a CTA holds, called by all consumer threads (thread
-// -> row r when `valid`); in exchange mode each row's epoch counter (in this
-// rank's mailbox header) is read before and advanced after the exchange.
-__device__ void finish_block(const Params& p, Smem& s, int b, bool valid, int r, int d4, float4 O, float M, float L) {
-  int* epochs = p.mode == kModeExchange ? reinterpret_cast<int*>(p.ex.mbox[p.ex.rank]) + (int64_t)b * ROWS : nullptr;
-  if (epochs) {
-    if (valid && d4 == 0) s.ep[r] = (uint32_t)(*reinterpret_cast<volatile int*>(epochs + r)) + 1u;
-    consumer_sync();
-  }
-  if (valid) finish_row(p, b, r, d4, O, M, L, epochs ? s.ep[r] : 0u);
-  if (epochs) {
-    consumer_sync();
-    if (valid && d4 == 0) *reinterpret_cast<volatile int*>(epochs + r) = (int)s.ep[r];
-  }
+// The epoch of row r of sequence b for this step (exchange mode with more than
+// one rank): one past the counter kept in this rank's mailbox header.  Issued
+// early (it is consumed only by finish_block) so that its load overlaps the merge.
+__device__ __forceinline__ uint32_t row_epoch(const Params& p, int b, int r) {
+  if (p.mode != kModeExchange || p.ex.world == 1) return 0u;
+  const int* epochs = reinterpret_cast<const int*>(p.ex.mbox[p.ex.rank]) + (int64_t)b * ROWS;
+  return (uint32_t)(*reinterpret_cast<const volatile int*>(epochs + r)) + 1u;
+}
+
+// finish_row for the rows a CTA holds (thread -> row r when `valid`, with its
+// step epoch from row_epoch); in exchange mode the row's epoch counter is
+// advanced after the exchange.  No other CTA touches the row in this step, and
+// the next step is a later launch, so no barrier is needed around the counter.
+__device__ void finish_block(const Params& p, int b, bool valid, int r, int d4, float4 O, float M, float L,
+                             uint32_t epoch) {
+  if (!valid) return;
+  finish_row(p, b, r, d4, O, M, L, epoch);
+  if (epoch != 0u && d4 == 0)
+    *reinterpret_cast<volatile int*>(reinterpret_cast<int*>(p.ex.mbox[p.ex.rank]) + (int64_t)b * ROWS + r) =
+        (int)epoch;
 }
 
 // Bounded wait until *c >= target (acquire at gpu scope); false on timeout.
@@ -482,6 +507,159 @@ __device__ bool wait_count(const int32_t* c, int target, long long timeout_ns) {
     if (v >= target) return true;
     if ((long long)(global_ns() - t0) > timeout_ns) return false;
     __nanosleep(64);
+  }
+}
+
+// The rest of a segment's end, after the warps' partials are in shared memory:
+// the CTA's partial of sequence b (finished here when the CTA covers b alone,
+// else stored for the merge), the count-in and, in the merging CTAs, the merge,
+// the exchange and the output.  Called by all consumer threads.
+__device__ __forceinline__ void segment_end(const Params& p, Smem& s, int b, int pb, int W, int total, int seg_hi,
+                                         int end) {
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int mr = t >> 4, md4 = (t & 15) * 4;
+  const int pe_ = s.prefix[b + 1];
+  const int first_b = pb / W, last_b = (pe_ - 1) / W, n_b = last_b - first_b + 1;
+  {
+    // a sequence this CTA covers alone is finished here: its rows' epochs load
+    // while the partials are folded
+    const uint32_t ep_self = (n_b == 1 && t < MT) ? row_epoch(p, b, mr) : 0u;
+    // thread t < MT -> (query head mr = KV head mr / 8, head mr % 8; dims md4 ..):
+    // the partials of warps kv, kv + 4, kv + 8, ...
+    constexpr int NW = NCW / NKV;
+    const int kv = (mr >> 3) & (NKV - 1), hh = mr & 7;
+    float ms[NW], ls[NW];
+    float4 os[NW];
+#pragma unroll
+    for (int j = 0; j < NW; ++j) {
+      const float* src = reinterpret_cast<const float*>(s.wk[kv + 4 * j]) + hh * CP;
+      ms[j] = src[HD];
+      ls[j] = src[HD + 1];
+      os[j] = *reinterpret_cast<const float4*>(src + md4);
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < NW; ++j)
+      if (ls[j] > 0.f) M = fmaxf(M, ms[j]);
+    float L = 0.f;
+    float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < NW; ++j) {
+      if (!(ls[j] > 0.f)) continue;
+      const float w = exp2f(ms[j] - M);
+      L = fmaf(w, ls[j], L);
+      O.x = fmaf(w, os[j].x, O.x);
+      O.y = fmaf(w, os[j].y, O.y);
+      O.z = fmaf(w, os[j].z, O.z);
+      O.w = fmaf(w, os[j].w, O.w);
+    }
+    if (n_b == 1 && p.mode != kModeRing) finish_block(p, b, t < MT, mr, md4, O, M, L, ep_self);   // this CTA alone
+    else if (t < MT) store_slot(p, blockIdx.x + b, mr, md4, O, M, L);
+  }
+  consumer_sync();   // partials stored (and shared partials read) before the count-in
+  if (n_b > 1 && p.mode != kModeRing) {
+    // Row-parallel merge: every covering CTA counts in (gcnt[b]); of the
+    // eligible ones, the last R to take a merge ticket (gcnt[MAX_SEQS + b]; R =
+    // the query heads, or the eligible CTAs if fewer) each merge rows j, j + R,
+    // ... of the sequence once every covering CTA has counted in (all CTAs of
+    // the grid are resident, one per SM, so the wait ends; it is bounded all
+    // the same).  The last covering CTA is not eligible when its range goes on
+    // past this sequence: it reaches b first (b's last chunks lead its range)
+    // and the other CTAs reach b only at the end of theirs, so a wait there
+    // would hold back its later sequences and chain the sequences' merges.
+    const bool more = seg_hi < end;
+    const int n_m = n_b - (min(total, (last_b + 1) * W) > pe_ ? 1 : 0);
+    const int R = min(n_m, ROWS);
+    if (t == 0) {
+      // the arrival is a release reduction (no reply awaited); only the
+      // ticket's reply is waited for
+      asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(&p.gcnt[b]) : "memory");
+      s.flag = more ? -1 : atomicAdd(&p.gcnt[MAX_SEQS + b], 1);
+    }
+    consumer_sync();
+    const int ticket = s.flag;
+    consumer_sync();
+    if (ticket >= n_m - R) {
+      const int j = ticket - (n_m - R);
+      // the rows this thread finishes after the merge (thread -> merged row slot
+      // t / 16, row j + (t / 16) R, dims (t % 16) 4): their epochs load meanwhile
+      const int nr = (ROWS - j + R - 1) / R;
+      const uint32_t ep_row = (t >> 4) < nr ? row_epoch(p, b, j + (t >> 4) * R) : 0u;
+      if (t == 0 && !wait_count(&p.gcnt[b], n_b, p.mode == kModeExchange ? p.ex.timeout_ns : 2000000000LL))
+        record_error(p.err, kErrWaitTimeout);
+      consumer_sync();
+      // thread -> partial group pg = t / 16 (covering CTAs pg, pg + 32, ...), dims d4;
+      // the 32 groups are folded pairwise (lanes 16 apart, by a shuffle), then the
+      // first 16 threads fold the 16 warps' partials from shared memory
+      const int pg = t >> 4, d4 = (t & 15) * 4;
+      uint8_t* const wk = &s.wk[0][0];   // the per-warp regions as one flat scratch area
+      float4* ro = reinterpret_cast<float4*>(wk);                         // [16 warps][16] o
+      float2* rml = reinterpret_cast<float2*>(wk + 16 * 16 * 16);          // [16 warps][16] (m, l)
+      float4* fo = reinterpret_cast<float4*>(wk + 16 * 16 * 24);          // [rows][16] merged o
+      float2* fml = reinterpret_cast<float2*>(wk + 16 * 16 * 24 + ROWS * 16 * 16);   // [rows][16]
+      static_assert(16 * 16 * 24 + ROWS * 16 * 24 <= NCW * WK_BYTES,
+                    "merge scratch fits the warp regions");
+      for (int rs = 0; rs < nr; ++rs) {
+        const int r = j + rs * R;
+        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+        float M = -INFINITY, L = 0.f;
+        if (t < MT) {   // whole warps
+          merge_slots(p, first_b + b + pg, 32, n_b > pg ? (n_b - pg + 31) / 32 : 0, r, d4, O, M, L);
+          const float Mo = __shfl_xor_sync(0xffffffffu, M, 16), Lo = __shfl_xor_sync(0xffffffffu, L, 16);
+          const float4 Oo = make_float4(__shfl_xor_sync(0xffffffffu, O.x, 16), __shfl_xor_sync(0xffffffffu, O.y, 16),
+                                        __shfl_xor_sync(0xffffffffu, O.z, 16), __shfl_xor_sync(0xffffffffu, O.w, 16));
+          merge_pair(O, M, L, Oo, Mo, Lo);
+          if (lane < 16) {
+            ro[warp * 16 + lane] = O;
+            rml[warp * 16 + lane] = make_float2(M, L);
+          }
+        }
+        consumer_sync();
+        // the 16 warps' partials of the row folded by the first 16 threads: the
+        // common maximum first, then the weighted sums (independent exponentials)
+        if (t < 16) {
+          float Mx = -INFINITY;
+#pragma unroll
+          for (int w = 0; w < 16; ++w) {
+            const float2 mo = rml[w * 16 + t];
+            if (mo.y > 0.f) Mx = fmaxf(Mx, mo.x);
+          }
+          float Lx = 0.f;
+          float4 Ox = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (Mx > -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < 16; ++w) {
+              const float2 mo = rml[w * 16 + t];
+              if (!(mo.y > 0.f)) continue;
+              const float4 oo = ro[w * 16 + t];
+              const float sc = exp2f(mo.x - Mx);
+              Lx = fmaf(sc, mo.y, Lx);
+              Ox.x = fmaf(sc, oo.x, Ox.x);
+              Ox.y = fmaf(sc, oo.y, Ox.y);
+              Ox.z = fmaf(sc, oo.z, Ox.z);
+              Ox.w = fmaf(sc, oo.w, Ox.w);
+            }
+          }
+          fo[rs * 16 + t] = Ox;
+          fml[rs * 16 + t] = make_float2(Mx, Lx);
+        }
+        consumer_sync();
+      }
+      // thread -> merged row slot rs = t / 16 (row j + rs R), dims d4
+      const int rs = t >> 4;
+      const bool valid = rs < nr;
+      const float2 ml = valid ? fml[rs * 16 + (t & 15)] : make_float2(-INFINITY, 0.f);
+      finish_block(p, b, valid, valid ? j + rs * R : 0, d4,
+                   valid ? fo[rs * 16 + (t & 15)] : make_float4(0.f, 0.f, 0.f, 0.f), ml.x, ml.y, ep_row);
+      consumer_sync();
+      if (t == 0 && atom_add_acq_rel(&p.scnt[b], 1) == R - 1) {
+        // the last merger resets the counters: every CTA has counted in and
+        // taken its ticket, and no CTA reads them again in this launch
+        __stcg(&p.gcnt[b], 0);
+        __stcg(&p.gcnt[MAX_SEQS + b], 0);
+        __stcg(&p.scnt[b], 0);
+      }
+    }
   }
 }
 
@@ -507,6 +685,9 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
   // waits for this one the same way
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // one token range for every sequence (no per-sequence arrays): the chunk
+  // offsets follow without a scan
+  const bool uniform = !p.seq_lens && !p.tok_begin && !p.tok_end;
   for (int b = t; b < p.batch; b += THREADS) {
     int lo, hi;
     if (p.seq_lens) {
@@ -523,9 +704,14 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
     s.beg[b] = lo;
     s.end[b] = hi;
     s.c0[b] = lo / CHUNK;
+    if (uniform) {
+      const int c = hi > lo ? (hi + CHUNK - 1) / CHUNK - lo / CHUNK : 0;
+      s.prefix[b] = b * c;
+      if (b == p.batch - 1) s.prefix[p.batch] = p.batch * c;
+    }
   }
   __syncthreads();
-  {
+  if (!uniform) {
     // exclusive prefix of the chunk counts: thread t owns sequence t
     static_assert(THREADS >= MAX_SEQS + 1, "one thread per sequence in the prefix scan");
     const int b = t;
@@ -542,8 +728,8 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
     int woff = 0;
     for (int w = 0; w < warp; ++w) woff += s.warp_tot[w];
     if (b <= p.batch) s.prefix[b] = woff + incl - c;
+    __syncthreads();
   }
-  __syncthreads();
 
   const int total = s.prefix[p.batch];
   const int W = (total + gridDim.x - 1) / gridDim.x;
@@ -770,17 +956,21 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
         //      reference max (d <= 2 in almost every chunk); the chunk max,
         //      reduced over the lanes meanwhile, only decides whether the
         //      reference moves (when d passes 2, so that p <= 4), in which case
-        //      the state is rescaled and p recomputed ----
+        //      the state is rescaled and p recomputed.  The branch is taken by
+        //      the whole warp when any of its heads moves (heads that do not
+        //      move scale by 1), so that it never diverges ----
         float2 pp[4];
 #pragma unroll
-        for (int nt = 0; nt < 4; ++nt) pp[nt] = make_float2(exp2f(dv[nt].x), exp2f(dv[nt].y));
+        for (int nt = 0; nt < 4; ++nt) pp[nt] = make_float2(ex2_ftz(dv[nt].x), ex2_ftz(dv[nt].y));
         float mx = fmaxf(dv[0].x, dv[0].y);
 #pragma unroll
         for (int nt = 1; nt < 4; ++nt) mx = fmaxf(mx, fmaxf(dv[nt].x, dv[nt].y));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        if (mx > 2.0f || (m == -INFINITY && mx > -INFINITY)) {
-          const float al = m == -INFINITY ? 0.f : exp2f(-mx);
+        const bool moves = mx > 2.0f || (m == -INFINITY && mx > -INFINITY);
+        if (__any_sync(0xffffffffu, moves)) {
+          const float sh = moves ? mx : 0.f;
+          const float al = moves ? (m == -INFINITY ? 0.f : ex2_ftz(-mx)) : 1.f;
           const float2 al2 = make_float2(al, al);
           l2 = __fmul2_rn(l2, al2);
           cb0 = __fmul2_rn(cb0, al2);
@@ -791,9 +981,9 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
             const float2 c = __fmul2_rn(make_float2(o[nt][2], o[nt][3]), al2);
             o[nt][0] = a.x; o[nt][1] = a.y; o[nt][2] = c.x; o[nt][3] = c.y;
           }
-          m = mref + mx;
+          if (moves) m = mref + mx;
 #pragma unroll
-          for (int nt = 0; nt < 4; ++nt) pp[nt] = make_float2(exp2f(dv[nt].x - mx), exp2f(dv[nt].y - mx));
+          for (int nt = 0; nt < 4; ++nt) pp[nt] = make_float2(ex2_ftz(dv[nt].x - sh), ex2_ftz(dv[nt].y - sh));
         }
         // ---- per V block: P'_blk = p d_V (the A operand, hi + lo) and the dmin
         //      term, then O += P'_blk V'_blk with the B fragments built straight
@@ -870,131 +1060,15 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
       }
     }
     consumer_sync();
-    const int pe_ = s.prefix[b + 1];
-    const int first_b = pb / W, last_b = (pe_ - 1) / W, n_b = last_b - first_b + 1;
-    {
-      // thread t < MT -> (query head mr = KV head mr / 8, head mr % 8; dims md4 ..):
-      // the partials of warps kv, kv + 4, kv + 8, ...
-      constexpr int NW = NCW / NKV;
-      const int kv = (mr >> 3) & (NKV - 1), hh = mr & 7;
-      float ms[NW], ls[NW];
-      float4 os[NW];
-#pragma unroll
-      for (int j = 0; j < NW; ++j) {
-        const float* src = reinterpret_cast<const float*>(s.wk[kv + 4 * j]) + hh * CP;
-        ms[j] = src[HD];
-        ls[j] = src[HD + 1];
-        os[j] = *reinterpret_cast<const float4*>(src + md4);
-      }
-      float M = -INFINITY;
-#pragma unroll
-      for (int j = 0; j < NW; ++j)
-        if (ls[j] > 0.f) M = fmaxf(M, ms[j]);
-      float L = 0.f;
-      float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int j = 0; j < NW; ++j) {
-        if (!(ls[j] > 0.f)) continue;
-        const float w = exp2f(ms[j] - M);
-        L = fmaf(w, ls[j], L);
-        O.x = fmaf(w, os[j].x, O.x);
-        O.y = fmaf(w, os[j].y, O.y);
-        O.z = fmaf(w, os[j].z, O.z);
-        O.w = fmaf(w, os[j].w, O.w);
-      }
-      if (n_b == 1 && p.mode != kModeRing) finish_block(p, s, b, t < MT, mr, md4, O, M, L);   // this CTA alone
-      else if (t < MT) store_slot(p, blockIdx.x + b, mr, md4, O, M, L);
-    }
-    consumer_sync();   // partials stored (and shared partials read) before the count-in
-    if (n_b > 1 && p.mode != kModeRing) {
-      // Row-parallel merge: every covering CTA counts in (gcnt[b]); of the
-      // eligible ones, the last R to take a merge ticket (gcnt[MAX_SEQS + b]; R =
-      // the query heads, or the eligible CTAs if fewer) each merge rows j, j + R,
-      // ... of the sequence once every covering CTA has counted in (all CTAs of
-      // the grid are resident, one per SM, so the wait ends; it is bounded all
-      // the same).  The last covering CTA is not eligible when its range goes on
-      // past this sequence: it reaches b first (b's last chunks lead its range)
-      // and the other CTAs reach b only at the end of theirs, so a wait there
-      // would hold back its later sequences and chain the sequences' merges.
-      const bool more = seg_hi < end;
-      const int n_m = n_b - (min(total, (last_b + 1) * W) > pe_ ? 1 : 0);
-      const int R = min(n_m, ROWS);
-      if (t == 0) {
-        atom_add_acq_rel(&p.gcnt[b], 1);
-        s.flag = more ? -1 : atomicAdd(&p.gcnt[MAX_SEQS + b], 1);
-      }
-      consumer_sync();
-      const int ticket = s.flag;
-      consumer_sync();
-      if (ticket >= n_m - R) {
-        const int j = ticket - (n_m - R);
-        if (t == 0 && !wait_count(&p.gcnt[b], n_b, p.mode == kModeExchange ? p.ex.timeout_ns : 2000000000LL))
-          record_error(p.err, kErrWaitTimeout);
-        consumer_sync();
-        // thread -> partial group pg = t / 16 (covering CTAs pg, pg + 32, ...), dims d4;
-        // the 32 groups are folded pairwise: lanes 16 apart by a shuffle, then a
-        // tree over the 16 warps through shared memory
-        const int pg = t >> 4, d4 = (t & 15) * 4;
-        uint8_t* const wk = &s.wk[0][0];   // the per-warp regions as one flat scratch area
-        float4* ro = reinterpret_cast<float4*>(wk);                         // [16 warps][16] o
-        float2* rml = reinterpret_cast<float2*>(wk + 16 * 16 * 16);          // [16 warps][16] (m, l)
-        float4* fo = reinterpret_cast<float4*>(wk + 16 * 16 * 24);          // [rows][16] merged o
-        float2* fml = reinterpret_cast<float2*>(wk + 16 * 16 * 24 + ROWS * 16 * 16);   // [rows][16]
-        static_assert(16 * 16 * 24 + ROWS * 16 * 24 <= NCW * WK_BYTES, "merge scratch fits the warp regions");
-        const int nr = (ROWS - j + R - 1) / R;
-        for (int rs = 0; rs < nr; ++rs) {
-          const int r = j + rs * R;
-          float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
-          float M = -INFINITY, L = 0.f;
-          if (t < MT) {   // whole warps
-            merge_slots(p, first_b + b + pg, 32, n_b > pg ? (n_b - pg + 31) / 32 : 0, r, d4, O, M, L);
-            const float Mo = __shfl_xor_sync(0xffffffffu, M, 16), Lo = __shfl_xor_sync(0xffffffffu, L, 16);
-            const float4 Oo = make_float4(__shfl_xor_sync(0xffffffffu, O.x, 16), __shfl_xor_sync(0xffffffffu, O.y, 16),
-                                          __shfl_xor_sync(0xffffffffu, O.z, 16), __shfl_xor_sync(0xffffffffu, O.w, 16));
-            merge_pair(O, M, L, Oo, Mo, Lo);
-            if (lane < 16) {
-              ro[warp * 16 + lane] = O;
-              rml[warp * 16 + lane] = make_float2(M, L);
-            }
-          }
-#pragma unroll
-          for (int half = 8; half >= 1; half >>= 1) {
-            consumer_sync();
-            if (warp < half && lane < 16) {
-              const float4 Oo = ro[(warp + half) * 16 + lane];
-              const float2 mo = rml[(warp + half) * 16 + lane];
-              merge_pair(O, M, L, Oo, mo.x, mo.y);
-              ro[warp * 16 + lane] = O;
-              rml[warp * 16 + lane] = make_float2(M, L);
-            }
-          }
-          if (warp == 0 && lane < 16) {
-            fo[rs * 16 + lane] = O;
-            fml[rs * 16 + lane] = make_float2(M, L);
-          }
-          consumer_sync();
-        }
-        // thread -> merged row slot rs = t / 16 (row j + rs R), dims d4
-        const int rs = t >> 4;
-        const bool valid = rs < nr;
-        const float2 ml = valid ? fml[rs * 16 + (t & 15)] : make_float2(-INFINITY, 0.f);
-        finish_block(p, s, b, valid, valid ? j + rs * R : 0, d4, valid ? fo[rs * 16 + (t & 15)] : make_float4(0.f, 0.f, 0.f, 0.f),
-                     ml.x, ml.y);
-        consumer_sync();
-        if (t == 0 && atom_add_acq_rel(&p.scnt[b], 1) == R - 1) {   // the last merger resets the counters
-          atomicExch(&p.gcnt[b], 0);
-          atomicExch(&p.gcnt[MAX_SEQS + b], 0);
-          atomicExch(&p.scnt[b], 0);
-        }
-      }
-    }
+    segment_end(p, s, b, pb, W, total, seg_hi, end);
     i = seg_hi;
   }
   // sequences with nothing to attend: CTA 0 writes their (empty) results
   if (blockIdx.x == 0 && p.mode != kModeRing) {
     for (int b = 0; b < p.batch; ++b)
       if (s.prefix[b + 1] == s.prefix[b])
-        finish_block(p, s, b, t < MT, mr, md4, make_float4(0.f, 0.f, 0.f, 0.f), -INFINITY, 0.f);
+        finish_block(p, b, t < MT, mr, md4, make_float4(0.f, 0.f, 0.f, 0.f), -INFINITY, 0.f,
+                     t < MT ? row_epoch(p, b, mr) : 0u);
   }
 }
 
