@@ -467,7 +467,7 @@ def run_config5(A, S, torch, dev, stream, args, barrier, dist, world, rank, with
 
     ms, mode = res["p2p"]
     shard_bytes = config5_bytes(dec.hi - dec.lo)
-    launches = S.SplitKVDecoder.LAUNCHES_PER_STEP
+    launches = dec.launches_per_step
     return {
         "ms": ms, "mode": mode, "clocks": clocks.summary(), "e2e_ms": e2e_ms, "e2e_mode": e2e_mode,
         "host_out_matches_device": host_ok, "shard_bytes": shard_bytes, "launches_per_step": launches,

@@ -289,7 +289,7 @@ int32_t nyion_attn_decode_zoned_f32_tracked(float* out, const float* q, const fl
                                             int64_t q_pos, int32_t n_heads, int32_t n_kv_heads,
                                             int32_t head_dim, double* importance, void* stream);
 
-/* ---------------------------------- split-KV across GPUs, exchange fused ----
+/* ------------------------------------------- split-KV across GPUs, peer exchange ----
  * No reference counterpart (the reference has no multi-GPU attention); the
  * merge is the log-sum-exp identity of attention.mojo:89-96.  One process
  * per GPU; rank r holds the 4-bit pages of its token range [u_begin, u_end).
@@ -297,12 +297,13 @@ int32_t nyion_attn_decode_zoned_f32_tracked(float* out, const float* q, const fl
  * zeroed by nyion_attn_mailbox_alloc) and opens every other rank's through
  * CUDA IPC (nyion_attn_ipc_handle gives 64 bytes to send, nyion_attn_ipc_open
  * maps a received one).  nyion_attn_decode_q4_splitkv then runs the rank's
- * decode and, in the same launch (the CTAs that merge a sequence's partials),
- * writes each (sequence, head) row's partial into every rank's mailbox over
- * peer memory as 64-bit words tagged with the step's epoch, waits (at most
- * timeout_ms; 0 = 2000) until all ranks' words of the row carry it, and writes
- * the combined attention to `out` [batch][n_heads][head_dim] on every rank.
- * With world 1 the merged rows are written directly (no mailbox traffic).
+ * decode, whose CTAs that merge a sequence's partials write each (sequence,
+ * head) row's partial into every rank's mailbox over peer memory as 64-bit
+ * words tagged with the step's epoch; a second kernel on the same stream waits
+ * (at most timeout_ms; 0 = 2000) until all ranks' words of the row carry it
+ * and writes the combined attention to `out` [batch][n_heads][head_dim] on
+ * every rank (two launches per call).  With world 1 the merged rows are
+ * written directly by the decode (one launch, no mailbox traffic).
  * workspace: nyion_attn_q4_workspace_size(batch) bytes (reset once) or NULL.
  * `mailboxes` is a host array of `world` device pointers ([rank] = own).
  * All ranks must call it the same number of times with the same batch;

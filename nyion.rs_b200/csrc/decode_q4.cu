@@ -408,12 +408,13 @@ __device__ __noinline__ void finish_row(const Params& p, int b, int r, int d4, f
     *reinterpret_cast<float4*>(p.out + row * HD + d4) = o;
     return;
   }
-  // ---- exchange: this rank's row to every other rank, then the ranks' rows combined ----
+  // ---- exchange: this rank's row into every rank's mailbox (its own included);
+  //      q4_exchange_kernel, launched after this kernel, waits for the ranks'
+  //      rows and combines them ----
   const Exchange& ex = p.ex;
   const int buf = epoch & 1;
   const size_t slot = ((size_t)(buf * MAX_RANKS + ex.rank) * ex.rows + row) * (HD + 2);
   for (int rk = 0; rk < ex.world; ++rk) {
-    if (rk == ex.rank) continue;
     uint64_t* dst = reinterpret_cast<uint64_t*>(ex.mbox[rk] + mbox_data_off(ex.rows)) + slot;
     st_word(dst + d4, o.x, epoch);
     st_word(dst + d4 + 1, o.y, epoch);
@@ -424,56 +425,6 @@ __device__ __noinline__ void finish_row(const Params& p, int b, int r, int d4, f
       st_word(dst + HD + 1, L, epoch);
     }
   }
-  // each other rank's words, polled (bounded) until all six carry this step's
-  // epoch, folded in as they arrive; this rank's own row from registers.  One
-  // rank at a time: holding several ranks' words in flight costs registers that
-  // the chunk loop of the kernel needs
-  const uint64_t* box = reinterpret_cast<const uint64_t*>(ex.mbox[ex.rank] + mbox_data_off(ex.rows));
-  const unsigned long long t0 = global_ns();
-  float Mr = -INFINITY, den = 0.f;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  auto fold = [&](float4 orr, float mr, float lr) {
-    if (!(lr > 0.f)) return;
-    const float Mn = fmaxf(Mr, mr);
-    const float sa = expf(Mr - Mn), sb = lr * expf(mr - Mn);
-    den = den * sa + sb;
-    acc.x = acc.x * sa + orr.x * sb;
-    acc.y = acc.y * sa + orr.y * sb;
-    acc.z = acc.z * sa + orr.z * sb;
-    acc.w = acc.w * sa + orr.w * sb;
-    Mr = Mn;
-  };
-  fold(o, mnat, L);
-  bool ok = true;
-  for (int rk = 0; rk < ex.world && ok; ++rk) {
-    if (rk == ex.rank) continue;
-    const uint64_t* src = box + ((size_t)(buf * MAX_RANKS + rk) * ex.rows + row) * (HD + 2);
-    uint32_t spins = 0;
-    while (true) {
-      uint64_t w[6];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) w[i] = ld_word(src + d4 + i);
-      w[4] = ld_word(src + HD);
-      w[5] = ld_word(src + HD + 1);
-      bool here = true;
-#pragma unroll
-      for (int i = 0; i < 6; ++i) here &= (uint32_t)(w[i] >> 32) == epoch;
-      if (here) {
-        fold(make_float4(__uint_as_float((uint32_t)w[0]), __uint_as_float((uint32_t)w[1]),
-                         __uint_as_float((uint32_t)w[2]), __uint_as_float((uint32_t)w[3])),
-             __uint_as_float((uint32_t)w[4]), __uint_as_float((uint32_t)w[5]));
-        break;
-      }
-      if (++spins > 32) __nanosleep(64);
-      if ((long long)(global_ns() - t0) > ex.timeout_ns) {
-        ok = false;
-        break;
-      }
-    }
-  }
-  if (!ok) record_error(p.err, kErrWaitTimeout);
-  const float ir = den > 0.f ? 1.0f / den : 0.f;
-  *reinterpret_cast<float4*>(p.out + row * HD + d4) = make_float4(acc.x * ir, acc.y * ir, acc.z * ir, acc.w * ir);
 }
 
 // The epoch of row r of sequence b for this step (exchange mode with more than
@@ -1293,6 +1244,82 @@ __global__ void lse_combine_kernel(const float* __restrict__ parts, int G, int64
   for (int j = 0; j < PER; ++j) out[r * D + d0 + j] = acc[j] * inv;
 }
 
+// ============================================================================
+// split-KV exchange: the ranks' merged rows combined (one CTA per row)
+// ============================================================================
+// Launched with programmatic dependent launch after decode_q4_kernel in
+// exchange mode, whose merging CTAs wrote this rank's row r into slot [rank] of
+// every rank's mailbox as (epoch, value) words and advanced row r's epoch
+// counter.  Thread (rank rk = t / 16, dims 4 (t % 16)) polls slot [rk] of this
+// rank's mailbox (bounded) until its six words carry the step's epoch; the
+// ranks' rows meet in shared memory and 16 threads combine them.  All ranks'
+// words are in flight at once (one round trip when they have arrived); this
+// kernel's registers are its own, so the decode's chunk loop keeps its
+// allocation.
+__global__ void __launch_bounds__(16 * MAX_RANKS) q4_exchange_kernel(const Exchange ex, float* __restrict__ out,
+                                                                     int32_t* err) {
+  __shared__ float4 xo[MAX_RANKS][16];
+  __shared__ float2 xml[MAX_RANKS][16];
+  asm volatile("griddepcontrol.wait;" ::: "memory");   // the decode's words and epoch counters are written
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int t = threadIdx.x, rk = t >> 4, d4 = (t & 15) * 4;
+  const int64_t row = blockIdx.x;
+  const uint32_t epoch = (uint32_t)(*reinterpret_cast<const volatile int*>(
+      reinterpret_cast<const int*>(ex.mbox[ex.rank]) + row));
+  const int buf = epoch & 1;
+  if (rk < ex.world) {
+    const uint64_t* src = reinterpret_cast<const uint64_t*>(ex.mbox[ex.rank] + mbox_data_off(ex.rows)) +
+                          ((size_t)(buf * MAX_RANKS + rk) * ex.rows + row) * (HD + 2);
+    const unsigned long long t0 = global_ns();
+    uint32_t spins = 0;
+    float4 ov = make_float4(0.f, 0.f, 0.f, 0.f);
+    float2 ml = make_float2(-INFINITY, 0.f);
+    while (true) {
+      uint64_t w[6];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) w[i] = ld_word(src + d4 + i);
+      w[4] = ld_word(src + HD);
+      w[5] = ld_word(src + HD + 1);
+      bool here = true;
+#pragma unroll
+      for (int i = 0; i < 6; ++i) here &= (uint32_t)(w[i] >> 32) == epoch;
+      if (here) {
+        ov = make_float4(__uint_as_float((uint32_t)w[0]), __uint_as_float((uint32_t)w[1]),
+                         __uint_as_float((uint32_t)w[2]), __uint_as_float((uint32_t)w[3]));
+        ml = make_float2(__uint_as_float((uint32_t)w[4]), __uint_as_float((uint32_t)w[5]));
+        break;
+      }
+      if (++spins > 32) __nanosleep(64);
+      if ((long long)(global_ns() - t0) > ex.timeout_ns) {
+        record_error(err, kErrWaitTimeout);   // this rank's row is left out
+        break;
+      }
+    }
+    xo[rk][t & 15] = ov;
+    xml[rk][t & 15] = ml;
+  }
+  __syncthreads();
+  if (t < 16) {
+    float Mr = -INFINITY, den = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < ex.world; ++k) {
+      const float2 ml = xml[k][t];
+      if (!(ml.y > 0.f)) continue;
+      const float4 ov = xo[k][t];
+      const float Mn = fmaxf(Mr, ml.x);
+      const float sa = expf(Mr - Mn), sb = ml.y * expf(ml.x - Mn);
+      den = den * sa + sb;
+      acc.x = acc.x * sa + ov.x * sb;
+      acc.y = acc.y * sa + ov.y * sb;
+      acc.z = acc.z * sa + ov.z * sb;
+      acc.w = acc.w * sa + ov.w * sb;
+      Mr = Mn;
+    }
+    const float ir = den > 0.f ? 1.0f / den : 0.f;
+    *reinterpret_cast<float4*>(out + row * HD + d4) = make_float4(acc.x * ir, acc.y * ir, acc.z * ir, acc.w * ir);
+  }
+}
+
 size_t smem_bytes() { return sizeof(Smem); }
 static_assert(sizeof(Smem) <= 227 * 1024, "decode_q4 shared memory must fit one CTA per SM");
 
@@ -1654,5 +1681,12 @@ extern "C" int32_t nyion_attn_decode_q4_splitkv(
   // one rank: the merged rows are the output (no exchange needed)
   p.mode = world > 1 ? kModeExchange : kModeFinal;
   p.out = out;
-  return launch_partial(p, batch, nullptr, nullptr, q, workspace, s);
+  st = launch_partial(p, batch, nullptr, nullptr, q, workspace, s);
+  if (st || world == 1) return st;
+  DeviceInfo* dev = nullptr;
+  st = device_info(&dev);
+  if (st) return st;
+  return check_cuda(launch_pdl(q4_exchange_kernel, dim3((unsigned)(batch * n_heads)), dim3(16 * MAX_RANKS), 0, s,
+                               p.ex, out, dev->err_word),
+                    "q4_exchange launch");
 }

@@ -5,12 +5,11 @@ rank (each rank's KV arena holds only its pages).  Every rank computes a
 log-sum-exp partial (o/l, m, l) per (sequence, query head) over its range and
 the ranks' partials are merged on every rank.  Two exchanges:
 
-  * "p2p" (the GPU path): nyion_attn_decode_q4_splitkv writes each rank's
-    partials straight into every rank's mailbox over peer memory (NVLink) from
-    the reduce kernel, and the same kernel waits for the other ranks' rows and
-    combines them: one kernel after the decode, no collective call.  The
-    mailboxes are opened once through CUDA IPC handles exchanged with
-    torch.distributed.
+  * "p2p" (the GPU path): nyion_attn_decode_q4_splitkv's decode launch
+    writes each rank's merged rows straight into every rank's mailbox over
+    peer memory (NVLink), and a second small kernel waits for the ranks' rows
+    and combines them: no collective call.  The mailboxes are opened once
+    through CUDA IPC handles exchanged with torch.distributed.
   * "collective": nyion_attn_decode_q4_partial, one all-gather (NCCL on GPUs,
     gloo in the CPU tests), nyion_attn_lse_combine — the library-collective
     baseline, and the host logic the CPU tests exercise.
@@ -68,9 +67,12 @@ class SplitKVDecoder:
     mode: str = "p2p"
     timeout_ms: int = 2000
 
-    # kernels one p2p step launches on each rank: the decode, whose last CTAs
-    # merge the partials and run the exchange
-    LAUNCHES_PER_STEP = 1
+    @property
+    def launches_per_step(self) -> int:
+        """Kernels one p2p step launches on each rank: the decode (whose merging
+        CTAs send the rank's rows to every rank) and, with more than one rank,
+        the exchange kernel that waits for the ranks' rows and combines them."""
+        return 1 if self.world == 1 else 2
 
     def __post_init__(self):
         self.lo, self.hi = rank_range(self.rank, self.world, self.total_tokens)
