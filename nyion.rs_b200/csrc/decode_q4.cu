@@ -149,7 +149,16 @@ constexpr int GROUPS = NYION_Q4_GROUPS; // consumer groups: stage s is consumed 
 constexpr int STAGES = GROUPS == 2 ? 8 : 6;   // 20 KB each
 constexpr int NCW = GROUPS * NKV * 2;   // consumer warps: group x KV head x 32-token half
 constexpr int NCT = NCW * 32;           // consumer threads
-constexpr int THREADS = NCT + 32;       // + the producer warp
+#ifndef NYION_Q4_PRODUCERS
+#define NYION_Q4_PRODUCERS 1
+#endif
+// producer warps: producer w copies the chunks k = w (mod NPROD), each its own
+// chain of stages and page-id ring.  Independent copy pipelines stream more
+// bytes per SM with no math (4 pipelines: 4.6 TB/s against 3.9 for one), but
+// this kernel is bound by its consumers and the extra warps cost it issue slots
+// (config 5: 118 us with 4 producers, 116 with 2, 115 with 1)
+constexpr int NPROD = NYION_Q4_PRODUCERS;
+constexpr int THREADS = NCT + 32 * NPROD;
 constexpr int MAX_SEQS = 512;
 constexpr int MAX_GRID = 1024;
 constexpr int RING = 32;                // chunks whose page ids the producer stages ahead
@@ -160,6 +169,7 @@ constexpr int CP = HD + 4;              // floats per row of a CTA partial: o[64
 constexpr int WK_BYTES = GROUP * CP * 4;   // per-warp region: factor table, then the segment partial
 static_assert(16 * PAIR_STRIDE <= WK_BYTES, "the factor table fits the per-warp region");
 static_assert(STAGES % GROUPS == 0, "a stage must always be consumed by the same warps");
+static_assert(STAGES % NPROD == 0, "a stage must always be filled by the same producer");
 static_assert(MT == ROWS * 16 && NCT >= MT, "merge mapping: 16 threads per query head, 4 dims each");
 
 enum : int32_t { kModePart = 0, kModeFinal = 1, kModeExchange = 2, kModeRing = 3 };
@@ -237,7 +247,7 @@ struct Smem {
   int32_t prefix[MAX_SEQS + 1];      // flat chunk index where sequence b starts
   int32_t c0[MAX_SEQS];              // first chunk (absolute, in 64-token units) of sequence b
   int32_t beg[MAX_SEQS], end[MAX_SEQS];
-  int32_t rows[2][RING][5];          // per chunk: 4 page ids (or -1 / -2) and the sequence index
+  int32_t rows[NPROD][2][RING][5];   // per producer and chunk: 4 page ids (or -1 / -2), the sequence
   int32_t warp_tot[THREADS / 32];
   int32_t flag;
   int32_t abort_;
@@ -273,7 +283,7 @@ __device__ __forceinline__ void rows_start(RowJob& j, const Smem& s, const Param
   }
 }
 
-__device__ __forceinline__ void rows_finish(Smem& s, const Params& p, const RowJob& j, int slot,
+__device__ __forceinline__ void rows_finish(int32_t (*rows)[RING][5], const Params& p, const RowJob& j, int slot,
                                             int lane) {
   if (!j.valid) return;
 #pragma unroll
@@ -283,9 +293,9 @@ __device__ __forceinline__ void rows_finish(Smem& s, const Params& p, const RowJ
       record_error(p.err, kErrPageRange);
       v = -2;    // not copied: the page's tokens are masked out by the consumers
     }
-    s.rows[slot][lane][pg] = v;
+    rows[slot][lane][pg] = v;
   }
-  s.rows[slot][lane][4] = j.b;
+  rows[slot][lane][4] = j.b;
 }
 
 __device__ __forceinline__ float2 hdr2f(uint32_t w) {   // (d, dmin) of a block header word
@@ -694,36 +704,41 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
   const int begin = blockIdx.x * W;
   const int end = min(total, begin + W);
 
-  if (warp == NCW) {
-    // ================= producer warp: whole pages by bulk copy =================
-    if (begin >= end) return;
-    const int n = end - begin;
+  if (warp >= NCW) {
+    // ========== producer warps: whole pages by bulk copy; producer pw copies
+    // ========== the chunks k = pw + NPROD it into stages k % STAGES ==========
+    const int pw = warp - NCW;
+    if (begin + pw >= end) return;
+    const int nit = (end - begin - pw + NPROD - 1) / NPROD;   // this producer's chunks
+    int32_t (*rows)[RING][5] = s.rows[pw];
+    auto chunk_of = [&](int it) { return begin + pw + NPROD * it; };
     RowJob job;
-    rows_start(job, s, p, begin + lane, end);
-    rows_finish(s, p, job, 0, lane);
-    rows_start(job, s, p, begin + RING + lane, end);
+    rows_start(job, s, p, chunk_of(lane), end);
+    rows_finish(rows, p, job, 0, lane);
+    rows_start(job, s, p, chunk_of(RING + lane), end);
     __syncwarp();
-    int stage = 0;
-    for (int k = 0; k < n; ++k) {
-      if ((k & (RING - 1)) == RING / 2) {
-        rows_finish(s, p, job, ((k / RING) + 1) & 1, lane);
+    for (int it = 0; it < nit; ++it) {
+      if ((it & (RING - 1)) == RING / 2) {
+        rows_finish(rows, p, job, ((it / RING) + 1) & 1, lane);
         __syncwarp();
-      } else if ((k & (RING - 1)) == 0 && k > 0) {
-        rows_start(job, s, p, begin + k + RING + lane, end);
+      } else if ((it & (RING - 1)) == 0 && it > 0) {
+        rows_start(job, s, p, chunk_of(it + RING + lane), end);
       }
+      const int k = pw + NPROD * it, stage = k % STAGES;
       bool ok = true;
       if (k >= STAGES) ok = mbar_wait_bounded(&s.empty[stage], (uint32_t)((k / STAGES - 1) & 1));
       if (!__all_sync(0xffffffffu, ok)) {
         record_error(p.err, kErrWaitTimeout);
         if (lane == 0) {
           atomicExch(&s.abort_, 1);
-          for (int c = k - 1; c >= 0 && c >= k - STAGES; --c)
+          // no copy of this producer may still be in flight when the CTA exits
+          for (int c = k - NPROD; c >= 0 && c >= k - STAGES; c -= NPROD)
             mbar_wait_bounded(&s.full[c % STAGES], (uint32_t)((c / STAGES) & 1));
         }
         return;
       }
       if (lane == 0) {
-        const int32_t* e = s.rows[(k / RING) & 1][k & (RING - 1)];
+        const int32_t* e = rows[(it / RING) & 1][it & (RING - 1)];
         uint32_t bytes = 0;
         int mask = 0;
 #pragma unroll
@@ -742,7 +757,6 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
                       PAGE_BYTES, &s.full[stage]);
       }
       __syncwarp();
-      stage = stage + 1 == STAGES ? 0 : stage + 1;
     }
     return;
   }
