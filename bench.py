@@ -4,14 +4,15 @@ Headline workload = BASELINE config 5 at every GPU count: one sequence of
 1,048,576 tokens of 4-bit KV (the reference quantizer's 20-byte blocks from
 N(0,1) sources, shuffled 16-token pages), TinyLlama heads (32 q / 4 kv / 64).
 The sequence axis is split evenly over the N ranks (one GPU each); every rank
-decodes its token range into log-sum-exp partials and the ranks' partials are
-merged by an exchange over peer memory fused into the reduce kernel (strong
-scaling: the total work is fixed).  One step = one decode of the whole
+decodes its token range into log-sum-exp partials merged inside the decode
+launch; the decode's merging CTAs write the rank's rows into every rank's
+mailbox over peer memory, and an exchange kernel chained after it combines
+the ranks' rows (strong scaling: the total work is fixed).  One step = one decode of the whole
 context.  The metric is decode-attention KV GB/s: algorithmic bytes (40 B per
 (token, KV head, K|V): 335,544,320 B per step) over the device time of the
-step, max over ranks; a 256 MB L2 flush and a one-word alignment exchange
-precede every timed step on every rank (a rank's shard fits in L2 from four
-ranks on).
+step, max over ranks; a 256 MB L2 flush precedes every timed step on every
+rank, and with more than one rank a one-chunk split-KV step over peer memory
+lines the ranks up after it (a rank's shard fits in L2 from four ranks on).
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
 
@@ -299,9 +300,9 @@ def timed_graph(torch, fn, stream, steps, warmup, barrier, dist=None, world=1, d
                 flush=None, align=None, clocks=None, per_rank=None):
     """CUDA-event time of fn() per call (graph replay when capture works), max over ranks.
     With `flush` (a buffer larger than L2), every timed step is preceded by a
-    write of the whole buffer and then by `align` (a one-word all-reduce, so
-    that the ranks leave their flushes together), both outside the step's own
-    event pair.  `clocks`: a ClockSampler context entered around the timed loop."""
+    write of the whole buffer and then by `align` (a step that ends on every
+    rank at about the same time, so that the ranks leave their flushes
+    together), both outside the step's own event pair.  `clocks`: a ClockSampler context entered around the timed loop."""
     g = None
     torch.cuda.synchronize()   # inputs built on other streams are complete
     with torch.cuda.stream(stream):
@@ -397,9 +398,10 @@ def build_q4_shard(A, torch, dev, tok_lo, tok_hi, perm_seed, total=T5, seed_base
 # ===================================================================== headline
 def run_config5(A, S, torch, dev, stream, args, barrier, dist, world, rank, with_cpu):
     """Config 5: B=1, 1M-token Q4 context split evenly over the ranks (strong
-    scaling).  Timed path: the fused exchange (the reduce kernel writes each
-    rank's partials into every rank's mailbox over peer memory and combines
-    after a bounded flag wait); the NCCL all-gather + LSE combine variant is
+    scaling).  Timed path: the exchange over peer memory (the decode's merging
+    CTAs write the rank's rows into every rank's mailbox; the exchange kernel
+    chained after it waits, bounded, for every rank's rows and combines them);
+    the NCCL all-gather + LSE combine variant is
     timed beside it as the library-collective baseline.  Parity on rank 0:
     against a one-GPU whole-context decode and against the CPU oracle."""
     decs = {m: S.SplitKVDecoder(rank, world, T5, mode=m) for m in ("p2p", "collective")}
@@ -407,16 +409,36 @@ def run_config5(A, S, torch, dev, stream, args, barrier, dist, world, rank, with
     pool, table = build_q4_shard(A, torch, dev, dec.lo, dec.hi, perm_seed=77 + rank)
     q = torch.randn(1, H, D, device=dev, generator=torch.Generator(device=dev).manual_seed(555))
     flush = l2_flush_buffer(torch, dev)
-    tiny = torch.zeros(1, device=dev)
-    align = (lambda: dist.all_reduce(tiny)) if world > 1 else None
+    align, align_ar, al_dec = None, None, None
+    if world > 1:
+        # Ranks leave their flushes together through a one-chunk split-KV step
+        # of their own (decode + exchange over peer memory): it ends on every
+        # rank once every rank's row has arrived, within about one NVLink
+        # latency of each other.  A one-word NCCL all-reduce leaves the ranks
+        # several microseconds apart, and that skew would fall inside the
+        # timed step of the rank released first (timed beside it for reference).
+        al_dec = S.SplitKVDecoder(rank, world, 64 * world, mode="p2p")
+        al_pool = torch.zeros(4, N_KV, 2, PT, 40, dtype=torch.uint8, device=dev)
+        al_table = torch.zeros(1, 4 * world, dtype=torch.int32, device=dev)
+        align = lambda: al_dec.step(q, al_pool, al_table, stream=stream)
+        with torch.cuda.stream(stream):
+            align()     # mailboxes set up outside the timed loop
+        torch.cuda.synchronize()
+        tiny = torch.zeros(1, device=dev)
+        align_ar = lambda: dist.all_reduce(tiny)
     res = {}
     clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
-    ranks = {"p2p": [], "collective": [], "local": []}
+    ranks = {"p2p": [], "collective": [], "local": [], "p2p_allreduce_align": []}
     for m in ("p2p", "collective"):
         d = decs[m]
         fn = lambda d=d: d.step(q, pool, table, stream=stream)
         res[m] = timed_graph(torch, fn, stream, args.steps, args.warmup, barrier, dist, world, dev, flush=flush,
                              align=align, clocks=clocks if m == "p2p" else None, per_rank=ranks[m])
+    if world > 1:
+        fn = lambda: dec.step(q, pool, table, stream=stream)
+        res["p2p_allreduce_align"] = timed_graph(torch, fn, stream, args.steps, args.warmup, barrier, dist, world,
+                                                 dev, flush=flush, align=align_ar,
+                                                 per_rank=ranks["p2p_allreduce_align"])
     if world > 1:
         # the rank's own decode of its shard, merged locally, without the exchange
         part = torch.empty(1, H, D + 2, device=dev)
@@ -448,6 +470,8 @@ def run_config5(A, S, torch, dev, stream, args, barrier, dist, world, rank, with
     err = A.device_error(stream)
     for d in decs.values():
         d.close()
+    if al_dec is not None:
+        al_dec.close()
     del pool
 
     # ---- parity on rank 0: one-GPU whole-context decode and the CPU oracle ----
@@ -474,6 +498,7 @@ def run_config5(A, S, torch, dev, stream, args, barrier, dist, world, rank, with
         "collective_ms": res["collective"][0], "p2p_vs_collective_max_abs": diff, "device_error": err,
         "parity": parity, "h2d": int(qh.numel() * 4), "d2h": int(oh.numel() * 4),
         "per_rank_ms": ranks, "local_ms": res["local"][0] if "local" in res else None,
+        "allreduce_align_ms": res["p2p_allreduce_align"][0] if "p2p_allreduce_align" in res else None,
     }
 
 
@@ -943,16 +968,22 @@ def run_gpu(args, rank, world):
         extra["reference_cuda_compiled"] = run_reference_cuda(A, torch, dev, stream, args)
         extra["position_lists"] = run_position_lists(A, torch, dev, stream, args, with_cpu)
     if rank == 0:
+        # DRAM bytes of one launch from the committed one-GPU ncu capture; a
+        # rank's launch reads its shard, so the figure scales with the shard
+        traffic = profiled_traffic("decode_q4_config3_config5.md")
+        if traffic is not None:
+            traffic = int(traffic * c5["shard_bytes"] / total)
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": c5["ms"], "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32 over 4-bit KV", "data": "synthetic N(0,1), seeded",
             "config": config5(world),
             "us_per_step": us,
-            "roofline": roofline_hbm(c5["shard_bytes"], us, profiled_traffic("decode_q4_config3_config5.md")) | {
+            "roofline": roofline_hbm(c5["shard_bytes"], us, traffic) | {
                 "kernel": "decode_q4 step of one rank (its shard of the context)",
                 "note": "achieved = the rank's shard bytes over the step's device time (the step's launches "
-                        "included), max over ranks"},
+                        "included), max over ranks; traffic = ncu DRAM read + write of the one-GPU launch "
+                        "(profiles/decode_q4_config3_config5.md), scaled to the shard"},
             "cpu_baseline": cpu,
             "e2e": {"value": total / (c5["e2e_ms"] * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": c5["e2e_ms"],
                     "h2d_bytes_per_step": c5["h2d"] * world, "d2h_bytes_per_step": c5["d2h"] * world,
@@ -965,6 +996,7 @@ def run_gpu(args, rank, world):
                          "p2p_vs_collective_max_abs": c5["p2p_vs_collective_max_abs"],
                          "bytes_per_gpu": c5["shard_bytes"], "exchange_bytes_per_gpu": world * H * (D + 2) * 4,
                          "per_rank_ms": c5["per_rank_ms"],
+                         "ms_per_step_with_allreduce_alignment": c5["allreduce_align_ms"],
                          "rank_decode_alone_ms": c5["local_ms"], **c5["parity"]},
             "device_error": c5["device_error"],
         }
