@@ -341,7 +341,7 @@ __device__ __forceinline__ void merge_pair(float4& O, float& M, float& L, float4
     return;
   }
   const float Mn = fmaxf(M, Mo);
-  const float sa = exp2f(M - Mn), sb = exp2f(Mo - Mn);
+  const float sa = ex2_ftz(M - Mn), sb = ex2_ftz(Mo - Mn);
   L = L * sa + Lo * sb;
   O.x = O.x * sa + Oo.x * sb;
   O.y = O.y * sa + Oo.y * sb;
@@ -351,7 +351,10 @@ __device__ __forceinline__ void merge_pair(float4& O, float& M, float& L, float4
 }
 
 // Merge of n partials at slots first, first + stride, ... for this thread's
-// (query head r, dims d4 .. d4 + 3): o relative to M (log2), L.
+// (query head r, dims d4 .. d4 + 3): o relative to M (log2), L.  The loads of
+// a batch of U slots are all in flight at once; the batch's maximum is taken
+// first, so that its weights are independent exponentials (no chain through
+// the running maximum).
 __device__ __forceinline__ void merge_slots(const Params& p, int first, int stride, int n, int r, int d4,
                                             float4& O, float& M, float& L) {
   M = -INFINITY;
@@ -372,18 +375,28 @@ __device__ __forceinline__ void merge_slots(const Params& p, int first, int stri
         ov[u] = make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
+    float Mn = M;
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (ml[u].y > 0.f) Mn = fmaxf(Mn, ml[u].x);
+    if (Mn == -INFINITY) continue;   // nothing attended so far
+    const float sa = L > 0.f ? ex2_ftz(M - Mn) : 0.f;
+    L *= sa;
+    O.x *= sa;
+    O.y *= sa;
+    O.z *= sa;
+    O.w *= sa;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       if (!(ml[u].y > 0.f)) continue;
-      const float Mn = fmaxf(M, ml[u].x);
-      const float sa = exp2f(M - Mn), sb = exp2f(ml[u].x - Mn);
-      L = L * sa + ml[u].y * sb;
-      O.x = O.x * sa + ov[u].x * sb;
-      O.y = O.y * sa + ov[u].y * sb;
-      O.z = O.z * sa + ov[u].z * sb;
-      O.w = O.w * sa + ov[u].w * sb;
-      M = Mn;
+      const float w = ex2_ftz(ml[u].x - Mn);
+      L = fmaf(w, ml[u].y, L);
+      O.x = fmaf(w, ov[u].x, O.x);
+      O.y = fmaf(w, ov[u].y, O.y);
+      O.z = fmaf(w, ov[u].z, O.z);
+      O.w = fmaf(w, ov[u].w, O.w);
     }
+    M = Mn;
   }
 }
 
@@ -507,7 +520,7 @@ __device__ __forceinline__ void segment_end(const Params& p, Smem& s, int b, int
 #pragma unroll
     for (int j = 0; j < NW; ++j) {
       if (!(ls[j] > 0.f)) continue;
-      const float w = exp2f(ms[j] - M);
+      const float w = ex2_ftz(ms[j] - M);
       L = fmaf(w, ls[j], L);
       O.x = fmaf(w, os[j].x, O.x);
       O.y = fmaf(w, os[j].y, O.y);
@@ -576,33 +589,47 @@ __device__ __forceinline__ void segment_end(const Params& p, Smem& s, int b, int
           }
         }
         consumer_sync();
-        // the 16 warps' partials of the row folded by the first 16 threads: the
-        // common maximum first, then the weighted sums (independent exponentials)
-        if (t < 16) {
+        // the 16 warps' partials of the row folded by warp 0: lane (h, c) = (lane / 16,
+        // lane % 16) takes dims 4c .. 4c + 3 of warps 8h .. 8h + 7, all loads at once;
+        // the common maximum first, then the weighted sums (independent
+        // exponentials), the two halves summed by a shuffle
+        if (warp == 0) {
+          const int c = lane & 15, h = lane >> 4;
+          float2 mo[8];
+          float4 oo[8];
+#pragma unroll
+          for (int w = 0; w < 8; ++w) {
+            mo[w] = rml[(8 * h + w) * 16 + c];
+            oo[w] = ro[(8 * h + w) * 16 + c];
+          }
           float Mx = -INFINITY;
 #pragma unroll
-          for (int w = 0; w < 16; ++w) {
-            const float2 mo = rml[w * 16 + t];
-            if (mo.y > 0.f) Mx = fmaxf(Mx, mo.x);
-          }
+          for (int w = 0; w < 8; ++w)
+            if (mo[w].y > 0.f) Mx = fmaxf(Mx, mo[w].x);
+          Mx = fmaxf(Mx, __shfl_xor_sync(0xffffffffu, Mx, 16));
           float Lx = 0.f;
           float4 Ox = make_float4(0.f, 0.f, 0.f, 0.f);
           if (Mx > -INFINITY) {
 #pragma unroll
-            for (int w = 0; w < 16; ++w) {
-              const float2 mo = rml[w * 16 + t];
-              if (!(mo.y > 0.f)) continue;
-              const float4 oo = ro[w * 16 + t];
-              const float sc = exp2f(mo.x - Mx);
-              Lx = fmaf(sc, mo.y, Lx);
-              Ox.x = fmaf(sc, oo.x, Ox.x);
-              Ox.y = fmaf(sc, oo.y, Ox.y);
-              Ox.z = fmaf(sc, oo.z, Ox.z);
-              Ox.w = fmaf(sc, oo.w, Ox.w);
+            for (int w = 0; w < 8; ++w) {
+              if (!(mo[w].y > 0.f)) continue;
+              const float sc = ex2_ftz(mo[w].x - Mx);
+              Lx = fmaf(sc, mo[w].y, Lx);
+              Ox.x = fmaf(sc, oo[w].x, Ox.x);
+              Ox.y = fmaf(sc, oo[w].y, Ox.y);
+              Ox.z = fmaf(sc, oo[w].z, Ox.z);
+              Ox.w = fmaf(sc, oo[w].w, Ox.w);
             }
           }
-          fo[rs * 16 + t] = Ox;
-          fml[rs * 16 + t] = make_float2(Mx, Lx);
+          Lx += __shfl_xor_sync(0xffffffffu, Lx, 16);
+          Ox.x += __shfl_xor_sync(0xffffffffu, Ox.x, 16);
+          Ox.y += __shfl_xor_sync(0xffffffffu, Ox.y, 16);
+          Ox.z += __shfl_xor_sync(0xffffffffu, Ox.z, 16);
+          Ox.w += __shfl_xor_sync(0xffffffffu, Ox.w, 16);
+          if (h == 0) {
+            fo[rs * 16 + c] = Ox;
+            fml[rs * 16 + c] = make_float2(Mx, Lx);
+          }
         }
         consumer_sync();
       }
@@ -649,6 +676,20 @@ __global__ void __launch_bounds__(THREADS, 1) decode_q4_kernel(const __grid_cons
   // one token range for every sequence (no per-sequence arrays): the chunk
   // offsets follow without a scan
   const bool uniform = !p.seq_lens && !p.tok_begin && !p.tok_end;
+  if (uniform && warp == NCW) {
+    // the page-table entries of this CTA's first chunks head for L2 while the
+    // prologue runs (lane l: chunk begin + l; the same split as below)
+    const int lo = max(p.u_begin, 0), hi = max(p.u_end, lo);
+    const int c = hi > lo ? (hi + CHUNK - 1) / CHUNK - lo / CHUNK : 0;
+    const int tot = p.batch * c;
+    const int w = (tot + (int)gridDim.x - 1) / (int)gridDim.x;
+    const int i = (int)blockIdx.x * w + lane;
+    if (c > 0 && lane < w && i < tot) {
+      const int pidx = (lo / CHUNK + i % c) * 4;
+      if (pidx < p.max_pages)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(p.table + (int64_t)(i / c) * p.max_pages + pidx));
+    }
+  }
   for (int b = t; b < p.batch; b += THREADS) {
     int lo, hi;
     if (p.seq_lens) {
@@ -1206,16 +1247,25 @@ __global__ void __launch_bounds__(256) q4_reduce_ring_kernel(const float* __rest
         ov[u] = make_float2(0.f, 0.f);
       }
     }
+    // the batch's maximum first: its weights are independent exponentials
+    float Mn = M;
+#pragma unroll
+    for (int u = 0; u < RU; ++u)
+      if (ml[u].y > 0.f) Mn = fmaxf(Mn, ml[u].x);
+    if (Mn == -INFINITY) continue;
+    const float sa = L > 0.f ? ex2_ftz(M - Mn) : 0.f;
+    L *= sa;
+    o0 *= sa;
+    o1 *= sa;
 #pragma unroll
     for (int u = 0; u < RU; ++u) {
       if (!(ml[u].y > 0.f)) continue;
-      const float Mn = fmaxf(M, ml[u].x);
-      const float sa = exp2f(M - Mn), sb = exp2f(ml[u].x - Mn);
-      L = L * sa + ml[u].y * sb;
-      o0 = o0 * sa + ov[u].x * sb;
-      o1 = o1 * sa + ov[u].y * sb;
-      M = Mn;
+      const float w = ex2_ftz(ml[u].x - Mn);
+      L = fmaf(w, ml[u].y, L);
+      o0 = fmaf(w, ov[u].x, o0);
+      o1 = fmaf(w, ov[u].y, o1);
     }
+    M = Mn;
   }
   const float inv = L > 0.f ? 1.0f / L : 0.f;
   float* dst = final_out + ((int64_t)b * NKV * GROUP + kvh * GROUP + hh) * HD;

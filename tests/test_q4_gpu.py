@@ -127,7 +127,9 @@ def _window_ring_case(B, L, window, ring_tokens, seed, dev):
 
 
 @pytest.mark.parametrize("L,window,ring_tokens", [([1000, 300], 512, 128), ([130, 64, 1000], 4096, 128),
-                                                  ([777], 100, 128), ([500, 60], 256, 64)])
+                                                  ([777], 100, 128), ([500, 60], 256, 64),
+                                                  # 160 (sequence, KV head) ring units: some CTAs take two
+                                                  ([3000 + 97 * i for i in range(40)], 1024, 100)])
 def test_window_ring_vs_oracle(cuda_device, L, window, ring_tokens):
     B = len(L)
     q, pool, table, ring = _window_ring_case(B, L, window, ring_tokens, seed=sum(L), dev=cuda_device)
