@@ -612,8 +612,8 @@ def ipc_close(ptr: int) -> None:
 
 def decode_q4_splitkv(q, kv_pool, page_table, u_begin: int, u_end: int, mailboxes, rank: int, out=None,
                       scale: float = 0.0, timeout_ms: int = 0, workspace=None, stream=None):
-    """Rank `rank`'s share of a split-KV decode with the exchange fused in:
-    returns the combined attention out [B, H, D] (same on every rank)."""
+    """Rank `rank`'s share of a split-KV decode, the ranks' rows exchanged over
+    peer memory: returns the combined attention out [B, H, D] (same on every rank)."""
     torch = _torch()
     B, H, D = q.shape
     if out is None:

@@ -1633,7 +1633,7 @@ extern "C" int32_t nyion_attn_decode_q4_window_ring(
 }
 
 
-// ---- split-KV decode with the exchange fused into the decode launch --------
+// ---- split-KV decode: rows sent by the decode, combined by the exchange kernel ----
 
 extern "C" size_t nyion_attn_splitkv_mailbox_bytes(int32_t batch, int32_t n_heads) {
   if (batch <= 0 || n_heads <= 0) return 0;

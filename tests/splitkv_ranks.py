@@ -1,7 +1,8 @@
 """Rank program for the multi-GPU split-KV test (launched by torchrun from
 tests/test_splitkv_multi_gpu.py).  Every rank uploads only its own pages, runs
-SplitKVDecoder.step in both exchange modes — "p2p" (partials written into the
-peers' mailboxes by the reduce kernel, combined after a bounded flag wait)
+SplitKVDecoder.step in both exchange modes — "p2p" (rows written into every
+rank's mailbox by the decode's merging CTAs, combined by the exchange kernel
+after a bounded wait)
 and "collective" (NCCL all-gather + LSE combine) — for several steps, inside
 and outside a CUDA graph, and checks the merged output against the one-GPU
 decode over the whole context and the oracle."""
